@@ -1,0 +1,513 @@
+#!/usr/bin/env python
+"""Benchmark: verify-block throughput of the Qwen3-8B-shaped 4-bit target, M = 16 rows at 2k
+context, on B200.
+
+A step is one speculative verify round of one request: verify forward of 16 rows (the anchor
+token + 15 drafts) through all 36 layers and the lm_head, argmax, greedy accept, and the KV
+rollback — one CUDA graph of the library's fused kernels. Random-init weights never accept a
+random draft, so the rollback follows seeded accept lengths n ~ U{0..15} (the cache grows by
+n + 1 per step and is reset to 2048 tokens every 16 steps: mean context ~2.1k).
+
+value      verify-block tokens/s = 16 * steps * n_gpus / max-over-ranks device time, inputs
+           resident in HBM (weights 4.26 GB per step, far larger than the 126 MB L2: no flush
+           needed).
+e2e        same step through the public API (VerifyGraph) with the step's token ids copied
+           from pinned host memory and the accept result (argmax row, n, next token) read back
+           to pinned host memory every step.
+roofline   the dominant kernel (gate/up QMM, ~48% of the bytes of a step), timed live with
+           CUDA events over back-to-back launches on all 36 layers' weights: achieved =
+           algorithmic bytes per launch / mean launch time vs the measured HBM copy bandwidth.
+cpu_baseline  the CPU oracle (C + OpenMP restatement of the same forward) on this host's cores.
+
+Multi-GPU (torchrun, one process per GPU): each rank runs independent requests on its own
+replica of the weights (data-parallel requests, no collective in the timed work): weak
+scaling. ``--impl reference`` times the reference arm: the CPU restatement of the path (the
+reference itself is MLX/Metal-only and cannot run here) on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CTX = 2048
+ROWS = 16
+METRIC = "verify-block tok/s at Qwen3-8B 4-bit M=16 (2k context)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quick", action="store_true", help="skip e2e/roofline extras")
+    return ap.parse_args()
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+
+    Q = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id: str):
+        self.bus = bus_id.lower().split(":", 1)[-1]
+        self.f = tempfile.NamedTemporaryFile("w+", delete=False, suffix=".csv")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait(timeout=10)
+        self.f.flush()
+        rows = []
+        for line in Path(self.f.name).read_text().splitlines():
+            cols = [c.strip() for c in line.split(",")]
+            if len(cols) < 9 or cols[0].lower().split(":", 1)[-1] != self.bus:
+                continue
+            rows.append(cols)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = sorted(float(r[1]) for r in rows)
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][2]),
+                "reasons": sorted(reasons), "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())
+                if any(r[3].replace(".", "").isdigit() for r in rows) else None}
+
+
+# ----------------------------------------------------------------------------- helpers
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def cpu_forward_sample(t, ids, n_layers_sample: int, reps_budget_s: float = 20.0) -> dict:
+    """Time the CPU oracle's forward on this host: embed + n_layers_sample layers + lm_head,
+    extrapolated to the model's depth (the per-layer work is identical across layers)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+
+    import oracle  # checker / CPU baseline only
+
+    oracle.build()
+    cores = oracle.threads()
+    cfg = t.cfg
+    W = t.oracle_weights(layers=n_layers_sample)
+    ocfg = t.oracle_config()
+    mk = lambda: [np.zeros((cfg.n_kv_heads, CTX + ROWS, cfg.head_dim), np.float32)  # noqa: E731
+                  for _ in range(n_layers_sample)]
+    kc, vc = mk(), mk()
+    rng = np.random.default_rng(0)
+    for a in kc + vc:
+        a[:, :CTX] = oracle.round_bf16(rng.standard_normal(a[:, :CTX].shape, dtype=np.float32))
+    ids_np = ids.cpu().numpy()
+    head = dict(W, layers=[])
+    t0 = time.perf_counter()
+    oracle.verify_forward(head, ocfg, ids_np, [], [], CTX)
+    t_head = time.perf_counter() - t0
+    times = []
+    start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        oracle.verify_forward(W, ocfg, ids_np, kc, vc, CTX)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - start > reps_budget_s * 0.5 or len(times) >= 3:
+            break
+    t_sample = min(times)
+    per_layer = max(t_sample - t_head, 1e-9) / n_layers_sample
+    est = t_head + per_layer * cfg.n_layers
+    return {"value": ROWS / est, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": (f"CPU oracle (C/OpenMP) verify forward of {ROWS} rows at {CTX} context: "
+                       f"embed + {n_layers_sample} of {cfg.n_layers} layers + lm_head timed "
+                       f"({t_sample:.2f} s, head {t_head:.2f} s), extrapolated linearly to "
+                       f"{cfg.n_layers} layers ({est:.2f} s per block)"),
+            "seconds_per_block": est}
+
+
+# ----------------------------------------------------------------------------- our arm
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    import mlx_dspark_b200  # noqa: F401
+    from mlx_dspark_b200 import _lib
+    from mlx_dspark_b200.target import QWEN3_8B, Target, VerifyGraph
+
+    _lib.ensure_init(local)
+    cfg = QWEN3_8B
+    t = Target(cfg, kv_cap=4096, seed=1 + rank, max_rows=32)
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    for L in t.layers:
+        L["k_cache"][0, :, :CTX] = torch.randn(L["k_cache"][0, :, :CTX].shape, device=dev,
+                                               generator=g).to(torch.bfloat16)
+        L["v_cache"][0, :, :CTX] = torch.randn(L["v_cache"][0, :, :CTX].shape, device=dev,
+                                               generator=g).to(torch.bfloat16)
+    vg = VerifyGraph(t, ROWS, L_max=CTX + ROWS * 17, forced_rejects=True)
+    vg.lens.fill_(CTX)
+    vg.capture()
+    total = args.warmup + args.steps
+    rng = np.random.default_rng(1234 + rank)
+    acc = rng.integers(0, ROWS, total)                   # accepted drafts n ~ U{0..15}
+    ids_all = torch.randint(0, cfg.vocab, (total, ROWS), device=dev, dtype=torch.int32,
+                            generator=g)
+    nrej_all = torch.from_numpy((ROWS - 1 - acc).astype(np.int32)).to(dev)
+
+    def step(i):
+        if i % 16 == 0:
+            vg.lens.fill_(CTX)
+        vg.ids.copy_(ids_all[i])
+        vg.n_rej.copy_(nrej_all[i : i + 1])
+        vg.replay()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    pr = torch.cuda.get_device_properties(dev)
+    bus = (f"{getattr(pr, 'pci_domain_id', 0):08x}:{getattr(pr, 'pci_bus_id', 0):02x}:"
+           f"{getattr(pr, 'pci_device_id', 0):02x}.0")
+    barrier(world)
+    clk = Clocks(bus)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.warmup, total):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms = e0.elapsed_time(e1)
+    ms = max_over_ranks(ms, world, dev)
+    barrier(world)
+    st = _lib.device_status(local)
+    secs = ms / 1e3
+    value = world * args.steps * ROWS / secs
+    committed = world * float((acc[args.warmup:] + 1).sum()) / secs
+    weight_bytes = cfg.weight_bytes()
+    kv_bytes = 2 * cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * 2 * (CTX + 60)
+    step_bytes = weight_bytes + kv_bytes
+
+    out = {"metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (random-init N(0,0.02) weights quantized MLX-affine 4-bit g64; "
+                   "random tokens; random bf16 KV prefix)",
+           "config": {"workload": "qwen3-8b-shape 4-bit verify, 16-row blocks at 2k context "
+                                  "(BASELINE configs[2])",
+                      "model": "Qwen3-8B-shaped (36 layers, hidden 4096, inter 12288, GQA 32/8, "
+                               "head_dim 128, vocab 151936), random init",
+                      "global_batch": world, "rows_per_block": ROWS, "seq_len": CTX,
+                      "parallelism": f"dp{world} (independent requests per GPU)",
+                      "l2": "inputs larger than L2 (4.26 GB of weights per step)",
+                      "accept": "seeded accept lengths U{0..15}; cache reset to 2048 every 16 steps"},
+           "blocks_per_s": round(world * args.steps / secs, 2),
+           "committed_tok_s": round(committed, 1),
+           "hbm_bytes_per_step": step_bytes,
+           "step_hbm_gbs": round(step_bytes * args.steps / secs / 1e9, 1),
+           "gpu_launches": vg.launches_per_step * args.steps,
+           "launches_per_step": vg.launches_per_step,
+           "clocks": clocks, "device_status": st}
+    pk = peaks()
+    out["step_roofline_frac"] = round(out["step_hbm_gbs"] / pk["hbm_gbs"], 3)
+
+    if not args.quick:
+        out["e2e"] = e2e(vg, ids_all, nrej_all, args, world, dev)
+        out["roofline"] = roofline(t, dev, pk)
+        out["qmm_microbench"] = qmm_microbench(dev, pk)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            out["cpu_baseline"] = {k: v for k, v in cpu_forward_sample(
+                t, ids_all[0], n_layers_sample=2).items() if k != "seconds_per_block"}
+            out["cpu_baseline"]["value"] = round(out["cpu_baseline"]["value"], 3)
+        except Exception as e:  # noqa: BLE001 — the baseline must not sink the bench line
+            out["cpu_baseline"] = {"value": None, "error": f"{type(e).__name__}: {e}"}
+    vg.graph = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def e2e(vg, ids_all, nrej_all, args, world, dev) -> dict:
+    """Verify rounds through the public API with host buffers: per step, H2D of the block's
+    ids from pinned memory, the graph, and D2H of (argmax row, n, next token) + sync."""
+    import torch
+
+    R = vg.R
+    host_ids = torch.empty((args.steps, R), dtype=torch.int32).pin_memory()
+    host_ids.copy_(ids_all[args.warmup :].cpu())
+    host_out = torch.empty((R + 2,), dtype=torch.int32).pin_memory()
+    s = torch.cuda.current_stream(dev)
+
+    def one(i, ids_row):
+        if i % 16 == 0:
+            vg.lens.fill_(CTX)
+        vg.ids.copy_(ids_row, non_blocking=True)
+        vg.n_rej.copy_(nrej_all[(args.warmup + i) % nrej_all.numel()].view(1))
+        vg.replay()
+        host_out[:R].copy_(vg.out["tt"], non_blocking=True)
+        host_out[R : R + 1].copy_(vg.out["n"], non_blocking=True)
+        host_out[R + 1 : R + 2].copy_(vg.out["next"], non_blocking=True)
+        s.synchronize()
+
+    for i in range(min(3, args.steps)):
+        one(i, host_ids[i])
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(args.steps):
+        one(i, host_ids[i])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    return {"value": round(world * args.steps * R / (ms / 1e3), 1), "unit": "tok/s",
+            "h2d_bytes_per_step": R * 4, "d2h_bytes_per_step": (R + 2) * 4,
+            "ms_per_step": round(ms / args.steps, 4)}
+
+
+def _qmm_bytes(n, k, m, bits):
+    return n * k * bits // 8 + n * (k // 64) * 4 + m * k * 2 + m * n * 2
+
+
+def roofline(t, dev, pk) -> dict:
+    """Dominant kernel: the gate/up QMM (N = 24576, K = 4096, 16 rows). Back-to-back launches
+    over all 36 layers' weights (2 GB, no L2 reuse), CUDA events on the launching stream."""
+    import torch
+
+    from mlx_dspark_b200 import skinny_qmm
+
+    cfg = t.cfg
+    x = torch.randn((ROWS, cfg.hidden), device=dev).to(torch.bfloat16)
+    out = torch.empty((ROWS, 2 * cfg.intermediate), dtype=torch.bfloat16, device=dev)
+    ws = [L["gate_up"] for L in t.layers]
+
+    def burst():
+        for w in ws:
+            skinny_qmm.qmm(x, w.wq, w.scales, w.biases, w.bits, out=out)
+
+    burst()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            burst()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    reps = 10
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    per = e0.elapsed_time(e1) / (reps * len(ws)) / 1e3
+    nbytes = _qmm_bytes(2 * cfg.intermediate, cfg.hidden, ROWS, cfg.bits)
+    ach = nbytes / per / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "qmm_gate_up_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+    return {"kernel": "dspark qmm_kernel (gate/up 24576x4096, 4-bit, 16 rows)", "bound": "hbm",
+            "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(ach / pk["hbm_gbs"], 3), "traffic": traffic,
+            "algorithmic_bytes_per_launch": nbytes, "us_per_launch": round(per * 1e6, 2),
+            "peak_source": pk["src"]}
+
+
+def qmm_microbench(dev, pk) -> dict:
+    """K = N = 4096, 4-bit, M in {1, 4, 8, 16}; 48 distinct weight copies
+    (~450 MB, > 3x L2) rotated back to back inside a CUDA graph."""
+    import torch
+
+    from mlx_dspark_b200 import quant, skinny_qmm
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    ws = [quant.random_qweight(4096, 4096, 4, device=dev, generator=g) for _ in range(48)]
+    res = {}
+    for M in (1, 4, 8, 16):
+        x = torch.randn((M, 4096), device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty((M, 4096), dtype=torch.bfloat16, device=dev)
+
+        def burst():
+            for w in ws:
+                skinny_qmm.qmm(x, w.wq, w.scales, w.biases, 4, out=out)
+
+        burst()
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=side):
+                burst()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        per = e0.elapsed_time(e1) / (10 * len(ws)) / 1e3
+        gbs = _qmm_bytes(4096, 4096, M, 4) / per / 1e9
+        res[f"M{M}"] = {"us": round(per * 1e6, 3), "gbs": round(gbs, 1),
+                        "frac": round(gbs / pk["hbm_gbs"], 3)}
+    return res
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+
+    import oracle  # the reference arm: CPU restatement of the path (see module docstring)
+
+    oracle.build()
+    cores = oracle.threads()
+    # the same workload on the host: random-init Qwen3-8B-shaped 4-bit weights, sampled
+    # layers (identical per-layer work), 16 rows at 2k context
+    H, I, Hq, Hk, D, V = 4096, 12288, 32, 8, 128, 151936
+    rng = np.random.default_rng(0)
+    sample_layers = 2
+
+    def qw(n, k):
+        w = rng.standard_normal((n, k), dtype=np.float32) * 0.02
+        wq, sc, bi = oracle.quantize(w, 4)
+        return {"wq": wq, "scales": sc, "biases": bi, "bits": 4}
+
+    def nw(n):
+        return oracle.round_bf16(1 + 0.05 * rng.standard_normal(n).astype(np.float32))
+
+    layers = [{"q": qw(Hq * D, H), "k": qw(Hk * D, H), "v": qw(Hk * D, H), "o": qw(H, Hq * D),
+               "gate": qw(I, H), "up": qw(I, H), "down": qw(H, I), "in_norm": nw(H),
+               "post_norm": nw(H), "q_norm": nw(D), "k_norm": nw(D)}
+              for _ in range(sample_layers)]
+    emb_rows = 4096  # the embedding is a 16-row gather; a slice of the table serves it
+    W = {"embed": qw(emb_rows, H), "lm_head": qw(V, H), "final_norm": nw(H), "layers": layers}
+    ocfg = {"hidden": H, "n_heads": Hq, "n_kv_heads": Hk, "head_dim": D, "rms_eps": 1e-6,
+            "rope_theta": 1e6}
+    kc = [oracle.round_bf16(rng.standard_normal((Hk, CTX + ROWS, D), dtype=np.float32))
+          for _ in range(sample_layers)]
+    vc = [oracle.round_bf16(rng.standard_normal((Hk, CTX + ROWS, D), dtype=np.float32))
+          for _ in range(sample_layers)]
+    ids = rng.integers(0, emb_rows, ROWS)
+    head = dict(W, layers=[])
+    t0 = time.perf_counter()
+    oracle.verify_forward(head, ocfg, ids, [], [], CTX)
+    t_head = time.perf_counter() - t0
+    est = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        oracle.verify_forward(W, ocfg, ids, kc, vc, CTX)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            est.append(t_head + (dt - t_head) / sample_layers * 36)
+    secs = float(np.mean(est))
+    value = ROWS / secs
+    sample = (f"CPU restatement (C/OpenMP oracle) of the verify forward, {ROWS} rows at {CTX} "
+              f"context: embed + {sample_layers} of 36 layers + lm_head per step, extrapolated "
+              f"linearly to 36 layers ({secs:.2f} s per block)")
+    out = {"metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs * 1e3, 2),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (random-init weights, random tokens / KV)",
+           "config": {"workload": "qwen3-8b-shape 4-bit verify, 16-row blocks at 2k context "
+                                  "(BASELINE configs[2])"},
+           "impl": "reference",
+           "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": cores,
+                            "kind": "port", "sample": sample},
+           "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0},
+           "note": "mlx-dspark's own path is MLX/Metal (Apple GPU) and MLX is not installable "
+                   "here; the arm runs the CPU restatement of the same arithmetic"}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

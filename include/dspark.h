@@ -1,0 +1,263 @@
+/*
+ * dspark.h — C ABI of the B200 (sm_100a) speculative-decoding verify path.
+ *
+ * Every entry point takes plain device pointers (caller-owned, written in place), sizes and
+ * a cudaStream_t passed as void*, launches asynchronously on that stream and returns an int
+ * status: DSPARK_OK, or an error code with a message in dspark_last_error(). Nothing is
+ * allocated per call; scratch space, where a launch needs any, is passed in. There is no
+ * CPU fallback: an unsupported shape is an error.
+ *
+ * bf16 tensors are passed as void* (2-byte elements); the weight format is MLX's affine
+ * quantization with group size 64: packed uint32 [N, K*bits/32] LSB-first, bf16 scales and
+ * biases [N, K/64], w = scale*q + bias.
+ */
+#ifndef DSPARK_H_
+#define DSPARK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSPARK_OK 0
+#define DSPARK_ERR_ARG 1          /* invalid argument */
+#define DSPARK_ERR_UNSUPPORTED 2  /* shape / alignment / format the kernels do not serve */
+#define DSPARK_ERR_CUDA 3         /* CUDA runtime error (launch, attribute, ...) */
+#define DSPARK_ERR_TIMEOUT 4      /* a bounded wait ran out (device status word set) */
+#define DSPARK_ERR_NOT_INIT 5     /* dspark_init() was not called for this device */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int dspark_version(void);
+
+/* Message for the last error returned on this host thread ("" when none). */
+const char* dspark_last_error(void);
+
+/* One-time per-device set-up (allocates the device status word). Call before any launch on
+ * `device` and before capturing launches into a CUDA graph. */
+int dspark_init(int device);
+
+/* Read (and optionally clear) the device status word: 0, or the code of the first bounded
+ * wait that ran out on that device. Synchronizes the device. */
+int dspark_device_status(int device, int* code, int clear);
+
+/* Number of streaming multiprocessors of `device` (launch planning). */
+int dspark_sm_count(int device);
+
+/* Kernel launches this library has issued since it was loaded (all devices; launches
+ * captured into a CUDA graph count once, at capture). */
+long long dspark_launch_count(void);
+
+/* ------------------------------------------------------------------------------------ K1 */
+
+/* out[M,N] = x[M,K] . dequant(W)^T, fp32 accumulation, bf16 result, 1 <= M <= 32.
+ * Replaces skinny_qmm.qmm(x2, weight, scales, biases, bits)
+ * (src/mlx_dspark/skinny_qmm.py:239) and mx.quantized_matmul(x, w, scales, biases,
+ * transpose=True, group_size=64, bits) at the call site skinny_qmm.call
+ * (src/mlx_dspark/skinny_qmm.py:249) reached from small_m_qmm._mma_call
+ * (src/mlx_dspark/small_m_qmm.py:71). Requires K % 64 == 0, N % 8 == 0, group == 64,
+ * bits in {4, 8}, x 16-byte aligned, contiguous rows. */
+int dspark_qmm(const void* x, int M, int K, const uint32_t* wq, const void* scales,
+               const void* biases, int N, int bits, int group, void* out, void* stream);
+
+/* dspark_qmm with row strides (elements) and an optional bf16 bias [N] added after the
+ * product in bf16 (QuantizedLinear's bias, src/mlx_dspark/skinny_qmm.py:263-264). */
+int dspark_qmm_ex(const void* x, int64_t ldx, int M, int K, const uint32_t* wq,
+                  const void* scales, const void* biases, const void* bias, int N, int bits,
+                  int group, void* out, int64_t ldo, void* stream);
+
+/* Launch geometry the QMM would use for [N, K] at `bits` (depends on the weight shape only,
+ * so a row's result never depends on M): tile width, split-K cluster size, k per split,
+ * pipeline depth. Mirrors skinny_qmm.plan/geometry (src/mlx_dspark/skinny_qmm.py:214-236). */
+int dspark_qmm_plan(int N, int K, int bits, int* tile_n, int* split_k, int* k_slice,
+                    int* stages);
+
+/* ------------------------------------------------------------------------------------ K2 */
+
+/* Multi-row GQA verify attention, out = softmax(scale * q.k^T + mask) . v.
+ * Replaces multirow_attn.multirow_sdpa(q, k, v, scale=, causal=, tree_anc=)
+ * (src/mlx_dspark/multirow_attn.py:223), i.e. mx.fast.scaled_dot_product_attention with
+ * mask=None/"causal" for few-row blocks (patched at src/mlx_dspark/multirow_attn.py:338).
+ * Shapes: q [B, Hq, qL, D], k/v [B, Hk, L, D] (any strides with D contiguous, cache views
+ * allowed), out [B, Hq, qL, D]; strides are element strides {batch, head, row}. Causal rule:
+ * row i sees keys <= L - qL + i. tree_anc (uint32 [B*qL], optional) switches to the
+ * tree-verify rule: every key < L - qL, and key L - qL + j iff bit j of anc[i]
+ * (src/mlx_dspark/multirow_attn.py:184-195). kv_len (device int32 [B], optional) gives a
+ * per-row key count <= L. D in {64, 128}. workspace may be NULL when
+ * dspark_verify_attn_workspace() returns 0 for the shape. */
+int dspark_verify_attn(const void* q, const int64_t q_strides[3], const void* k,
+                       const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
+                       int B, int Hq, int Hk, int qL, int D, int L, const int32_t* kv_len,
+                       float scale, int causal, const uint32_t* tree_anc, void* out,
+                       const int64_t o_strides[3], void* workspace, size_t ws_bytes,
+                       void* stream);
+
+/* Launch geometry of dspark_verify_attn for a shape (mirrors multirow_attn.plan,
+ * src/mlx_dspark/multirow_attn.py:204-220): out[0] 16-row tiles per CTA, out[1] warps
+ * splitting each K/V tile, out[2] row groups, out[3] key splits merged in a cluster, out[4]
+ * cluster groups merged through the workspace, out[5] keys per split. */
+int dspark_verify_attn_plan(int B, int Hq, int Hk, int qL, int D, int L, int out[6]);
+
+/* Bytes of workspace dspark_verify_attn needs for this shape (0 for most shapes). */
+size_t dspark_verify_attn_workspace(int B, int Hq, int Hk, int qL, int D, int L);
+
+/* Ragged form used by the batch engine: request b owns q/out rows starting at row_start[b]
+ * (element offset row_start[b]*q_si / *o_si) with q_len[b] rows, and kv_len[b] keys at
+ * element offset kv_off[b] of the K/V pools. Max sizes qL_max / L_max bound the launch. */
+int dspark_verify_attn_ragged(const void* q, int64_t q_sh, int64_t q_si, const void* k,
+                              int64_t k_sh, int64_t k_ss, const void* v, int64_t v_sh,
+                              int64_t v_ss, const int32_t* row_start, const int32_t* q_len,
+                              const int64_t* kv_off, const int32_t* kv_len, int B, int Hq,
+                              int Hk, int qL_max, int D, int L_max, float scale, void* out,
+                              int64_t o_sh, int64_t o_si, void* workspace, size_t ws_bytes,
+                              void* stream);
+
+/* ------------------------------------------------------------------------------------ K3 */
+
+/* Append T new rows per batch row at that row's current length and advance it:
+ * cache[b, h, lens[b] + t, :] = new[b, h, t, :]; lens[b] += T. Rows that would pass `cap`
+ * are not written (the device status word records it). Replaces the per-row write loop of
+ * BatchCache.update_and_fetch (src/mlx_dspark/batch_engine.py:193-208). Strides in
+ * elements {batch, head, row}; D contiguous; elem_size bytes per element (rows of
+ * D*elem_size bytes, a multiple of 16, 16-byte aligned). */
+int dspark_kv_append(const void* k_new, const int64_t kn_strides[3], const void* v_new,
+                     const int64_t vn_strides[3], void* k_cache, const int64_t kc_strides[3],
+                     void* v_cache, const int64_t vc_strides[3], int32_t* lens, int B, int H,
+                     int T, int D, int elem_size, int cap, void* stream);
+
+/* In-place rollback: lens[b] = max(0, lens[b] - n_rejected[b]) on the device. Metadata only;
+ * the next append overwrites the tail. Replaces KVCache.trim / Target.rollback
+ * (src/mlx_dspark/target.py:679-698) and BatchCache.trim (src/mlx_dspark/batch_engine.py:220-224). */
+int dspark_kv_rollback(int32_t* lens, const int32_t* n_rejected, int B, void* stream);
+
+/* Copy row src's live K/V columns onto row dst and vacate src (lens[dst] = lens[src],
+ * lens[src] = 0). Replaces BatchCache.move_row (src/mlx_dspark/batch_engine.py:177-185). */
+int dspark_kv_move_row(void* k_cache, const int64_t kc_strides[3], void* v_cache,
+                       const int64_t vc_strides[3], int32_t* lens, int src, int dst, int H,
+                       int D, int elem_size, int max_len, void* stream);
+
+/* --------------------------------------------------------------------- accept / argmax */
+
+/* tt[r] = argmax(logits[r, :V]) for R rows (first index on ties), logits row stride ld. */
+int dspark_argmax(const void* logits, int64_t ld, int R, int V, int32_t* tt, void* stream);
+
+/* Greedy accept over ragged verify blocks, fused with the KV rollback.
+ * Request b's block is rows cu_rows[b] .. cu_rows[b+1]-1 of `ids` ([pending, drafts...]) and
+ * `tt` (argmax per row). n_accept[b] = length of the leading run of drafts equal to the
+ * target's argmax (cumprod(drafts == tt[:cap]).sum(), src/mlx_dspark/generate.py:1548-1550,
+ * batched src/mlx_dspark/batch_engine.py:684-686); next_tok[b] = tt[cu_rows[b] + n] (the
+ * bonus token); if lens != NULL, lens[b] -= cap - n (the rollback of the rejected tail,
+ * src/mlx_dspark/batch_engine.py:692-705). */
+int dspark_accept(const int32_t* tt, const int32_t* ids, const int32_t* cu_rows, int B,
+                  int32_t* n_accept, int32_t* next_tok, int32_t* lens, void* stream);
+
+/* ------------------------------------------------------------------------------------ K4 */
+
+/* Ragged request packing for one batched verify step, built on the device.
+ * Inputs per active request b < B: block_len[b] (cap_b + 1 rows), kv_len[b] (tokens cached
+ * before the step), slot_off[b] (element offset of the request's K/V slot in the pools),
+ * ids_pad [B, t_max] ([pending, drafts...], row stride t_max).
+ * Outputs: cu_rows [B+1] (prefix sum of block_len), row_pos [R] (absolute position of each
+ * packed row = kv_len[b] + i), row_kv [R] (= slot_off of the row's request), row_req [R],
+ * ids [R] (packed tokens), kv_len_new [B] (= kv_len + block_len: keys visible to the
+ * step's attention), with R = cu_rows[B] <= r_max. Rows r >= R up to r_max are filled
+ * with a harmless copy of row 0's metadata. Replaces the host loops of SpecSlots.step /
+ * build_batch_mask / BatchCache.update_and_fetch (src/mlx_dspark/batch_engine.py:635-708,
+ * :231-239, :193-208). */
+int dspark_pack_ragged(const int32_t* block_len, const int32_t* kv_len, const int64_t* slot_off,
+                       const int32_t* ids_pad, int t_max, int B, int r_max, int32_t* cu_rows,
+                       int32_t* row_pos, int64_t* row_kv, int32_t* row_req, int32_t* ids,
+                       int32_t* kv_len_new, void* stream);
+
+/* Boolean mask [B, 1, T, Lcur] (uint8) of build_batch_mask (src/mlx_dspark/batch_engine.py:
+ * 231-239): mask[b, 0, i, j] = j <= offsets[b] + i, Lcur = max(offsets) + T. For checking
+ * the packing against the reference's dense formulation; the kernels never build it. */
+int dspark_batch_mask(const int32_t* offsets, int B, int T, int Lcur, uint8_t* mask,
+                      void* stream);
+
+/* --------------------------------------------------------------------- forward glue */
+
+/* h[m] = dequant(embedding[ids[m]]) (MLX QuantizedEmbedding, 4/8-bit g64) in bf16;
+ * ssq[m] (optional) = sum(h[m]^2) in fp32 over the bf16 values. */
+int dspark_embed(const int32_t* ids, int M, const uint32_t* wq, const void* scales,
+                 const void* biases, int V, int H, int bits, void* h, float* ssq, void* stream);
+
+/* out = x * rsqrt(mean(x^2) + eps) * w  (mx.fast.rms_norm), fp32 math, bf16 out. */
+int dspark_rmsnorm(const void* x, int64_t ldx, int M, int H, const void* w, float eps,
+                   void* out, int64_t ldo, void* stream);
+
+/* Dense Qwen3-style target (random-init or loaded) described by device pointers. */
+typedef struct {
+  const uint32_t* wq;
+  const void* scales;
+  const void* biases;
+  int N, K, bits;
+} dspark_qweight;
+
+typedef struct {
+  dspark_qweight qkv;      /* rows [q heads | k heads | v heads], K = hidden */
+  dspark_qweight o;        /* N = hidden, K = Hq*D */
+  dspark_qweight gate_up;  /* rows interleaved in blocks of 32: gate 32, up 32, ... */
+  dspark_qweight down;     /* N = hidden, K = intermediate */
+  const void* in_norm;     /* [hidden] */
+  const void* post_norm;   /* [hidden] */
+  const void* q_norm;      /* [head_dim] */
+  const void* k_norm;      /* [head_dim] */
+  void* k_cache;           /* layer's K pool: element (h, pos, d) at h*k_sh + pos*k_ss + d */
+  void* v_cache;
+} dspark_layer;
+
+typedef struct {
+  int n_layers, hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab;
+  float rms_eps, rope_theta;
+  dspark_qweight embed;    /* [vocab, hidden] quantized embedding */
+  dspark_qweight lm_head;  /* [vocab, hidden] */
+  const void* final_norm;  /* [hidden] */
+  const dspark_layer* layers;  /* host array [n_layers] */
+  int64_t k_sh, k_ss, v_sh, v_ss;  /* cache strides (elements) */
+  int kv_cap;              /* positions per request slot */
+} dspark_model;
+
+/* Caller-owned device buffers for one verify forward of up to r_max rows. */
+typedef struct {
+  void* h;          /* bf16 [r_max, hidden] residual stream */
+  void* xq;         /* bf16 [r_max, n_heads*head_dim] roped queries */
+  void* attn;       /* bf16 [r_max, n_heads*head_dim] attention output */
+  void* act;        /* bf16 [r_max, intermediate] SwiGLU output */
+  float* ssq_a;     /* fp32 [1024 * 32] RMSNorm partial statistics */
+  float* ssq_b;     /* fp32 [1024 * 32] */
+  float* inv_freq;  /* fp32 [head_dim/2] RoPE frequencies (filled by the forward) */
+  int32_t* row_pos; /* int32 [r_max] absolute positions */
+  int64_t* row_kv;  /* int64 [r_max] element offset of each row's cache slot */
+  int32_t* kv_len;  /* int32 [B] keys visible per request (after the append) */
+  int32_t* row_start;  /* int32 [B] first packed row of each request */
+  int32_t* q_len;      /* int32 [B] rows per request */
+  int64_t* kv_off;     /* int64 [B] cache slot offset per request */
+  void* attn_ws;    /* attention workspace (may be NULL) */
+  size_t attn_ws_bytes;
+} dspark_fwd_buffers;
+
+/* One verify forward (Target.verify -> _body_mlxlm + head, src/mlx_dspark/target.py:642,
+ * :208-221; batched_forward src/mlx_dspark/batch_engine.py:245-276) over R packed rows of B
+ * requests: embed -> n_layers x [RMSNorm, fused QKV QMM + q/k-norm + RoPE + cache write,
+ * verify attention, O QMM + residual, RMSNorm, gate/up QMM + SwiGLU, down QMM + residual]
+ * -> RMSNorm -> lm_head QMM -> logits [R, vocab] (row stride ld_logits).
+ * The packing arrays in `buf` (row_pos, row_kv, kv_len, row_start, q_len, kv_off) must be
+ * filled for the step (dspark_pack_ragged, or dspark_verify_prepare for one request).
+ * L_max / qL_max bound the requests' key counts / block rows. R <= 32. */
+int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf,
+                          const int32_t* ids, int R, int B, int qL_max, int L_max,
+                          void* logits, int64_t ld_logits, void* stream);
+
+/* Single-request packing for dspark_verify_forward: with L0 = *len (device int32, tokens
+ * cached before the step): row_pos[m] = L0 + m, row_kv[m] = 0, kv_len[0] = L0 + R,
+ * row_start[0] = 0, q_len[0] = R, kv_off[0] = 0, and *len = L0 + R (the forward appends the
+ * block's K/V; dspark_accept then trims the rejected tail). */
+int dspark_verify_prepare(int32_t* len, int R, const dspark_fwd_buffers* buf, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSPARK_H_ */

@@ -1,0 +1,491 @@
+// K2: multi-row causal GQA verify attention  (sm_100a)
+//
+// Replaces multirow_sdpa / _P1 / _P2 (src/mlx_dspark/multirow_attn.py:223-259, :52-178),
+// the kernel behind mx.fast.scaled_dot_product_attention for few-row verify blocks.
+//
+// Semantics (multirow_attn.py:85-87, :120-124): all G*qL query rows of a KV head are packed
+// (GQA head major, then q position), so each K/V byte is read once per head for all rows.
+// Row qi of a block of qL rows over L keys sees keys <= L - qL + qi (causal) or all keys;
+// the tree-verify variant (multirow_attn.py:184-195) sees every prefix key and, among the
+// last qL keys, key L-qL+j iff bit j of anc[qi] is set. Softmax in fp32 (exp2 domain, scale
+// folded in); P is rounded to bf16 for the P.V product, as in the reference.
+//
+// B200 design: one CTA per (key split, batch row, KV head, row group). A producer warp
+// streams 64-key K/V tiles into a 3-slot shared-memory ring with bulk copies (one per
+// 16-byte-aligned cache row, so strided cache views need no copy) completing on mbarriers.
+// Consumer warps run Q.K^T and P.V on tensor cores (mma.m16n8k16, ldmatrix from padded
+// rows) with a flash-attention online softmax; warps that split a tile's keys merge in shared
+// memory, the key splits of a cluster merge through distributed shared memory, and (only
+// when more splits are needed than a cluster holds) cluster groups merge through a workspace.
+#include <algorithm>
+#include <cmath>
+
+#include "attn.h"
+#include "common.cuh"
+#include "host_common.h"
+
+namespace dspark {
+namespace attn {
+
+constexpr int KT = 64;     // keys per stage
+constexpr int NSLOT = 3;   // ring depth
+
+// Workspace row of one partial: D accumulators, then m and l, padded to 16 bytes so the
+// accumulators are written with aligned 16-byte stores.
+template <int D>
+constexpr int kWsRow = D + 4;
+
+template <int D>
+struct AttnSmem {
+  static constexpr int ROWB = D * 2 + 16;           // padded row (bank-conflict-free ldmatrix)
+  static constexpr int STG = 2 * KT * ROWB;          // K tile + V tile
+  static constexpr int RING = NSLOT * STG;
+};
+
+template <int D, int NRT, int KS>
+__host__ __device__ constexpr int attn_smem_bytes() {
+  // ring (reused after the key loop for the merge buffers) + merge stats + barriers
+  constexpr int RPG = NRT * 16;
+  constexpr int merge = KS * RPG * D * 4;
+  constexpr int ring = AttnSmem<D>::RING;
+  constexpr int body = ring > merge ? ring : merge;
+  return body + (2 * KS + 2) * RPG * 4 + 2 * NSLOT * 8 + 128;
+}
+
+__device__ __forceinline__ int64_t q_base(const AttnParams& p, int b, const int64_t sb,
+                                          const int64_t si) {
+  return p.row_start ? int64_t(p.row_start[b]) * si : int64_t(b) * sb;
+}
+
+template <int D, int NRT, int KS>
+__global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnParams p) {
+  constexpr int NC = NRT * KS;
+  constexpr int RPG = NRT * 16;
+  constexpr int ROWB = AttnSmem<D>::ROWB;
+  constexpr int STG = AttnSmem<D>::STG;
+  constexpr int KPW = KT / KS;         // keys per warp per stage (64 or 32)
+  constexpr int KB = 32;               // keys per softmax step
+  constexpr int NDT = D / 8;           // n8 tiles of the output
+  constexpr int NKK = D / 16;          // k16 steps of Q.K^T
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* ring = smem;
+  constexpr int BODY = attn_smem_bytes<D, NRT, KS>() - (2 * KS + 2) * RPG * 4 - 2 * NSLOT * 8 - 128;
+  float* bufO = reinterpret_cast<float*>(smem);            // [KS][RPG][D] (aliases the ring)
+  float* bufM = reinterpret_cast<float*>(smem + BODY);     // [KS][RPG]
+  float* bufL = bufM + KS * RPG;                           // [KS][RPG]
+  float* finM = bufL + KS * RPG;                           // [RPG]
+  float* finL = finM + RPG;                                // [RPG]
+  uint64_t* full = reinterpret_cast<uint64_t*>(finL + RPG);
+  uint64_t* empty = full + NSLOT;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sidx_c = blockIdx.x;                 // split within the cluster
+  const int g_grp = blockIdx.z;                  // cluster group
+  const int bhr = blockIdx.y;                    // (b * Hk + hk) * nrg + rg
+  const int rg = bhr % p.nrg;
+  const int bh = bhr / p.nrg;
+  const int hk = bh % p.Hk;
+  const int b = bh / p.Hk;
+  const int G = p.Hq / p.Hk;
+
+  // zero the ring once: keys past a split's end read finite zeros, never stale garbage
+  for (int i = threadIdx.x; i < AttnSmem<D>::RING / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(ring)[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NC);
+    }
+    fence_mbar_init();
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  pdl_launch_dependents();
+  pdl_wait();  // q and the freshly appended cache rows come from the previous kernel
+
+  const int Lb = p.kv_len ? p.kv_len[b] : p.L;
+  const int qLb = p.q_len ? p.q_len[b] : p.qL;
+  const int split = g_grp * p.ns + sidx_c;
+  const int k0 = min(Lb, split * p.chunk);
+  const int kend = min(Lb, k0 + p.chunk);
+  const int nst = (kend - k0 + KT - 1) / KT;
+
+  const bf16* kb_ptr = p.k + (p.kv_off ? p.kv_off[b] : int64_t(b) * p.k_sb) + int64_t(hk) * p.k_sh;
+  const bf16* vb_ptr = p.v + (p.kv_off ? p.kv_off[b] : int64_t(b) * p.v_sb) + int64_t(hk) * p.v_sh;
+
+  if (warp == NC) {
+    // ------------------------------------------------------------------ producer warp
+    for (int st = 0; st < nst; ++st) {
+      const int slot = st % NSLOT;
+      if (st >= NSLOT) {
+        if (!mbar_wait(&empty[slot], ((st / NSLOT) - 1) & 1, p.status, kErrWaitKVEmpty)) break;
+      }
+      const int kt = k0 + st * KT;
+      const int nv = min(KT, kend - kt);
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], uint32_t(nv) * D * 2 * 2);
+      __syncwarp();
+      uint8_t* ks = ring + slot * STG;
+      uint8_t* vs = ks + KT * ROWB;
+      for (int r = lane; r < 2 * nv; r += 32) {
+        const int key = r >> 1;
+        if (r & 1)
+          bulk_load(vs + key * ROWB, vb_ptr + int64_t(kt + key) * p.v_ss, D * 2, &full[slot]);
+        else
+          bulk_load(ks + key * ROWB, kb_ptr + int64_t(kt + key) * p.k_ss, D * 2, &full[slot]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ consumer warps
+    const int rt = warp % NRT, kslot = warp / NRT;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int r0 = rt * 16 + gid, r1 = r0 + 8;             // rows within the group
+    const int pr0 = rg * RPG + r0, pr1 = rg * RPG + r1;    // packed rows
+    const int nrows = G * qLb;
+    const int qi0 = pr0 % qLb, qi1 = pr1 % qLb;
+    int kmax0 = Lb - 1, kmax1 = Lb - 1;
+    if (p.causal && p.tree_anc == nullptr) {
+      kmax0 = Lb - qLb + qi0;
+      kmax1 = Lb - qLb + qi1;
+    }
+    uint32_t anc0 = 0xffffffffu, anc1 = 0xffffffffu;
+    if (p.tree_anc != nullptr) {
+      anc0 = pr0 < nrows ? p.tree_anc[b * p.qL + qi0] : 0u;
+      anc1 = pr1 < nrows ? p.tree_anc[b * p.qL + qi1] : 0u;
+    }
+    const int tree_lo = Lb - qLb;  // first key governed by the ancestor bits
+
+    // Q fragments in registers
+    uint32_t qf[NKK][4];
+    {
+      const int64_t qb = q_base(p, b, p.q_sb, p.q_si);
+      const bf16* q0 = pr0 < nrows ? p.q + qb + int64_t(hk * G + pr0 / qLb) * p.q_sh + int64_t(qi0) * p.q_si : nullptr;
+      const bf16* q1 = pr1 < nrows ? p.q + qb + int64_t(hk * G + pr1 / qLb) * p.q_sh + int64_t(qi1) * p.q_si : nullptr;
+#pragma unroll
+      for (int kk = 0; kk < NKK; ++kk) {
+        const int d = kk * 16 + 2 * tig;
+        qf[kk][0] = q0 ? __ldcg(reinterpret_cast<const unsigned int*>(q0 + d)) : 0u;
+        qf[kk][1] = q1 ? __ldcg(reinterpret_cast<const unsigned int*>(q1 + d)) : 0u;
+        qf[kk][2] = q0 ? __ldcg(reinterpret_cast<const unsigned int*>(q0 + d + 8)) : 0u;
+        qf[kk][3] = q1 ? __ldcg(reinterpret_cast<const unsigned int*>(q1 + d + 8)) : 0u;
+      }
+    }
+    float o[NDT][4];
+#pragma unroll
+    for (int i = 0; i < NDT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;
+    const float sc = p.scale_log2;
+    const uint32_t ring_a = smem_u32(ring);
+
+    for (int st = 0; st < nst; ++st) {
+      const int slot = st % NSLOT;
+      mbar_wait(&full[slot], (st / NSLOT) & 1, p.status, kErrWaitKV);
+      const uint32_t ks_a = ring_a + slot * STG;
+      const uint32_t vs_a = ks_a + KT * ROWB;
+      const int kt = k0 + st * KT;
+#pragma unroll
+      for (int sub = 0; sub < KPW / KB; ++sub) {
+        const int kl = kslot * KPW + sub * KB;   // first key of this step within the tile
+        float s[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < NKK; ++kk) {
+#pragma unroll
+          for (int jp = 0; jp < 2; ++jp) {
+            const int mi = lane >> 3;
+            const int key = kl + jp * 16 + (mi >> 1) * 8 + (lane & 7);
+            const int d = kk * 16 + (mi & 1) * 8;
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4(ks_a + key * ROWB + d * 2, b0, b1, b2, b3);
+            mma_bf16_16816(s[2 * jp], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
+            mma_bf16_16816(s[2 * jp + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
+          }
+        }
+        // mask + online softmax (exp2 domain)
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = kt + kl + j * 8 + 2 * tig + (e & 1);
+            const bool row1 = e >= 2;
+            bool ok = key < kend && key <= (row1 ? kmax1 : kmax0);
+            if (p.tree_anc != nullptr && key >= tree_lo)
+              ok = ok && (((row1 ? anc1 : anc0) >> (key - tree_lo)) & 1u);
+            s[j][e] = ok ? s[j][e] * sc : -INFINITY;
+            if (row1) mx1 = fmaxf(mx1, s[j][e]); else mx0 = fmaxf(mx0, s[j][e]);
+          }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float f0 = exp2f(m0 - mn0), f1 = exp2f(m1 - mn1);
+        m0 = mn0;
+        m1 = mn1;
+        float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s[j][0] = exp2f(s[j][0] - mn0);
+          s[j][1] = exp2f(s[j][1] - mn0);
+          s[j][2] = exp2f(s[j][2] - mn1);
+          s[j][3] = exp2f(s[j][3] - mn1);
+          ps0 += s[j][0] + s[j][1];
+          ps1 += s[j][2] + s[j][3];
+        }
+        l0 = l0 * f0 + ps0;
+        l1 = l1 * f1 + ps1;
+#pragma unroll
+        for (int i = 0; i < NDT; ++i) {
+          o[i][0] *= f0; o[i][1] *= f0;
+          o[i][2] *= f1; o[i][3] *= f1;
+        }
+        // O += P . V over two k16 steps of keys
+#pragma unroll
+        for (int k2 = 0; k2 < 2; ++k2) {
+          const uint32_t a0 = pack_bf16x2(s[2 * k2][0], s[2 * k2][1]);
+          const uint32_t a1 = pack_bf16x2(s[2 * k2][2], s[2 * k2][3]);
+          const uint32_t a2 = pack_bf16x2(s[2 * k2 + 1][0], s[2 * k2 + 1][1]);
+          const uint32_t a3 = pack_bf16x2(s[2 * k2 + 1][2], s[2 * k2 + 1][3]);
+          const int mi = lane >> 3;
+          const int key = kl + k2 * 16 + (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+          for (int dt = 0; dt < NDT; dt += 2) {
+            const int d = (dt + (mi >> 1)) * 8;
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4_trans(vs_a + key * ROWB + d * 2, b0, b1, b2, b3);
+            mma_bf16_16816(o[dt], a0, a1, a2, a3, b0, b1);
+            mma_bf16_16816(o[dt + 1], a0, a1, a2, a3, b2, b3);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+    // every warp is past the ring once all consumers reach this barrier
+    asm volatile("bar.sync 1, %0;" ::"n"(NC * 32));
+    float* myO = bufO + kslot * RPG * D;
+#pragma unroll
+    for (int dt = 0; dt < NDT; ++dt) {
+      const int d = dt * 8 + 2 * tig;
+      *reinterpret_cast<float2*>(&myO[r0 * D + d]) = make_float2(o[dt][0], o[dt][1]);
+      *reinterpret_cast<float2*>(&myO[r1 * D + d]) = make_float2(o[dt][2], o[dt][3]);
+    }
+    if (tig == 0) {
+      bufM[kslot * RPG + r0] = m0;
+      bufM[kslot * RPG + r1] = m1;
+      bufL[kslot * RPG + r0] = l0;
+      bufL[kslot * RPG + r1] = l1;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(NC * 32));
+    // merge the KS key slots of each row into slot 0
+    for (int idx = threadIdx.x; idx < RPG * D; idx += NC * 32) {
+      const int r = idx / D;
+      float M = bufM[r];
+#pragma unroll
+      for (int k = 1; k < KS; ++k) M = fmaxf(M, bufM[k * RPG + r]);
+      float acc = 0.f, L = 0.f;
+#pragma unroll
+      for (int k = 0; k < KS; ++k) {
+        const float w = exp2f(bufM[k * RPG + r] - M);
+        acc += w * bufO[k * RPG * D + idx];
+        L += w * bufL[k * RPG + r];
+      }
+      bufO[idx] = acc;
+      if ((idx % D) == 0) {
+        finM[r] = M;
+        finL[r] = L;
+      }
+    }
+  }
+
+  // ------------------------------------------------------------------ split merge + store
+  if (p.ns > 1) cluster_sync_all(); else __syncthreads();
+  const int ns = p.ns;
+  const int64_t ob = q_base(p, b, p.o_sb, p.o_si);
+  const int nrows = G * qLb;
+  for (int idx = threadIdx.x; idx < RPG * (D / 4); idx += blockDim.x) {
+    const int r = idx / (D / 4), d4 = (idx % (D / 4)) * 4;
+    if ((r % ns) != sidx_c) continue;
+    const int prow = rg * RPG + r;
+    if (prow >= nrows) continue;
+    float M = -1e30f, Lsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (ns > 1) {
+      const uint32_t am = smem_u32(&finM[r]), al = smem_u32(&finL[r]);
+      const uint32_t ao = smem_u32(&bufO[r * D + d4]);
+      for (int c = 0; c < ns; ++c) M = fmaxf(M, ld_dsmem_f32(mapa_shared(am, c)));
+      for (int c = 0; c < ns; ++c) {
+        const float w = exp2f(ld_dsmem_f32(mapa_shared(am, c)) - M);
+        Lsum += w * ld_dsmem_f32(mapa_shared(al, c));
+        const float4 v = ld_dsmem_f4(mapa_shared(ao, c));
+        acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
+      }
+    } else {
+      M = finM[r];
+      Lsum = finL[r];
+      acc = *reinterpret_cast<const float4*>(&bufO[r * D + d4]);
+    }
+    if (p.ng > 1) {
+      // unnormalized partial for the cross-cluster merge
+      float* w = p.ws + ((int64_t(bhr) * p.ng + g_grp) * RPG + r) * kWsRow<D>;
+      *reinterpret_cast<float4*>(&w[d4]) = acc;
+      if (d4 == 0) {
+        w[D] = M;
+        w[D + 1] = Lsum;
+      }
+    } else {
+      const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+      const int h = hk * G + prow / qLb, i = prow % qLb;
+      bf16* dst = p.o + ob + int64_t(h) * p.o_sh + int64_t(i) * p.o_si + d4;
+      uint2 pk;
+      pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+      pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+      *reinterpret_cast<uint2*>(dst) = pk;
+    }
+  }
+  if (p.ns > 1) cluster_sync_all();
+}
+
+// Cross-cluster merge of the ng partials (only when ng > 1).
+template <int D>
+__global__ void attn_merge_kernel(const AttnParams p, int rpg) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int bhr = blockIdx.x;
+  const int rg = bhr % p.nrg, bh = bhr / p.nrg;
+  const int hk = bh % p.Hk, b = bh / p.Hk;
+  const int G = p.Hq / p.Hk;
+  const int qLb = p.q_len ? p.q_len[b] : p.qL;
+  const int nrows = G * qLb;
+  const int64_t ob = q_base(p, b, p.o_sb, p.o_si);
+  for (int idx = threadIdx.x; idx < rpg * D; idx += blockDim.x) {
+    const int r = idx / D, d = idx % D;
+    const int prow = rg * rpg + r;
+    if (prow >= nrows) continue;
+    const float* base = p.ws + (int64_t(bhr) * p.ng * rpg + r) * kWsRow<D>;
+    const int64_t gstride = int64_t(rpg) * kWsRow<D>;
+    float M = -1e30f;
+    for (int g = 0; g < p.ng; ++g) M = fmaxf(M, base[g * gstride + D]);
+    float acc = 0.f, L = 0.f;
+    for (int g = 0; g < p.ng; ++g) {
+      const float w = exp2f(base[g * gstride + D] - M);
+      acc += w * base[g * gstride + d];
+      L += w * base[g * gstride + D + 1];
+    }
+    const int h = hk * G + prow / qLb, i = prow % qLb;
+    p.o[ob + int64_t(h) * p.o_sh + int64_t(i) * p.o_si + d] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
+  }
+}
+
+// ------------------------------------------------------------------------------ host side
+
+AttnPlan plan(int B, int Hq, int Hk, int qL, int D, int L) {
+  AttnPlan pl;
+  const int rows = (Hq / Hk) * qL;
+  const int tiles = (rows + 15) / 16;
+  int nrt;
+  if (tiles <= 1) nrt = 1;
+  else if (tiles <= 2) nrt = 2;
+  else if (tiles <= 4) nrt = 4;
+  else nrt = 8;
+  pl.nrt = nrt;
+  pl.ks = nrt >= 8 ? 1 : 2;
+  pl.nrg = (tiles + nrt - 1) / nrt;
+  const int sms = sm_count(current_device());
+  const int heads = B * Hk * pl.nrg;
+  // total key splits: aim for ~one CTA per SM, each streaming >= 256 keys
+  int want = std::max(1, sms / std::max(1, heads));
+  want = std::min(want, std::max(1, L / 256));
+  const int force = env_int("DSPARK_ATTN_SPLITS", 0);
+  if (force > 0) want = force;
+  int ns = std::min(want, 16);
+  if (ns > 8 && ns < 16) ns = 8;
+  int ng = (want + ns - 1) / ns;
+  int chunk = ((L + ns * ng - 1) / (ns * ng) + KT - 1) / KT * KT;
+  chunk = std::max(chunk, KT);
+  // drop splits that would start past the end
+  while (ns * ng > 1 && (ns * ng - 1) * chunk >= L) {
+    if (ng > 1) --ng; else --ns;
+  }
+  pl.ns = std::max(1, ns);
+  pl.ng = std::max(1, ng);
+  pl.chunk = ((L + pl.ns * pl.ng - 1) / (pl.ns * pl.ng) + KT - 1) / KT * KT;
+  pl.chunk = std::max(pl.chunk, KT);
+  return pl;
+}
+
+size_t workspace_bytes(const AttnPlan& pl, int B, int Hk, int D) {
+  if (pl.ng <= 1) return 0;
+  return size_t(B) * Hk * pl.nrg * pl.ng * (pl.nrt * 16) * (D + 4) * sizeof(float);
+}
+
+template <int D, int NRT, int KS>
+static int launch_attn(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) {
+  auto kern = attn_kernel<D, NRT, KS>;
+  constexpr int smem = attn_smem_bytes<D, NRT, KS>();
+  static bool configured = false;
+  if (!configured) {
+    DSPARK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                    "attn: set smem");
+    DSPARK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                    "attn: allow cluster 16");
+    configured = true;
+  }
+  dim3 grid(pl.ns, p.B * p.Hk * pl.nrg, pl.ng);
+  dim3 block((NRT * KS + 1) * 32);
+  DSPARK_CUDA_TRY(launch_ex(kern, grid, block, smem, s, pl.ns, true, p), "attn: launch");
+  if (pl.ng > 1) {
+    DSPARK_CUDA_TRY(launch_ex(attn_merge_kernel<D>, dim3(p.B * p.Hk * pl.nrg), dim3(256), 0, s, 1,
+                              true, p, NRT * 16),
+                    "attn: merge launch");
+  }
+  return DSPARK_OK;
+}
+
+template <int D>
+static int dispatch_d(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) {
+  if (pl.nrt == 1 && pl.ks == 2) return launch_attn<D, 1, 2>(p, pl, s);
+  if (pl.nrt == 2 && pl.ks == 2) return launch_attn<D, 2, 2>(p, pl, s);
+  if (pl.nrt == 4 && pl.ks == 2) return launch_attn<D, 4, 2>(p, pl, s);
+  if (pl.nrt == 8 && pl.ks == 1) return launch_attn<D, 8, 1>(p, pl, s);
+  return fail(DSPARK_ERR_UNSUPPORTED, "attn: no kernel for %d row tiles x %d key slots", pl.nrt, pl.ks);
+}
+
+int run(AttnParams p, const AttnPlan* plan_in, cudaStream_t stream) {
+  if (p.B <= 0 || p.Hq <= 0 || p.Hk <= 0 || p.Hq % p.Hk || p.qL <= 0 || p.L <= 0)
+    return fail(DSPARK_ERR_ARG, "attn: bad shape B=%d Hq=%d Hk=%d qL=%d L=%d", p.B, p.Hq, p.Hk, p.qL, p.L);
+  if (p.D != 64 && p.D != 128)
+    return fail(DSPARK_ERR_UNSUPPORTED, "attn: head_dim %d not supported (64, 128)", p.D);
+  if (p.qL > 32 && p.tree_anc)
+    return fail(DSPARK_ERR_UNSUPPORTED, "attn: tree verify supports at most 32 rows");
+  const uintptr_t al = reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v);
+  if ((al & 15) || ((p.k_sb | p.k_sh | p.k_ss | p.v_sb | p.v_sh | p.v_ss) & 7))
+    return fail(DSPARK_ERR_UNSUPPORTED, "attn: K/V rows must be 16-byte aligned (strides %% 8 == 0)");
+  if ((reinterpret_cast<uintptr_t>(p.q) & 3) || (reinterpret_cast<uintptr_t>(p.o) & 7) ||
+      ((p.q_sb | p.q_sh | p.q_si) & 1) || ((p.o_sb | p.o_sh | p.o_si) & 3))
+    return fail(DSPARK_ERR_UNSUPPORTED, "attn: q rows need 4-byte and output rows 8-byte alignment");
+  if (!p.kv_len && p.causal && !p.tree_anc && p.qL > p.L)
+    return fail(DSPARK_ERR_ARG, "attn: causal verify needs qL <= L (qL=%d L=%d)", p.qL, p.L);
+  AttnPlan pl = plan_in ? *plan_in : plan(p.B, p.Hq, p.Hk, p.qL, p.D, p.L);
+  p.nrg = pl.nrg;
+  p.ns = pl.ns;
+  p.ng = pl.ng;
+  p.chunk = pl.chunk;
+  if (pl.ng > 1 && p.ws == nullptr)
+    return fail(DSPARK_ERR_ARG, "attn: this launch needs a workspace of %zu bytes",
+                workspace_bytes(pl, p.B, p.Hk, p.D));
+  if (p.status == nullptr) p.status = status_word(current_device());
+  return p.D == 64 ? dispatch_d<64>(p, pl, stream) : dispatch_d<128>(p, pl, stream);
+}
+
+}  // namespace attn
+}  // namespace dspark

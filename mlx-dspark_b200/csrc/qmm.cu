@@ -1,0 +1,759 @@
+// K1: small-M affine-quantized matmul  y[M,N] = x[M,K] . dequant(W)^T   (sm_100a)
+//
+// Replaces skinny_qmm.qmm (src/mlx_dspark/skinny_qmm.py:239-246, kernel :61-160) and the
+// stock mx.quantized_matmul(transpose=True) it stands in for at 1-32 rows.
+//
+// Weight format (MLX affine, group 64): W packed as uint32 [N, K*bits/32], LSB-first; in
+// 4-bit word j of a row holds k = 8j..8j+7 (k = 8j+s at bits 4s..4s+3), in 8-bit word j holds
+// k = 4j..4j+3 (bits 8s..8s+7). scales/biases bf16 [N, K/64]; w = scale*q + bias.
+//
+// Design (B200-first, HBM-bound at these M):
+//  * The packed weights stream through a ring of shared-memory stages filled by TMA
+//    (cp.async.bulk.tensor, 128-byte swizzle, L2 evict-first) from one producer warp; the
+//    scales/biases of each stage ride on the same mbarrier. The weight TMA of a launch is
+//    issued before griddepcontrol.wait, so under programmatic dependent launch the weights
+//    of layer i+1 stream while layer i finishes.
+//  * Consumer warps dequantize in registers with the bf16 "magic exponent" trick: a nibble
+//    OR'd into the mantissa of 128.0 is exactly 128+q (one lop3 per two weights); 8-bit
+//    weights are split into low (128+lo) and high (2048+16*hi) nibble planes, two exact bf16
+//    MMAs. The weights are the A operand of mma.m16n8k16 (16 output columns), the x rows the
+//    B operand (8 rows per tile, M padded to 8/16/32), so a weight is read once per launch
+//    whatever M is.
+//  * Scale and bias factor out per group, as in the reference (skinny_qmm.py:131-145):
+//    acc += scale*P + (bias - MAGIC*scale) * sum_k x, with P the exact per-group MMA sum.
+//  * Split-K across the CTAs of a thread-block cluster; the fp32 partials are reduced in a
+//    fixed rank order through distributed shared memory, so results are deterministic and
+//    a row's output does not depend on M (the reference's row-count invariance,
+//    tests/test_small_m_qmm.py:107-119).
+//  * Epilogues: plain bf16 store (+ optional bias), residual add (+ per-row sum of squares
+//    for the next RMSNorm), SwiGLU on interleaved gate/up rows, and Qwen3 q/k RMSNorm + RoPE
+//    + KV-cache write. The prologue can apply RMSNorm to x while staging it.
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "host_common.h"
+#include "qmm.h"
+
+namespace dspark {
+namespace qmm {
+
+constexpr int KSTG = 512;        // k values per pipeline stage
+constexpr int GPS = KSTG / 64;   // quantization groups per stage
+constexpr int kSmemBudget = 220 * 1024;  // dynamic shared memory a plan may use at 32 rows
+
+template <int BITS>
+struct BitsTraits;
+template <>
+struct BitsTraits<4> {
+  static constexpr float MAGIC = 128.0f;
+  static constexpr int SB = 2;      // 128-byte TMA boxes per stage row (512 k * 4 bit)
+  static constexpr int XPAD = 16;   // staged-x row padding (bytes)
+};
+template <>
+struct BitsTraits<8> {
+  static constexpr float MAGIC = 2176.0f;
+  static constexpr int SB = 4;
+  static constexpr int XPAD = 8;
+};
+
+// Physical tile row used by MMA row `gid` (0..7). Chosen so the warp's shared-memory loads
+// of weight words are bank-conflict free under the 128-byte swizzle.
+template <int BITS>
+__device__ __forceinline__ int row_perm(int gid) {
+  return BITS == 4 ? (((gid & 3) << 1) | (gid >> 2)) : (((gid & 1) << 2) | (gid >> 1));
+}
+
+struct SmemLayout {
+  int ring, scs, bis, xs, sx, part, red, rs, bars, total;
+};
+
+template <int BITS, int NW, int RT>
+__host__ __device__ inline SmemLayout smem_layout(int kslice, int nslots) {
+  constexpr int TN = 16 * NW;
+  constexpr int RP = 8 * RT;
+  const int stg = BitsTraits<BITS>::SB * TN * 128;
+  const int scb = TN * 16;
+  SmemLayout L;
+  int off = 0;
+  L.ring = off;
+  off += nslots * stg;
+  L.scs = off;
+  off += nslots * scb;
+  L.bis = off;
+  off += nslots * scb;
+  L.xs = off;
+  off += RP * (kslice * 2 + BitsTraits<BITS>::XPAD);
+  off = (off + 15) & ~15;
+  L.sx = off;
+  off += RP * (kslice / 64) * 4;
+  off = (off + 15) & ~15;
+  L.part = off;
+  off += RP * (TN + 4) * 4;
+  L.red = off;
+  off += RP * (TN + 4) * 4;
+  L.rs = off;
+  off += 32 * 4;
+  off = (off + 15) & ~15;
+  L.bars = off;
+  off += 2 * nslots * 8;
+  L.total = off + 1024;  // slack for aligning the dynamic base to 1024 bytes
+  return L;
+}
+
+static int smem_bytes(int bits, int nw, int rt, int kslice, int nslots) {
+  const int tn = 16 * nw, rp = 8 * rt;
+  const int sb = bits == 4 ? BitsTraits<4>::SB : BitsTraits<8>::SB;
+  const int xpad = bits == 4 ? BitsTraits<4>::XPAD : BitsTraits<8>::XPAD;
+  int off = nslots * sb * tn * 128 + 2 * nslots * tn * 16;
+  off += rp * (kslice * 2 + xpad);
+  off = (off + 15) & ~15;
+  off += rp * (kslice / 64) * 4;
+  off = (off + 15) & ~15;
+  off += 2 * rp * (tn + 4) * 4 + 32 * 4;
+  off = (off + 15) & ~15;
+  return off + 2 * nslots * 8 + 1024;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
+
+// ----------------------------------------------------------------------------- kernel
+
+template <int BITS, int RT, int NW, int EPI, bool SCT>
+__global__ void __launch_bounds__((NW + 1) * 32)
+    qmm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
+               const __grid_constant__ CUtensorMap bmap, const QmmParams p) {
+  constexpr int TN = 16 * NW;
+  constexpr int RP = 8 * RT;
+  constexpr int NTHR = (NW + 1) * 32;
+  constexpr int SB = BitsTraits<BITS>::SB;
+  constexpr int BOX = TN * 128;
+  constexpr int STG = SB * BOX;
+  constexpr int SCB = TN * 16;
+  constexpr float MAGIC = BitsTraits<BITS>::MAGIC;
+  constexpr int PSTR = TN + 4;  // fp32 row stride of the partial / reduced tiles
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int S = p.nslots;
+  const SmemLayout Ls = smem_layout<BITS, NW, RT>(p.kslice, S);
+  uint8_t* ring = smem + Ls.ring;
+  uint8_t* scs = smem + Ls.scs;
+  uint8_t* bis = smem + Ls.bis;
+  uint8_t* xs = smem + Ls.xs;
+  float* sx = reinterpret_cast<float*>(smem + Ls.sx);
+  float* part = reinterpret_cast<float*>(smem + Ls.part);
+  float* red = reinterpret_cast<float*>(smem + Ls.red);
+  float* rsm = reinterpret_cast<float*>(smem + Ls.rs);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Ls.bars);
+  uint64_t* empty = full + S;
+
+  const int cs = p.cs;
+  const int rank = blockIdx.x;  // cluster rank == split-K slice (cluster dims are (cs,1,1))
+  const int ntile = blockIdx.y;
+  const int n0 = ntile * TN;
+  const int kbase = rank * p.kslice;
+  const int kvalid = min(p.kslice, p.K - kbase);
+  const int nst = (kvalid + KSTG - 1) / KSTG;
+  const int gslice = p.kslice / 64;
+  const int xrow = p.kslice * 2 + BitsTraits<BITS>::XPAD;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == NW) {
+    // ------------------------------------------------------------- producer warp
+    if (lane == 0) {
+      prefetch_tmap(&wmap);
+      if (SCT) {
+        prefetch_tmap(&smap);
+        prefetch_tmap(&bmap);
+      }
+      const uint64_t pol = l2_policy_evict_first();
+      const uint32_t bytes = STG + (SCT ? 2 * SCB : 0);
+      for (int st = 0; st < nst; ++st) {
+        const int slot = st % S;
+        if (st >= S) {
+          if (!mbar_wait(&empty[slot], ((st / S) - 1) & 1, p.status, kErrWaitEmpty)) break;
+        }
+        mbar_arrive_expect_tx(&full[slot], bytes);
+        const int kk = kbase + st * KSTG;
+        const int w0 = kk * BITS / 32;
+#pragma unroll
+        for (int b = 0; b < SB; ++b)
+          tma_load_2d(ring + slot * STG + b * BOX, &wmap, &full[slot], w0 + b * 32, n0, pol);
+        if (SCT) {
+          tma_load_2d(scs + slot * SCB, &smap, &full[slot], kk / 64, n0, pol);
+          tma_load_2d(bis + slot * SCB, &bmap, &full[slot], kk / 64, n0, pol);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------- consumer warps
+    pdl_wait();  // x / residual / norm statistics come from earlier kernels
+    constexpr int NC = NW * 32;
+    const int tid = threadIdx.x;
+
+    // RMSNorm statistics for the prologue: rs[m] = 1/sqrt(mean(x^2) + eps)
+    if (p.norm_w != nullptr) {
+      // one warp per row: lanes stride over the partial sums (fixed order per lane, then a
+      // fixed shuffle tree: deterministic)
+      for (int m = warp; m < RP; m += NW) {
+        float ss = 0.f;
+        if (m < p.M)
+          for (int e = lane; e < p.ssq_n; e += 32) ss += __ldcg(&p.ssq_in[e * p.ssq_stride + m]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) rsm[m] = m < p.M ? rsqrtf(ss / float(p.K) + p.eps) : 0.f;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(NC));
+    }
+
+    // Stage x[:, kbase : kbase + kslice] into shared memory in MMA-operand order. Each thread
+    // issues XB 16-byte loads before using any, so the staging costs ~one L2 round trip per
+    // batch instead of one per block. x is read through L2 only (ld.global.cg): it was
+    // written by the previous kernel.
+    const int blocks = p.kslice / 8;
+    const int total = RP * blocks;
+    constexpr int XB = 8;
+    const bool nrm = p.norm_w != nullptr;
+    for (int base = tid; base < total; base += NC * XB) {
+      uint4 v[XB], w[XB];
+#pragma unroll
+      for (int u = 0; u < XB; ++u) {
+        const int idx = base + u * NC;
+        const int m = idx / blocks, j = idx - m * blocks;
+        v[u] = make_uint4(0u, 0u, 0u, 0u);
+        w[u] = v[u];
+        if (idx < total && m < p.M && j * 8 < kvalid) {
+          const int k = kbase + j * 8;
+          v[u] = __ldcg(reinterpret_cast<const uint4*>(p.x + (size_t)m * p.ldx + k));
+          if (nrm) w[u] = __ldg(reinterpret_cast<const uint4*>(p.norm_w + k));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < XB; ++u) {
+        const int idx = base + u * NC;
+        if (idx >= total) break;
+        const int m = idx / blocks, j = idx - m * blocks;
+        uint4 vv = v[u];
+        if (nrm && m < p.M) {
+          const float r = rsm[m];
+          uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
+          const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w[u]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
+                                bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
+        }
+        uint8_t* dst = xs + m * xrow + j * 16;
+        if (BITS == 4) {  // 8-block order (0,4,1,5,2,6,3,7)
+          uint4 o;
+          o.x = __byte_perm(vv.x, vv.z, 0x5410);
+          o.y = __byte_perm(vv.x, vv.z, 0x7632);
+          o.z = __byte_perm(vv.y, vv.w, 0x5410);
+          o.w = __byte_perm(vv.y, vv.w, 0x7632);
+          *reinterpret_cast<uint4*>(dst) = o;
+        } else {          // two 4-blocks, each in order (0,2,1,3)
+          uint2 a, b;
+          a.x = __byte_perm(vv.x, vv.y, 0x5410);
+          a.y = __byte_perm(vv.x, vv.y, 0x7632);
+          b.x = __byte_perm(vv.z, vv.w, 0x5410);
+          b.y = __byte_perm(vv.z, vv.w, 0x7632);
+          reinterpret_cast<uint2*>(dst)[0] = a;
+          reinterpret_cast<uint2*>(dst)[1] = b;
+        }
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(NC));
+    // Per-group input sums (fixed order: deterministic, row-local), stored group-major.
+    for (int idx = tid; idx < RP * gslice; idx += NC) {
+      const int g = idx / RP, m = idx - g * RP;  // rows fastest: conflict-free 16-byte loads
+      const uint8_t* src = xs + m * xrow + g * 128;
+      float s = 0.f;
+      if (BITS == 4) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 q = *reinterpret_cast<const uint4*>(src + 16 * i);
+          s += (bf16_lo(q.x) + bf16_hi(q.x)) + (bf16_lo(q.y) + bf16_hi(q.y)) +
+               (bf16_lo(q.z) + bf16_hi(q.z)) + (bf16_lo(q.w) + bf16_hi(q.w));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint2 q = *reinterpret_cast<const uint2*>(src + 8 * i);
+          s += (bf16_lo(q.x) + bf16_hi(q.x)) + (bf16_lo(q.y) + bf16_hi(q.y));
+        }
+      }
+      sx[g * RP + m] = s;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(NC));
+
+    const int gid = lane >> 2, tig = lane & 3;
+    const int ra = warp * 16 + row_perm<BITS>(gid);
+    const int rb = ra + 8;
+    float acc[RT][4];
+#pragma unroll
+    for (int r = 0; r < RT; ++r)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[r][c] = 0.f;
+
+    const uint32_t ring_a = smem_u32(ring);
+    const uint32_t xs_a = smem_u32(xs);
+    const int gfirst = kbase / 64;
+
+    for (int st = 0; st < nst; ++st) {
+      const int slot = st % S;
+      mbar_wait(&full[slot], (st / S) & 1, p.status, kErrWaitFull);
+      const uint32_t wbase = ring_a + slot * STG;
+      uint4 sca, scb_, bia, bib;
+      if (SCT) {
+        sca = lds128(smem_u32(scs + slot * SCB + ra * 16));
+        scb_ = lds128(smem_u32(scs + slot * SCB + rb * 16));
+        bia = lds128(smem_u32(bis + slot * SCB + ra * 16));
+        bib = lds128(smem_u32(bis + slot * SCB + rb * 16));
+      }
+#pragma unroll
+      for (int gi = 0; gi < GPS; ++gi) {
+        const int gl = st * GPS + gi;  // group index within this slice
+        if (gfirst + gl >= p.G || gl * 64 >= kvalid) break;
+        float P[RT][4];
+#pragma unroll
+        for (int r = 0; r < RT; ++r)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) P[r][c] = 0.f;
+
+        if (BITS == 4) {
+          // words gi*8 + 2*tig + {0,1} of rows ra / rb
+          const int box = gi >> 2;
+          const int chunk = ((gi & 3) << 1) + (tig >> 1);
+          const int within = (tig & 1) * 8;
+          const uint2 wa = lds64(wbase + box * BOX + ra * 128 + ((chunk ^ (ra & 7)) << 4) + within);
+          const uint2 wb = lds64(wbase + box * BOX + rb * 128 + ((chunk ^ (rb & 7)) << 4) + within);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const uint32_t xa = h2 ? wa.y : wa.x;
+            const uint32_t xb = h2 ? wb.y : wb.x;
+            uint32_t A[4], Bq[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              A[i] = lop3_and_or(xa >> (4 * i), 0x000F000Fu, 0x43004300u);
+              Bq[i] = lop3_and_or(xb >> (4 * i), 0x000F000Fu, 0x43004300u);
+            }
+            const int blk = st * 64 + gi * 8 + 2 * tig + h2;  // 8-k block within the slice
+#pragma unroll
+            for (int r = 0; r < RT; ++r) {
+              const uint4 xv = lds128(xs_a + (r * 8 + gid) * xrow + blk * 16);
+              mma_bf16_16816(P[r], A[0], Bq[0], A[1], Bq[1], xv.x, xv.y);
+              mma_bf16_16816(P[r], A[2], Bq[2], A[3], Bq[3], xv.z, xv.w);
+            }
+          }
+        } else {
+          // words gi*16 + 4*tig + {0..3} of rows ra / rb
+          const int box = gi >> 1;
+          const int chunk = ((gi & 1) << 2) + tig;
+          const uint4 wa = lds128(wbase + box * BOX + ra * 128 + ((chunk ^ (ra & 7)) << 4));
+          const uint4 wb = lds128(wbase + box * BOX + rb * 128 + ((chunk ^ (rb & 7)) << 4));
+          const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
+          const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const uint32_t xa = wav[h], xb = wbv[h];
+            const uint32_t alo0 = lop3_and_or(xa, 0x000F000Fu, 0x43004300u);
+            const uint32_t alo1 = lop3_and_or(xa >> 8, 0x000F000Fu, 0x43004300u);
+            const uint32_t ahi0 = lop3_and_or(xa >> 4, 0x000F000Fu, 0x45004500u);
+            const uint32_t ahi1 = lop3_and_or(xa >> 12, 0x000F000Fu, 0x45004500u);
+            const uint32_t blo0 = lop3_and_or(xb, 0x000F000Fu, 0x43004300u);
+            const uint32_t blo1 = lop3_and_or(xb >> 8, 0x000F000Fu, 0x43004300u);
+            const uint32_t bhi0 = lop3_and_or(xb >> 4, 0x000F000Fu, 0x45004500u);
+            const uint32_t bhi1 = lop3_and_or(xb >> 12, 0x000F000Fu, 0x45004500u);
+            const int kq = st * KSTG + (gi * 16 + 4 * tig + h) * 4;  // k within slice
+#pragma unroll
+            for (int r = 0; r < RT; ++r) {
+              const uint2 xv = lds64(xs_a + (r * 8 + gid) * xrow + kq * 2);
+              mma_bf16_16816(P[r], alo0, blo0, alo1, blo1, xv.x, xv.y);
+              mma_bf16_16816(P[r], ahi0, bhi0, ahi1, bhi1, xv.x, xv.y);
+            }
+          }
+        }
+        // fold the group: acc += s*P + (b - MAGIC*s) * sum(x)
+        float sa, sbv, ba, bb;
+        if (SCT) {
+          const uint32_t* pa = reinterpret_cast<const uint32_t*>(&sca);
+          const uint32_t* pb = reinterpret_cast<const uint32_t*>(&scb_);
+          const uint32_t* qa = reinterpret_cast<const uint32_t*>(&bia);
+          const uint32_t* qb = reinterpret_cast<const uint32_t*>(&bib);
+          sa = (gi & 1) ? bf16_hi(pa[gi >> 1]) : bf16_lo(pa[gi >> 1]);
+          sbv = (gi & 1) ? bf16_hi(pb[gi >> 1]) : bf16_lo(pb[gi >> 1]);
+          ba = (gi & 1) ? bf16_hi(qa[gi >> 1]) : bf16_lo(qa[gi >> 1]);
+          bb = (gi & 1) ? bf16_hi(qb[gi >> 1]) : bf16_lo(qb[gi >> 1]);
+        } else {
+          const int g = gfirst + gl;
+          const int na = min(n0 + ra, p.N - 1), nb = min(n0 + rb, p.N - 1);
+          sa = bf2f(p.scales[(size_t)na * p.G + g]);
+          sbv = bf2f(p.scales[(size_t)nb * p.G + g]);
+          ba = bf2f(p.biases[(size_t)na * p.G + g]);
+          bb = bf2f(p.biases[(size_t)nb * p.G + g]);
+        }
+        const float ca = ba - MAGIC * sa, cb = bb - MAGIC * sbv;
+#pragma unroll
+        for (int r = 0; r < RT; ++r) {
+          const float2 s2 = *reinterpret_cast<const float2*>(&sx[gl * RP + r * 8 + 2 * tig]);
+          acc[r][0] = fmaf(sa, P[r][0], fmaf(ca, s2.x, acc[r][0]));
+          acc[r][1] = fmaf(sa, P[r][1], fmaf(ca, s2.y, acc[r][1]));
+          acc[r][2] = fmaf(sbv, P[r][2], fmaf(cb, s2.x, acc[r][2]));
+          acc[r][3] = fmaf(sbv, P[r][3], fmaf(cb, s2.y, acc[r][3]));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+
+    // partial tile -> shared memory [m][n]
+#pragma unroll
+    for (int r = 0; r < RT; ++r) {
+      const int m = r * 8 + 2 * tig;
+      part[m * PSTR + ra] = acc[r][0];
+      part[(m + 1) * PSTR + ra] = acc[r][1];
+      part[m * PSTR + rb] = acc[r][2];
+      part[(m + 1) * PSTR + rb] = acc[r][3];
+    }
+    __syncwarp();
+  }
+
+  // ------------------------------------------------------------- split-K reduction
+  if (cs > 1) cluster_sync_all(); else __syncthreads();
+  const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;  // rows m = rank + i*cs
+  for (int idx = threadIdx.x; idx < nmine * (TN / 4); idx += NTHR) {
+    const int mi = idx / (TN / 4), n4 = idx - mi * (TN / 4);
+    const int m = rank + mi * cs;
+    const uint32_t a = smem_u32(&part[m * PSTR + n4 * 4]);
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (cs > 1) {
+      for (int c = 0; c < cs; ++c) {
+        const float4 v = ld_dsmem_f4(mapa_shared(a, c));
+        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+      }
+    } else {
+      s = *reinterpret_cast<const float4*>(&part[m * PSTR + n4 * 4]);
+    }
+    *reinterpret_cast<float4*>(&red[m * PSTR + n4 * 4]) = s;
+  }
+  if (cs > 1) cluster_sync_all(); else __syncthreads();
+
+  // ------------------------------------------------------------- epilogues
+  if constexpr (EPI == EPI_PLAIN) {
+    for (int idx = threadIdx.x; idx < nmine * (TN / 2); idx += NTHR) {
+      const int mi = idx / (TN / 2), n2 = idx - mi * (TN / 2);
+      const int m = rank + mi * cs;
+      const int n = n0 + n2 * 2;
+      if (n >= p.N) continue;
+      float v0 = round_bf16(red[m * PSTR + n2 * 2]);
+      float v1 = round_bf16(red[m * PSTR + n2 * 2 + 1]);
+      if (p.bias != nullptr) {
+        v0 += bf2f(p.bias[n]);
+        v1 += bf2f(p.bias[n + 1]);
+      }
+      *reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n) = pack_bf16x2(v0, v1);
+    }
+  } else if constexpr (EPI == EPI_RESID) {
+    // out = bf16(bf16(acc) + resid); ssq_out[ntile][m] = sum over the tile of out^2
+    for (int mi = warp; mi < nmine; mi += NW + 1) {
+      const int m = rank + mi * cs;
+      float ss = 0.f;
+      for (int n2 = lane; n2 < TN / 2; n2 += 32) {
+        const int n = n0 + n2 * 2;
+        if (n >= p.N) continue;
+        const uint32_t rr = __ldcg(reinterpret_cast<const unsigned int*>(p.resid + (size_t)m * p.ldr + n));
+        const float h0 = round_bf16(round_bf16(red[m * PSTR + n2 * 2]) + bf16_lo(rr));
+        const float h1 = round_bf16(round_bf16(red[m * PSTR + n2 * 2 + 1]) + bf16_hi(rr));
+        *reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n) = pack_bf16x2(h0, h1);
+        ss += h0 * h0 + h1 * h1;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0 && p.ssq_out != nullptr) p.ssq_out[ntile * p.ssq_stride + m] = ss;
+    }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    // tile rows: pairs of (32 gate rows, 32 up rows); act column = pair*32 + j
+    constexpr int PAIRS = TN / 64;
+    for (int idx = threadIdx.x; idx < nmine * PAIRS * 32; idx += NTHR) {
+      const int mi = idx / (PAIRS * 32), rem = idx - mi * (PAIRS * 32);
+      const int pr = rem >> 5, j = rem & 31;
+      const int m = rank + mi * cs;
+      const int a = (ntile * PAIRS + pr) * 32 + j;
+      if (a >= p.n_act) continue;
+      const float g = round_bf16(red[m * PSTR + pr * 64 + j]);
+      const float u = round_bf16(red[m * PSTR + pr * 64 + 32 + j]);
+      p.out[(size_t)m * p.ldo + a] = __float2bfloat16_rn(silu_mul(g, u));
+    }
+  } else if constexpr (EPI == EPI_QKROPE) {
+    // tile = TN/128 heads of 128; columns [q heads | k heads | v heads]
+    constexpr int HPT = TN / 128;
+    for (int u = warp; u < nmine * HPT; u += NW + 1) {
+      const int mi = u / HPT, t = u - mi * HPT;
+      const int m = rank + mi * cs;
+      const int hh = n0 / 128 + t;
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = round_bf16(red[m * PSTR + t * 128 + lane + 32 * i]);
+      const int pos = p.row_pos[m];
+      const int64_t kvo = p.row_kv != nullptr ? p.row_kv[m] : 0;
+      if (hh >= p.hq && (pos < 0 || pos >= p.kv_cap)) {  // never write past a cache slot
+        if (lane == 0) report_error(p.status, 0x301);
+        continue;
+      }
+      if (hh < p.hq + p.hk) {
+        const bool isq = hh < p.hq;
+        const bf16* nw = isq ? p.qnorm : p.knorm;
+        float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float r = rsqrtf(ss / 128.0f + p.eps);
+        float y[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) y[i] = round_bf16(v[i] * r * bf2f(nw[lane + 32 * i]));
+        // rotate-half RoPE: pairs (d, d+64) for d = lane, lane+32
+        float o[4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float f = p.inv_freq[lane + 32 * i];
+          float sn, c;
+          sincosf(float(pos) * f, &sn, &c);
+          o[i] = y[i] * c - y[i + 2] * sn;
+          o[i + 2] = y[i] * sn + y[i + 2] * c;
+        }
+        if (isq) {
+          bf16* dst = p.qout + (size_t)m * p.ldq + hh * 128;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(o[i]);
+        } else {
+          bf16* dst = p.kcache + kvo + (int64_t)(hh - p.hq) * p.k_sh + (int64_t)pos * p.k_ss;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(o[i]);
+        }
+      } else if (hh < p.hq + 2 * p.hk) {
+        bf16* dst = p.vcache + kvo + (int64_t)(hh - p.hq - p.hk) * p.v_sh + (int64_t)pos * p.v_ss;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------- host side
+
+struct TmapKey {
+  const void* ptr;
+  uint64_t d0, d1, stride;
+  uint32_t b0, b1;
+  int dt, swz;
+  bool operator==(const TmapKey& o) const {
+    return ptr == o.ptr && d0 == o.d0 && d1 == o.d1 && stride == o.stride && b0 == o.b0 &&
+           b1 == o.b1 && dt == o.dt && swz == o.swz;
+  }
+};
+struct TmapKeyHash {
+  size_t operator()(const TmapKey& k) const {
+    size_t h = reinterpret_cast<size_t>(k.ptr);
+    h ^= (k.d0 * 0x9E3779B97F4A7C15ull) ^ (k.d1 << 17) ^ (k.stride << 5) ^ (size_t(k.b1) << 40);
+    return h;
+  }
+};
+
+static std::mutex g_tmap_mu;
+static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> g_tmap_cache;
+
+static bool get_tmap(CUtensorMap* out, CUtensorMapDataType dt, const void* base, uint64_t d0,
+                     uint64_t d1, uint64_t stride, uint32_t b0, uint32_t b1,
+                     CUtensorMapSwizzle swz) {
+  TmapKey key{base, d0, d1, stride, b0, b1, int(dt), int(swz)};
+  {
+    std::lock_guard<std::mutex> lk(g_tmap_mu);
+    auto it = g_tmap_cache.find(key);
+    if (it != g_tmap_cache.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  if (!encode_tmap_2d(out, dt, base, d0, d1, stride, b0, b1, swz)) return false;
+  std::lock_guard<std::mutex> lk(g_tmap_mu);
+  if (g_tmap_cache.size() > 65536) g_tmap_cache.clear();
+  g_tmap_cache[key] = *out;
+  return true;
+}
+
+template <int BITS, int RT, int NW, int EPI, bool SCT>
+static int launch_one(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream) {
+  auto kern = qmm_kernel<BITS, RT, NW, EPI, SCT>;
+  constexpr int TN = 16 * NW;
+  const SmemLayout L = smem_layout<BITS, NW, RT>(pl.kslice, pl.nslots);
+  static int configured_smem = 0;  // per instantiation
+  if (L.total > configured_smem) {
+    DSPARK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total),
+                    "qmm: set smem");
+    DSPARK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                    "qmm: allow cluster 16");
+    const int carve = env_int("DSPARK_QMM_CARVEOUT", -1);
+    if (carve >= 0)
+      DSPARK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, carve),
+                      "qmm: carveout");
+    configured_smem = L.total;
+  }
+  CUtensorMap wmap, smap, bmap;
+  const uint64_t words = (uint64_t)p.K * BITS / 32;
+  if (!get_tmap(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.wq, words, p.N, words * 4, 32, TN,
+                CU_TENSOR_MAP_SWIZZLE_128B))
+    return DSPARK_ERR_CUDA;
+  if (SCT) {
+    if (!get_tmap(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, p.scales, p.G, p.N, (uint64_t)p.G * 2,
+                  8, TN, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return DSPARK_ERR_CUDA;
+    if (!get_tmap(&bmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, p.biases, p.G, p.N, (uint64_t)p.G * 2,
+                  8, TN, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return DSPARK_ERR_CUDA;
+  } else {
+    smap = wmap;
+    bmap = wmap;
+  }
+  dim3 grid(pl.cs, (p.N + TN - 1) / TN);
+  dim3 block((NW + 1) * 32);
+  DSPARK_CUDA_TRY(launch_ex(kern, grid, block, (size_t)L.total, stream, pl.cs, true, wmap, smap, bmap, p),
+                  "qmm: launch");
+  return DSPARK_OK;
+}
+
+template <int BITS, int RT, int EPI>
+static int dispatch_nw(const QmmParams& p, const QmmPlan& pl, cudaStream_t s) {
+  const bool sct = pl.sct;
+  if constexpr (EPI == EPI_PLAIN) {
+    if (pl.nw == 2) return sct ? launch_one<BITS, RT, 2, EPI, true>(p, pl, s) : launch_one<BITS, RT, 2, EPI, false>(p, pl, s);
+    if (pl.nw == 4) return sct ? launch_one<BITS, RT, 4, EPI, true>(p, pl, s) : launch_one<BITS, RT, 4, EPI, false>(p, pl, s);
+    if (pl.nw == 8) return sct ? launch_one<BITS, RT, 8, EPI, true>(p, pl, s) : launch_one<BITS, RT, 8, EPI, false>(p, pl, s);
+  } else if constexpr (EPI == EPI_QKROPE) {
+    if (!sct) return fail(DSPARK_ERR_UNSUPPORTED, "qmm: fused epilogues need K %% 512 == 0");
+    if (pl.nw == 8) return launch_one<BITS, RT, 8, EPI, true>(p, pl, s);
+  } else {
+    if (!sct) return fail(DSPARK_ERR_UNSUPPORTED, "qmm: fused epilogues need K %% 512 == 0");
+    if (pl.nw == 4) return launch_one<BITS, RT, 4, EPI, true>(p, pl, s);
+    if (pl.nw == 8) return launch_one<BITS, RT, 8, EPI, true>(p, pl, s);
+  }
+  return fail(DSPARK_ERR_UNSUPPORTED, "qmm: no kernel for %d warps with epilogue %d", pl.nw, EPI);
+}
+
+template <int BITS, int EPI>
+static int dispatch_rt(const QmmParams& p, const QmmPlan& pl, cudaStream_t s) {
+  if (p.M <= 8) return dispatch_nw<BITS, 1, EPI>(p, pl, s);
+  if (p.M <= 16) return dispatch_nw<BITS, 2, EPI>(p, pl, s);
+  return dispatch_nw<BITS, 4, EPI>(p, pl, s);
+}
+
+// Launch geometry for [N, K] at `bits` and row class rt: tile width (16 * nw output
+// columns), split-K factor (cluster size) and ring depth. Modelled per SM as: the bytes its
+// CTAs stream (load balance over SMs), a fixed per-CTA latency (x staging, first TMA bytes,
+// split-K reduction), and a penalty for shallow pipelines.
+QmmPlan plan(int N, int K, int bits, int epi, int min_tn, int rt) {
+  QmmPlan pl;
+  const int sms = sm_count(current_device());
+  pl.sct = (K % 512 == 0);
+  int nw_choices[3] = {2, 4, 8};
+  double best = 1e30;
+  const int force_nw = env_int("DSPARK_QMM_NW", 0);
+  const int force_cs = env_int("DSPARK_QMM_CS", 0);
+  const double bw_sm = 6.5e12 / sms;     // bytes/s each SM can draw when all stream
+  const double t_fix = 2.0e-6;           // per-CTA fixed latency (s)
+  for (int nw : nw_choices) {
+    if (16 * nw < min_tn) continue;
+    if (epi != EPI_PLAIN && nw == 2) continue;
+    if (epi == EPI_QKROPE && nw != 8) continue;
+    if (force_nw && nw != force_nw) continue;
+    const int tn = 16 * nw;
+    const int ntiles = (N + tn - 1) / tn;
+    for (int cs = 1; cs <= 16; ++cs) {
+      if (force_cs && cs != force_cs) continue;
+      if (cs > 8 && cs != 16) continue;
+      const int kslice = ((K + cs - 1) / cs + KSTG - 1) / KSTG * KSTG;
+      if ((cs - 1) * kslice >= K) continue;  // every rank needs work
+      const int nst = (kslice + KSTG - 1) / KSTG;
+      const int ctas = cs * ntiles;
+      const double wbytes = double(tn) * kslice * bits / 8.0;  // weight bytes per CTA
+      int slots = std::min(nst, std::max(1, env_int("DSPARK_QMM_SLOTS", 4)));
+      while (slots > 1 && smem_bytes(bits, nw, rt, kslice, slots) > kSmemBudget) --slots;
+      if (smem_bytes(bits, nw, rt, kslice, slots) > kSmemBudget) continue;
+      const int smem = smem_bytes(bits, nw, rt, kslice, slots);
+      const int occ = std::max(1, std::min(2048 / (32 * (nw + 1)), (227 * 1024) / std::max(smem, 1)));
+      // CTAs per SM over the launch, and the SM that gets the most
+      const double per_sm = std::ceil(double(ctas) / sms);
+      const double rounds = std::ceil(per_sm / occ);
+      double t = per_sm * wbytes / bw_sm + rounds * t_fix;
+      if (slots < std::min(nst, 3)) t *= 1.0 + 0.25 * (std::min(nst, 3) - slots);
+      t *= 1.0 + 0.01 * (cs - 1);  // split-K reduction
+      if (t < best) {
+        best = t;
+        pl.nw = nw;
+        pl.cs = cs;
+        pl.kslice = kslice;
+        pl.nslots = slots;
+      }
+    }
+  }
+  if (best >= 1e30) pl.nw = 0;
+  pl.rt = rt;
+  return pl;
+}
+
+int run(const QmmParams& p_in, int epi, const QmmPlan* plan_in, cudaStream_t stream) {
+  QmmParams p = p_in;
+  if (p.bits != 4 && p.bits != 8) return fail(DSPARK_ERR_UNSUPPORTED, "qmm: bits must be 4 or 8 (got %d)", p.bits);
+  if (p.M < 1 || p.M > 32) return fail(DSPARK_ERR_UNSUPPORTED, "qmm: M=%d outside 1..32", p.M);
+  if (p.K <= 0 || p.K % 64 || p.N <= 0 || p.N % 8)
+    return fail(DSPARK_ERR_UNSUPPORTED, "qmm: need K %% 64 == 0 and N %% 8 == 0 (K=%d N=%d)", p.K, p.N);
+  if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (p.ldx & 7))
+    return fail(DSPARK_ERR_UNSUPPORTED, "qmm: x must be 16-byte aligned with ldx %% 8 == 0");
+  if ((reinterpret_cast<uintptr_t>(p.wq) & 15) || (reinterpret_cast<uintptr_t>(p.out) & 3) || (p.ldo & 1))
+    return fail(DSPARK_ERR_UNSUPPORTED, "qmm: weights must be 16-byte aligned, out 4-byte aligned with even ldo");
+  if ((reinterpret_cast<uintptr_t>(p.norm_w) & 15) || (p.resid && ((reinterpret_cast<uintptr_t>(p.resid) & 3) || (p.ldr & 1))))
+    return fail(DSPARK_ERR_UNSUPPORTED, "qmm: norm weight must be 16-byte aligned, residual 4-byte aligned");
+  p.G = p.K / 64;
+  if (p.status == nullptr) p.status = status_word(current_device());
+  const int rt = p.M <= 16 ? 2 : 4;
+  QmmPlan pl = plan_in ? *plan_in : plan(p.N, p.K, p.bits, epi, epi == EPI_QKROPE ? 128 : 0, rt);
+  if (pl.nw == 0) return fail(DSPARK_ERR_UNSUPPORTED, "qmm: no launch geometry for N=%d K=%d", p.N, p.K);
+  if (pl.rt < rt)
+    return fail(DSPARK_ERR_ARG, "qmm: plan made for %d rows used for M=%d", 8 * pl.rt, p.M);
+  if (pl.sct && ((reinterpret_cast<uintptr_t>(p.scales) & 15) || (reinterpret_cast<uintptr_t>(p.biases) & 15)))
+    pl.sct = false;
+  p.kslice = pl.kslice;
+  p.cs = pl.cs;
+  p.nslots = pl.nslots;
+  if (p.bits == 4) {
+    switch (epi) {
+      case EPI_PLAIN: return dispatch_rt<4, EPI_PLAIN>(p, pl, stream);
+      case EPI_RESID: return dispatch_rt<4, EPI_RESID>(p, pl, stream);
+      case EPI_SWIGLU: return dispatch_rt<4, EPI_SWIGLU>(p, pl, stream);
+      case EPI_QKROPE: return dispatch_rt<4, EPI_QKROPE>(p, pl, stream);
+    }
+  } else {
+    switch (epi) {
+      case EPI_PLAIN: return dispatch_rt<8, EPI_PLAIN>(p, pl, stream);
+      case EPI_RESID: return dispatch_rt<8, EPI_RESID>(p, pl, stream);
+      case EPI_SWIGLU: return dispatch_rt<8, EPI_SWIGLU>(p, pl, stream);
+      case EPI_QKROPE: return dispatch_rt<8, EPI_QKROPE>(p, pl, stream);
+    }
+  }
+  return fail(DSPARK_ERR_ARG, "qmm: bad epilogue %d", epi);
+}
+
+}  // namespace qmm
+}  // namespace dspark

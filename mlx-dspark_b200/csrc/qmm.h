@@ -1,0 +1,69 @@
+// Internal interface of the small-M quantized matmul (K1); the C ABI is in include/dspark.h.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dspark {
+namespace qmm {
+
+enum Epilogue { EPI_PLAIN = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKROPE = 3 };
+
+struct QmmParams {
+  const __nv_bfloat16* x = nullptr;  // [M, K] row stride ldx (elements)
+  long ldx = 0;
+  const uint32_t* wq = nullptr;      // [N, K*bits/32]
+  const __nv_bfloat16* scales = nullptr;  // [N, K/64]
+  const __nv_bfloat16* biases = nullptr;  // [N, K/64]
+  const __nv_bfloat16* bias = nullptr;    // optional [N] (EPI_PLAIN)
+  __nv_bfloat16* out = nullptr;      // [M, N] row stride ldo (EPI_SWIGLU: [M, N/2])
+  long ldo = 0;
+  int M = 0, N = 0, K = 0, G = 0, bits = 4;
+  // launch geometry (filled from the plan)
+  int kslice = 0, cs = 1, nslots = 1;
+  int* status = nullptr;
+  // prologue RMSNorm of x: rs[m] = rsqrt(sum_e ssq_in[e*ssq_stride+m] / K + eps); x *= rs*norm_w
+  const __nv_bfloat16* norm_w = nullptr;
+  const float* ssq_in = nullptr;
+  int ssq_n = 0;
+  int ssq_stride = 32;
+  float eps = 1e-6f;
+  // EPI_RESID: out = bf16(bf16(acc) + resid); ssq_out[ntile*ssq_stride + m] = sum(out^2)
+  const __nv_bfloat16* resid = nullptr;
+  long ldr = 0;
+  float* ssq_out = nullptr;
+  // EPI_SWIGLU: number of activation columns (N/2)
+  int n_act = 0;
+  // EPI_QKROPE: Qwen3 q/k RMSNorm + rotate-half RoPE + KV-cache write (head_dim 128)
+  int hq = 0, hk = 0;
+  const __nv_bfloat16* qnorm = nullptr;
+  const __nv_bfloat16* knorm = nullptr;
+  const float* inv_freq = nullptr;   // [64] theta^(-2i/128)
+  __nv_bfloat16* qout = nullptr;     // [M, hq*128]
+  long ldq = 0;
+  __nv_bfloat16* kcache = nullptr;
+  __nv_bfloat16* vcache = nullptr;
+  int64_t k_sh = 0, k_ss = 0, v_sh = 0, v_ss = 0;  // head / position strides (elements)
+  int kv_cap = 0;                    // positions per cache slot (writes at pos >= kv_cap are dropped)
+  const int32_t* row_pos = nullptr;  // [M] absolute position of each row
+  const int64_t* row_kv = nullptr;   // [M] element offset of the row's cache slot (or null)
+};
+
+struct QmmPlan {
+  int nw = 0;       // consumer warps; tile width 16*nw output columns
+  int cs = 1;       // split-K factor == cluster size
+  int kslice = 0;   // k per cluster rank (multiple of 512)
+  int nslots = 1;   // pipeline depth
+  bool sct = true;  // scales/biases by TMA (needs K % 512 == 0)
+  int rt = 2;       // row class the plan was made for (serves M <= 8 * rt)
+};
+
+// Geometry for [N, K] at `bits` serving up to 8*rt rows (rt = 2: M <= 16, rt = 4: M <= 32).
+// It depends on the weight shape and the row class only, so within a class a row's result
+// never depends on how many rows ride with it.
+QmmPlan plan(int N, int K, int bits, int epi, int min_tn, int rt = 2);
+int run(const QmmParams& p, int epi, const QmmPlan* plan, cudaStream_t stream);
+
+}  // namespace qmm
+}  // namespace dspark

@@ -1,0 +1,147 @@
+"""K2 parity on the GPU: dspark_verify_attn vs the CPU oracle (mirrors
+tests/test_multirow_attn.py and the tree-mask cases of tests/test_tree.py:479-500).
+
+Tolerances: rel-err max|out - ref| <= 1e-2 * max|ref| (the build's stated bound), and the
+reference's own rule (tests/test_multirow_attn.py:80) with the ideal bf16 rounding of the
+fp32 oracle standing in for MLX's error: err <= 2 * err(bf16(ref)) + 2e-3.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+REL = 1e-2
+
+
+def _mk(B, hq, hk, q_len, L, d, slack=0, seed=0, dev="cuda"):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    q = torch.randn((B, hq, q_len, d), generator=g).to(torch.bfloat16)
+    k = torch.randn((B, hk, L + slack, d), generator=g).to(torch.bfloat16)
+    v = torch.randn((B, hk, L + slack, d), generator=g).to(torch.bfloat16)
+    q, k, v = q.to(dev), k.to(dev), v.to(dev)
+    if slack:  # a cache-style view into a larger buffer
+        k, v = k[:, :, :L], v[:, :, :L]
+    return q, k, v
+
+
+def _bits(t):
+    return t.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _ref(oracle, q, k, v, scale, causal, anc=None):
+    return oracle.sdpa(_bits(q), _bits(k), _bits(v), scale, causal, anc)
+
+
+def _check(oracle, out, ref):
+    o = out.float().cpu().numpy()
+    mine = float(np.abs(o - ref).max())
+    ideal = float(np.abs(oracle.round_bf16(ref) - ref).max())
+    assert mine <= REL * max(float(np.abs(ref).max()), 1e-6), (mine, float(np.abs(ref).max()))
+    assert mine <= 2.0 * ideal + 2e-3, (mine, ideal)
+
+
+CASES = [
+    # B, hq, hk, q_len, L, d
+    (1, 32, 8, 15, 777, 128),     # drafter-block geometry, off-grid tail
+    (1, 32, 8, 2, 64, 128),
+    (1, 32, 2, 16, 500, 128),     # GQA 16 -> 256 rows: row groups
+    (2, 8, 8, 5, 129, 64),        # MHA, batch 2
+    (1, 16, 2, 7, 16, 128),       # KV exactly one 16-key tile
+    (1, 4, 1, 3, 23, 64),         # MQA, short tail
+    (1, 32, 8, 16, 1024, 128),    # BASELINE verify shape at 1k
+    (3, 32, 8, 16, 2049, 128),    # batch 3, odd length
+]
+
+
+@pytest.mark.parametrize("B,hq,hk,q_len,L,d", CASES)
+@pytest.mark.parametrize("causal", [True, False])
+def test_matches_oracle(cuda, oracle, B, hq, hk, q_len, L, d, causal):
+    from mlx_dspark_b200.multirow_attn import multirow_sdpa
+
+    q, k, v = _mk(B, hq, hk, q_len, L, d, slack=37, seed=L + q_len)
+    scale = d ** -0.5
+    c = causal and q_len > 1
+    out = multirow_sdpa(q, k, v, scale=scale, causal=c)
+    assert out.shape == q.shape and out.dtype == q.dtype
+    _check(oracle, out, _ref(oracle, q, k, v, scale, c))
+
+
+@pytest.mark.parametrize("L", [1024, 4096, 16384, 32768])
+def test_baseline_config(cuda, oracle, L):
+    """GQA 32/8, head_dim 128, 16 causal rows, KV lengths 1k..32k."""
+    from mlx_dspark_b200.multirow_attn import multirow_sdpa
+
+    q, k, v = _mk(1, 32, 8, 16, L, 128, seed=L)
+    out = multirow_sdpa(q, k, v, scale=128 ** -0.5, causal=True)
+    _check(oracle, out, _ref(oracle, q, k, v, 128 ** -0.5, True))
+
+
+def test_head_dim_256_is_refused_loudly(cuda):
+    from mlx_dspark_b200 import DSparkUnsupported
+    from mlx_dspark_b200.multirow_attn import multirow_sdpa
+
+    q, k, v = _mk(1, 24, 4, 8, 300, 256)
+    with pytest.raises(DSparkUnsupported):
+        multirow_sdpa(q, k, v, scale=256 ** -0.5, causal=True)
+
+
+def test_causal_rows_see_only_their_prefix(cuda, oracle):
+    """Masked keys made dominant: a mask leak would swamp the output
+    (tests/test_multirow_attn.py:90-99)."""
+    from mlx_dspark_b200.multirow_attn import multirow_sdpa
+
+    q, k, v = _mk(1, 4, 4, 4, 64, 64)
+    k = torch.cat([k[:, :, :-3], 50.0 * torch.ones_like(k[:, :, -3:])], dim=2)
+    v = torch.cat([v[:, :, :-3], 1e3 * torch.ones_like(v[:, :, -3:])], dim=2)
+    out = multirow_sdpa(q, k, v, scale=0.125, causal=True)
+    ref = _ref(oracle, q, k, v, 0.125, True)
+    assert float(np.abs(out.float().cpu().numpy() - ref).max()) < 50.0
+
+
+def test_per_row_kv_lengths(cuda, oracle):
+    """kv_len per batch row (ragged rows of the batch engine)."""
+    from mlx_dspark_b200.multirow_attn import multirow_sdpa
+
+    B, hq, hk, qL, L, d = 3, 32, 8, 12, 900, 128
+    q, k, v = _mk(B, hq, hk, qL, L, d, seed=9)
+    lens = [900, 413, 12]
+    kv_len = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    out = multirow_sdpa(q, k, v, scale=d ** -0.5, causal=True, kv_len=kv_len)
+    for b, Lb in enumerate(lens):
+        ref = _ref(oracle, q[b : b + 1], k[b : b + 1, :, :Lb], v[b : b + 1, :, :Lb], d ** -0.5,
+                   True)
+        _check(oracle, out[b : b + 1], ref)
+
+
+TREES = [
+    [-1, 0, 0, 1, 1, 2, 3, 0],
+    [-1, 0, 1, 2, 3, 0, 5, 1, 7, 2, 9, 0, 11, 12, 1, 14],
+]
+
+
+@pytest.mark.parametrize("parent", TREES)
+@pytest.mark.parametrize("hq,hk,d", [(8, 2, 128), (32, 8, 128), (16, 4, 64)])
+def test_tree_mask_variant(cuda, oracle, parent, hq, hk, d):
+    from mlx_dspark_b200.multirow_attn import multirow_sdpa, tree_bits
+
+    w = len(parent)
+    q, k, v = _mk(1, hq, hk, w, 301 + w, d, seed=w)
+    anc = np.array(tree_bits(parent), dtype=np.uint32)
+    out = multirow_sdpa(q, k, v, scale=d ** -0.5, causal=False,
+                        tree_anc=torch.from_numpy(anc.view(np.int32)).to(cuda))
+    _check(oracle, out, _ref(oracle, q, k, v, d ** -0.5, False, anc))
+
+
+def test_output_strides(cuda, oracle):
+    """Output written straight into a [rows, heads*D] layout (the forward's o_proj input)."""
+    from mlx_dspark_b200.multirow_attn import multirow_sdpa
+
+    q, k, v = _mk(1, 32, 8, 16, 2048, 128, seed=4)
+    buf = torch.zeros((16, 32 * 128), dtype=torch.bfloat16, device=cuda)
+    view = buf.view(16, 32, 128).permute(1, 0, 2).unsqueeze(0)  # [1, 32, 16, 128]
+    multirow_sdpa(q, k, v, scale=128 ** -0.5, causal=True, out=view)
+    _check(oracle, view, _ref(oracle, q, k, v, 128 ** -0.5, True))

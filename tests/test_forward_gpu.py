@@ -1,0 +1,130 @@
+"""Full verify forward on the GPU (fused kernels, one C call) vs the oracle's restatement of
+the Qwen3 dense forward (Target.verify -> _body_mlxlm + head, src/mlx_dspark/target.py:642,
+:208-221).
+
+Bars: logits relative error ||gpu - ref||_2 / ||ref||_2 <= 1e-2 against the oracle's bf16
+logits (a bf16 dataflow differs from any other bf16 dataflow by rounding flips of ~1 ulp
+that propagate layer to layer, so the whole-forward bar is stated on the L2 norm; every
+single op is held to max-abs 1e-2 in its own test); greedy argmax identical on every row
+whose oracle top-2 margin exceeds twice the observed max logit error (near-ties are
+reported, the reference's "fp-tie class", src/mlx_dspark/small_m_qmm.py:24-28); cache rows
+written by the forward within 2e-2 * max|row| of the oracle's; accept + rollback lengths
+bit-exact.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _prefill(target, L0, seed=0):
+    g = torch.Generator(device=target.device).manual_seed(seed)
+    kc, vc = [], []
+    for L in target.layers:
+        L["k_cache"][0, :, :L0] = torch.randn(L["k_cache"][0, :, :L0].shape, device=target.device,
+                                              generator=g).to(torch.bfloat16)
+        L["v_cache"][0, :, :L0] = torch.randn(L["v_cache"][0, :, :L0].shape, device=target.device,
+                                              generator=g).to(torch.bfloat16)
+        kc.append(L["k_cache"][0].float().cpu().numpy().copy())
+        vc.append(L["v_cache"][0].float().cpu().numpy().copy())
+    return kc, vc
+
+
+def _compare(oracle, got, ref):
+    ref = oracle.round_bf16(ref)
+    rel = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+    assert rel <= 1e-2, rel
+    err = float(np.abs(got - ref).max())
+    tt_ref = oracle.argmax_first(ref)
+    tt_got = oracle.argmax_first(got)
+    srt = np.sort(ref, axis=1)
+    margin = srt[:, -1] - srt[:, -2]
+    decided = margin > 2 * err + 1e-6
+    assert np.array_equal(tt_got[decided], tt_ref[decided]), (tt_got, tt_ref, margin)
+    return err, int((~decided).sum())
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("R,L0", [(16, 300), (5, 1), (1, 777), (16, 2048)])
+def test_verify_forward_matches_oracle(cuda, oracle, bits, R, L0):
+    from mlx_dspark_b200.target import Target, tiny_config
+
+    cfg = tiny_config(bits=bits)
+    t = Target(cfg, kv_cap=4096, seed=bits)
+    kc, vc = _prefill(t, L0, seed=R)
+    ids = torch.randint(0, cfg.vocab, (R,), device=cuda, dtype=torch.int32)
+    lens = torch.tensor([L0], dtype=torch.int32, device=cuda)
+    logits = t.verify(ids, lens).float().cpu().numpy()
+    assert int(lens[0]) == L0 + R
+    ref = oracle.verify_forward(t.oracle_weights(), t.oracle_config(), ids.cpu().numpy(),
+                                kc, vc, L0)
+    _compare(oracle, logits, ref)
+    # the block's K/V rows landed in the cache (q/k-norm + RoPE applied to K)
+    for li, L in enumerate(t.layers):
+        for name, ref_c in (("k_cache", kc[li]), ("v_cache", vc[li])):
+            got_c = L[name][0, :, L0 : L0 + R].float().cpu().numpy()
+            want = ref_c[:, L0 : L0 + R]
+            assert float(np.abs(got_c - want).max()) <= 2e-2 * float(np.abs(want).max()), name
+        # rows before the block are untouched
+        assert np.array_equal(L["k_cache"][0, :, :L0].float().cpu().numpy(), kc[li][:, :L0])
+
+
+def test_accept_and_rollback(cuda, oracle):
+    """One spec round: drafts that follow the target's own argmax for a prefix are accepted,
+    the rest rejected; the cache length ends at L0 + n + 1 (bit-exact)."""
+    from mlx_dspark_b200.target import Target, tiny_config
+
+    cfg = tiny_config()
+    t = Target(cfg, kv_cap=2048, seed=3)
+    _prefill(t, 500, seed=1)
+    R = 16
+    ids = torch.randint(0, cfg.vocab, (R,), device=cuda, dtype=torch.int32)
+    lens = torch.tensor([500], dtype=torch.int32, device=cuda)
+    logits = t.verify(ids, lens)
+    tt = logits.float().argmax(dim=1).to(torch.int32)
+    # rebuild the block so drafts 1..5 match: rerun from the same length
+    ids2 = ids.clone()
+    for _ in range(R):  # fixed point: each draft = argmax of the previous row
+        lens.fill_(500)
+        tt = t.verify(ids2, lens).float().argmax(dim=1).to(torch.int32)
+        ids2[1:6] = tt[0:5]
+    lens.fill_(500)
+    logits = t.verify(ids2, lens)
+    out = t.accept_and_rollback(logits, ids2, lens)
+    tt = oracle.argmax_first(logits.float().cpu().numpy())
+    n, committed, trim = oracle.accept(ids2[1:].cpu().numpy(), tt)
+    assert n >= 5
+    assert int(out["n"][0]) == n and int(out["next"][0]) == committed[-1]
+    assert int(lens[0]) == 500 + n + 1
+
+
+def test_qwen3_8b_shape_runs(cuda):
+    """Full Qwen3-8B-shaped model (36 layers, 4-bit): one verify block at 2k context runs,
+    produces finite logits and advances the length; graph capture replays identically."""
+    from mlx_dspark_b200.target import QWEN3_8B, Target
+
+    t = Target(QWEN3_8B, kv_cap=4096, seed=0)
+    for L in t.layers:
+        L["k_cache"][0, :, :2048].normal_()
+        L["v_cache"][0, :, :2048].normal_()
+    ids = torch.randint(0, QWEN3_8B.vocab, (16,), device=cuda, dtype=torch.int32)
+    lens = torch.tensor([2048], dtype=torch.int32, device=cuda)
+    a = t.verify(ids, lens).clone()
+    assert torch.isfinite(a.float()).all()
+    assert int(lens[0]) == 2064
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        lens.fill_(2048)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            lens.fill_(2048)
+            t.verify(ids, lens)
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(t.logits[:16], a)
