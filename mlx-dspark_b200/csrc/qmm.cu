@@ -30,11 +30,13 @@
 //    + KV-cache write. The prologue can apply RMSNorm to x while staging it.
 #include <algorithm>
 #include <mutex>
+#include <string>
 #include <unordered_map>
 
 #include "common.cuh"
 #include "host_common.h"
 #include "qmm.h"
+#include "qmm_epilogue.cuh"
 
 namespace dspark {
 namespace qmm {
@@ -115,8 +117,6 @@ static int smem_bytes(int bits, int nw, int rt, int kslice, int nslots) {
   off = (off + 15) & ~15;
   return off + 2 * nslots * 8 + 1024;
 }
-
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
 
 // ----------------------------------------------------------------------------- kernel
 
@@ -452,104 +452,7 @@ __global__ void __launch_bounds__((NW + 1) * 32)
   }
   if (cs > 1) cluster_sync_all(); else __syncthreads();
 
-  // ------------------------------------------------------------- epilogues
-  if constexpr (EPI == EPI_PLAIN) {
-    for (int idx = threadIdx.x; idx < nmine * (TN / 2); idx += NTHR) {
-      const int mi = idx / (TN / 2), n2 = idx - mi * (TN / 2);
-      const int m = rank + mi * cs;
-      const int n = n0 + n2 * 2;
-      if (n >= p.N) continue;
-      float v0 = round_bf16(red[m * PSTR + n2 * 2]);
-      float v1 = round_bf16(red[m * PSTR + n2 * 2 + 1]);
-      if (p.bias != nullptr) {
-        v0 += bf2f(p.bias[n]);
-        v1 += bf2f(p.bias[n + 1]);
-      }
-      *reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n) = pack_bf16x2(v0, v1);
-    }
-  } else if constexpr (EPI == EPI_RESID) {
-    // out = bf16(bf16(acc) + resid); ssq_out[ntile][m] = sum over the tile of out^2
-    for (int mi = warp; mi < nmine; mi += NW + 1) {
-      const int m = rank + mi * cs;
-      float ss = 0.f;
-      for (int n2 = lane; n2 < TN / 2; n2 += 32) {
-        const int n = n0 + n2 * 2;
-        if (n >= p.N) continue;
-        const uint32_t rr = __ldcg(reinterpret_cast<const unsigned int*>(p.resid + (size_t)m * p.ldr + n));
-        const float h0 = round_bf16(round_bf16(red[m * PSTR + n2 * 2]) + bf16_lo(rr));
-        const float h1 = round_bf16(round_bf16(red[m * PSTR + n2 * 2 + 1]) + bf16_hi(rr));
-        *reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n) = pack_bf16x2(h0, h1);
-        ss += h0 * h0 + h1 * h1;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0 && p.ssq_out != nullptr) p.ssq_out[ntile * p.ssq_stride + m] = ss;
-    }
-  } else if constexpr (EPI == EPI_SWIGLU) {
-    // tile rows: pairs of (32 gate rows, 32 up rows); act column = pair*32 + j
-    constexpr int PAIRS = TN / 64;
-    for (int idx = threadIdx.x; idx < nmine * PAIRS * 32; idx += NTHR) {
-      const int mi = idx / (PAIRS * 32), rem = idx - mi * (PAIRS * 32);
-      const int pr = rem >> 5, j = rem & 31;
-      const int m = rank + mi * cs;
-      const int a = (ntile * PAIRS + pr) * 32 + j;
-      if (a >= p.n_act) continue;
-      const float g = round_bf16(red[m * PSTR + pr * 64 + j]);
-      const float u = round_bf16(red[m * PSTR + pr * 64 + 32 + j]);
-      p.out[(size_t)m * p.ldo + a] = __float2bfloat16_rn(silu_mul(g, u));
-    }
-  } else if constexpr (EPI == EPI_QKROPE) {
-    // tile = TN/128 heads of 128; columns [q heads | k heads | v heads]
-    constexpr int HPT = TN / 128;
-    for (int u = warp; u < nmine * HPT; u += NW + 1) {
-      const int mi = u / HPT, t = u - mi * HPT;
-      const int m = rank + mi * cs;
-      const int hh = n0 / 128 + t;
-      float v[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) v[i] = round_bf16(red[m * PSTR + t * 128 + lane + 32 * i]);
-      const int pos = p.row_pos[m];
-      const int64_t kvo = p.row_kv != nullptr ? p.row_kv[m] : 0;
-      if (hh >= p.hq && (pos < 0 || pos >= p.kv_cap)) {  // never write past a cache slot
-        if (lane == 0) report_error(p.status, 0x301);
-        continue;
-      }
-      if (hh < p.hq + p.hk) {
-        const bool isq = hh < p.hq;
-        const bf16* nw = isq ? p.qnorm : p.knorm;
-        float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float r = rsqrtf(ss / 128.0f + p.eps);
-        float y[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) y[i] = round_bf16(v[i] * r * bf2f(nw[lane + 32 * i]));
-        // rotate-half RoPE: pairs (d, d+64) for d = lane, lane+32
-        float o[4];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const float f = p.inv_freq[lane + 32 * i];
-          float sn, c;
-          sincosf(float(pos) * f, &sn, &c);
-          o[i] = y[i] * c - y[i + 2] * sn;
-          o[i + 2] = y[i] * sn + y[i + 2] * c;
-        }
-        if (isq) {
-          bf16* dst = p.qout + (size_t)m * p.ldq + hh * 128;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(o[i]);
-        } else {
-          bf16* dst = p.kcache + kvo + (int64_t)(hh - p.hq) * p.k_sh + (int64_t)pos * p.k_ss;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(o[i]);
-        }
-      } else if (hh < p.hq + 2 * p.hk) {
-        bf16* dst = p.vcache + kvo + (int64_t)(hh - p.hq - p.hk) * p.v_sh + (int64_t)pos * p.v_ss;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(v[i]);
-      }
-    }
-  }
+  epilogue<EPI, TN, PSTR>(p, red, rank, cs, ntile, n0, NW + 1);
 }
 
 // ----------------------------------------------------------------------------- host side
@@ -594,6 +497,26 @@ static bool get_tmap(CUtensorMap* out, CUtensorMapDataType dt, const void* base,
   return true;
 }
 
+bool tma_maps(const QmmParams& p, int tn, bool sct, CUtensorMap* wmap, CUtensorMap* smap,
+              CUtensorMap* bmap) {
+  const uint64_t words = (uint64_t)p.K * p.bits / 32;
+  if (!get_tmap(wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.wq, words, p.N, words * 4, 32, tn,
+                CU_TENSOR_MAP_SWIZZLE_128B))
+    return false;
+  if (sct) {
+    if (!get_tmap(smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, p.scales, p.G, p.N, (uint64_t)p.G * 2, 8,
+                  tn, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return false;
+    if (!get_tmap(bmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, p.biases, p.G, p.N, (uint64_t)p.G * 2, 8,
+                  tn, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return false;
+  } else {
+    *smap = *wmap;
+    *bmap = *wmap;
+  }
+  return true;
+}
+
 template <int BITS, int RT, int NW, int EPI, bool SCT>
 static int launch_one(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream) {
   auto kern = qmm_kernel<BITS, RT, NW, EPI, SCT>;
@@ -612,21 +535,7 @@ static int launch_one(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream
     configured_smem = L.total;
   }
   CUtensorMap wmap, smap, bmap;
-  const uint64_t words = (uint64_t)p.K * BITS / 32;
-  if (!get_tmap(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.wq, words, p.N, words * 4, 32, TN,
-                CU_TENSOR_MAP_SWIZZLE_128B))
-    return DSPARK_ERR_CUDA;
-  if (SCT) {
-    if (!get_tmap(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, p.scales, p.G, p.N, (uint64_t)p.G * 2,
-                  8, TN, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return DSPARK_ERR_CUDA;
-    if (!get_tmap(&bmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, p.biases, p.G, p.N, (uint64_t)p.G * 2,
-                  8, TN, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return DSPARK_ERR_CUDA;
-  } else {
-    smap = wmap;
-    bmap = wmap;
-  }
+  if (!tma_maps(p, TN, SCT, &wmap, &smap, &bmap)) return DSPARK_ERR_CUDA;
   dim3 grid(pl.cs, (p.N + TN - 1) / TN);
   dim3 block((NW + 1) * 32);
   DSPARK_CUDA_TRY(launch_ex(kern, grid, block, (size_t)L.total, stream, pl.cs, true, wmap, smap, bmap, p),
@@ -663,8 +572,62 @@ static int dispatch_rt(const QmmParams& p, const QmmPlan& pl, cudaStream_t s) {
 // columns), split-K factor (cluster size) and ring depth. Modelled per SM as: the bytes its
 // CTAs stream (load balance over SMs), a fixed per-CTA latency (x staging, first TMA bytes,
 // split-K reduction), and a penalty for shallow pipelines.
+static QmmPlan plan_mma(int N, int K, int bits, int epi, int min_tn, int rt);
+
+static bool use_tc() {
+  const char* v = std::getenv("DSPARK_QMM_IMPL");
+  return !(v != nullptr && std::string(v) == "mma");
+}
+
 QmmPlan plan(int N, int K, int bits, int epi, int min_tn, int rt) {
+  if (use_tc()) return plan_tc(N, K, bits, rt);
+  return plan_mma(N, K, bits, epi, min_tn, rt);
+}
+
+// tcgen05 engine: tile 128 rows; choose the split-K factor (cluster size) and ring depth.
+QmmPlan plan_tc(int N, int K, int bits, int rt) {
   QmmPlan pl;
+  pl.engine = 1;
+  pl.nw = 8;  // 128-row tile
+  pl.rt = rt;
+  pl.sct = (K % 512 == 0);
+  const int sms = sm_count(current_device());
+  const int force_cs = env_int("DSPARK_QMM_CS", 0);
+  const int max_slots = std::max(1, env_int("DSPARK_QMM_SLOTS", 4));
+  const double bw_sm = 6.5e12 / sms;
+  const double t_fix = 2.5e-6;
+  const int ntiles = (N + 127) / 128;
+  double best = 1e30;
+  for (int cs = 1; cs <= 16; ++cs) {
+    if (force_cs && cs != force_cs) continue;
+    if (cs > 8 && cs != 16) continue;
+    const int kslice = ((K + cs - 1) / cs + KSTG - 1) / KSTG * KSTG;
+    if ((cs - 1) * kslice >= K) continue;
+    const int nst = (kslice + KSTG - 1) / KSTG;
+    int slots = std::min(nst, max_slots);
+    while (slots > 1 && tc_smem_bytes(bits, rt, kslice, slots) > kSmemBudget) --slots;
+    if (tc_smem_bytes(bits, rt, kslice, slots) > kSmemBudget) continue;
+    const int ctas = cs * ntiles;
+    const double wbytes = 128.0 * kslice * bits / 8.0;
+    const double per_sm = std::ceil(double(ctas) / sms);
+    double t = per_sm * wbytes / bw_sm + per_sm * t_fix;
+    if (slots < std::min(nst, 3)) t *= 1.0 + 0.25 * (std::min(nst, 3) - slots);
+    if (cs & (cs - 1)) t *= 1.15;  // clusters of 3/5/6 schedule poorly
+    t *= 1.0 + 0.01 * (cs - 1);
+    if (t < best) {
+      best = t;
+      pl.cs = cs;
+      pl.kslice = kslice;
+      pl.nslots = slots;
+    }
+  }
+  if (best >= 1e30) pl.nw = 0;
+  return pl;
+}
+
+static QmmPlan plan_mma(int N, int K, int bits, int epi, int min_tn, int rt) {
+  QmmPlan pl;
+  pl.engine = 0;
   const int sms = sm_count(current_device());
   pl.sct = (K % 512 == 0);
   int nw_choices[3] = {2, 4, 8};
@@ -737,6 +700,7 @@ int run(const QmmParams& p_in, int epi, const QmmPlan* plan_in, cudaStream_t str
   p.kslice = pl.kslice;
   p.cs = pl.cs;
   p.nslots = pl.nslots;
+  if (pl.engine == 1) return run_tc(p, epi, pl, stream);
   if (p.bits == 4) {
     switch (epi) {
       case EPI_PLAIN: return dispatch_rt<4, EPI_PLAIN>(p, pl, stream);

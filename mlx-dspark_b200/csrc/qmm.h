@@ -1,6 +1,7 @@
 // Internal interface of the small-M quantized matmul (K1); the C ABI is in include/dspark.h.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -57,7 +58,17 @@ struct QmmPlan {
   int nslots = 1;   // pipeline depth
   bool sct = true;  // scales/biases by TMA (needs K % 512 == 0)
   int rt = 2;       // row class the plan was made for (serves M <= 8 * rt)
+  int engine = 1;   // 1: tcgen05 (TMEM operands, qmm_tc.cu); 0: mma.sync (qmm.cu)
 };
+
+// TMA descriptors of the packed weights (128-byte swizzle, boxes of 32 words x tn rows) and,
+// when sct, of the scales / biases (boxes of 8 groups x tn rows).
+bool tma_maps(const QmmParams& p, int tn, bool sct, CUtensorMap* wmap, CUtensorMap* smap,
+              CUtensorMap* bmap);
+// tcgen05 engine: geometry and launch (tile 128 rows).
+QmmPlan plan_tc(int N, int K, int bits, int rt);
+int run_tc(const QmmParams& p, int epi, const QmmPlan& pl, cudaStream_t s);
+int tc_smem_bytes(int bits, int rt, int kslice, int nslots);
 
 // Geometry for [N, K] at `bits` serving up to 8*rt rows (rt = 2: M <= 16, rt = 4: M <= 32).
 // It depends on the weight shape and the row class only, so within a class a row's result

@@ -363,13 +363,16 @@ def qlinear(x_f32, w) -> np.ndarray:
 
 
 def verify_forward(weights: dict, cfg: dict, ids, kcache: list, vcache: list, L0: int,
-                   trace: list | None = None):
+                   trace: list | None = None, round_p: bool = False):
     """Qwen3 dense verify forward over one block (Target.verify -> _body_mlxlm + head,
     src/mlx_dspark/target.py:642, :208-221; mlx-lm's qwen3 decoder layer):
     h = embed(ids); per layer: r = attn(rmsnorm(h)); h = h + r; r = mlp(rmsnorm(h));
     h = h + r; logits = lm_head(rmsnorm(h)). Attention: q/k RMSNorm per head, RoPE at
     positions L0 + i, K/V appended to the cache at L0, causal verify attention over
     L0 + M keys. Every op output is rounded to bf16 as MLX's bf16 dataflow does.
+    ``round_p`` rounds the attention probabilities to bf16 before P.V (the fused Metal
+    kernels' dataflow) instead of keeping them in fp32: the two are equally valid bf16
+    dataflows, and the spread between them is the noise floor a GPU forward is judged by.
 
     weights: numpy arrays from the device model (separate q/k/v/gate/up matrices);
     kcache / vcache: per-layer float32 arrays [Hk, cap, D] (modified in place).
@@ -393,7 +396,7 @@ def verify_forward(weights: dict, cfg: dict, ids, kcache: list, vcache: list, L0
         kcache[li][:, L0:L] = k
         vcache[li][:, L0:L] = v.transpose(1, 0, 2)
         o = sdpa(to_bf16(q)[None], to_bf16(kcache[li][:, :L])[None],
-                 to_bf16(vcache[li][:, :L])[None], D ** -0.5, True)[0]
+                 to_bf16(vcache[li][:, :L])[None], D ** -0.5, True, round_p=round_p)[0]
         o = round_bf16(o).transpose(1, 0, 2).reshape(M, Hq * D)
         h = round_bf16(h + qlinear(o, lw["o"]))
         if trace is not None:

@@ -2,10 +2,13 @@
 the Qwen3 dense forward (Target.verify -> _body_mlxlm + head, src/mlx_dspark/target.py:642,
 :208-221).
 
-Bars: logits relative error ||gpu - ref||_2 / ||ref||_2 <= 1e-2 against the oracle's bf16
-logits (a bf16 dataflow differs from any other bf16 dataflow by rounding flips of ~1 ulp
-that propagate layer to layer, so the whole-forward bar is stated on the L2 norm; every
-single op is held to max-abs 1e-2 in its own test); greedy argmax identical on every row
+Bars: logits relative error ||gpu - ref||_2 / ||ref||_2 <= max(1e-2, 1.5 * spread) against
+the oracle's bf16 logits, where spread is the same norm between the oracle's two equally
+valid bf16 dataflows on the same inputs (attention probabilities kept in fp32 vs rounded to
+bf16 before P.V). A bf16 dataflow differs from any other by rounding flips of ~1 ulp that
+propagate layer to layer; on these random-init models that floor is itself ~1e-2, so the
+bar is stated relative to it (every single op is held to max-abs 1e-2 in its own test);
+greedy argmax identical on every row
 whose oracle top-2 margin exceeds twice the observed max logit error (near-ties are
 reported, the reference's "fp-tie class", src/mlx_dspark/small_m_qmm.py:24-28); cache rows
 written by the forward within 2e-2 * max|row| of the oracle's; accept + rollback lengths
@@ -34,10 +37,17 @@ def _prefill(target, L0, seed=0):
     return kc, vc
 
 
-def _compare(oracle, got, ref):
+def _rel(a, b):
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def _compare(oracle, got, ref, ref_p=None):
     ref = oracle.round_bf16(ref)
-    rel = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
-    assert rel <= 1e-2, rel
+    bar = 1e-2
+    if ref_p is not None:
+        bar = max(bar, 1.5 * _rel(oracle.round_bf16(ref_p), ref))
+    rel = _rel(got, ref)
+    assert rel <= bar, (rel, bar)
     err = float(np.abs(got - ref).max())
     tt_ref = oracle.argmax_first(ref)
     tt_got = oracle.argmax_first(got)
@@ -60,9 +70,11 @@ def test_verify_forward_matches_oracle(cuda, oracle, bits, R, L0):
     lens = torch.tensor([L0], dtype=torch.int32, device=cuda)
     logits = t.verify(ids, lens).float().cpu().numpy()
     assert int(lens[0]) == L0 + R
-    ref = oracle.verify_forward(t.oracle_weights(), t.oracle_config(), ids.cpu().numpy(),
-                                kc, vc, L0)
-    _compare(oracle, logits, ref)
+    ow, oc = t.oracle_weights(), t.oracle_config()
+    ref_p = oracle.verify_forward(ow, oc, ids.cpu().numpy(), [c.copy() for c in kc],
+                                  [c.copy() for c in vc], L0, round_p=True)
+    ref = oracle.verify_forward(ow, oc, ids.cpu().numpy(), kc, vc, L0)
+    _compare(oracle, logits, ref, ref_p)
     # the block's K/V rows landed in the cache (q/k-norm + RoPE applied to K)
     for li, L in enumerate(t.layers):
         for name, ref_c in (("k_cache", kc[li]), ("v_cache", vc[li])):
