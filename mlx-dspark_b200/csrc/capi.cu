@@ -484,7 +484,7 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf, 
       p.resid = h; p.ldr = H; p.out = h; p.ldo = H;
       p.ssq_out = buf->ssq_b; p.ssq_stride = kSsqStride;
       qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_RESID, R);
-      ssq_n_b = (p.N + 16 * pl.nw - 1) / (16 * pl.nw);
+      ssq_n_b = pl.nw > 0 ? (p.N + 16 * pl.nw - 1) / (16 * pl.nw) : 0;  // run() rejects nw == 0
       DSPARK_TRY(qmm::run(p, qmm::EPI_RESID, &pl, s));
     }
     // gate/up projection + post-attention RMSNorm + SwiGLU
@@ -510,7 +510,7 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf, 
       p.resid = h; p.ldr = H; p.out = h; p.ldo = H;
       p.ssq_out = buf->ssq_a; p.ssq_stride = kSsqStride;
       qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_RESID, R);
-      ssq_n = (p.N + 16 * pl.nw - 1) / (16 * pl.nw);
+      ssq_n = pl.nw > 0 ? (p.N + 16 * pl.nw - 1) / (16 * pl.nw) : 0;  // run() rejects nw == 0
       ssq_cur = buf->ssq_a;
       DSPARK_TRY(qmm::run(p, qmm::EPI_RESID, &pl, s));
     }

@@ -27,6 +27,8 @@ enum DeviceError : int {
   kErrWaitKV = 0x103,        // attention consumer gave up waiting for a K/V tile
   kErrWaitKVEmpty = 0x104,   // attention producer gave up waiting for a free K/V slot
   kErrWaitPeer = 0x105,      // a cross-GPU flag wait ran out of time
+  kErrWaitCluster = 0x106,   // a CTA gave up waiting for its cluster peers' partial sums
+  kErrWaitMma = 0x107,       // a tensor-core completion wait ran out of time
 };
 
 // ~2 s: far beyond any legitimate wait inside one kernel launch.
@@ -179,6 +181,48 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
+}
+
+__device__ __forceinline__ void fence_acq_rel_cluster() {
+  asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+
+// Arrive (release, cluster scope) on the mbarrier at the same shared-memory offset as `bar`
+// in CTA `rank` of this cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint64_t* bar, uint32_t rank) {
+  const uint32_t remote = mapa_shared(smem_u32(bar), rank);
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait with cluster-scope acquire: for phases completed by arrivals of peer CTAs, whose
+// writes to their own shared memory are read afterwards through distributed shared memory.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status,
+                                                  int code) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait_cluster(a, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait_cluster(a, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      report_error(status, code);
+      return false;
+    }
+  }
 }
 
 // ------------------------------------------------------------------ shared-memory vector loads

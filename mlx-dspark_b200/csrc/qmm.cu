@@ -580,48 +580,60 @@ static bool use_tc() {
 }
 
 QmmPlan plan(int N, int K, int bits, int epi, int min_tn, int rt) {
-  if (use_tc()) return plan_tc(N, K, bits, rt);
+  if (use_tc()) {
+    // shapes whose 32-row x slice and ring do not fit the tcgen05 engine's shared memory
+    // run on the mma.sync engine (the same contract, both hand-written CUDA)
+    const QmmPlan pl = plan_tc(N, K, bits, rt);
+    if (pl.nw > 0) return pl;
+  }
   return plan_mma(N, K, bits, epi, min_tn, rt);
 }
 
-// tcgen05 engine: tile 128 rows; choose the split-K factor (cluster size) and ring depth.
+// tcgen05 engine (persistent clusters): choose the split-K factor cs (= cluster size), the ring
+// depth and the number of clusters. Modelled as: every cluster walks ceil(tiles / clusters)
+// tiles, each CTA streaming 128 rows x K/cs of weights (+ scales/biases) at the smaller of a
+// per-SM streaming cap and its share of HBM bandwidth, plus a once-per-CTA start (x staging,
+// ring fill) and a small per-tile cost (split-K exchange, epilogue).
 QmmPlan plan_tc(int N, int K, int bits, int rt) {
   QmmPlan pl;
   pl.engine = 1;
-  pl.nw = 8;  // 128-row tile
+  pl.nw = 0;
   pl.rt = rt;
   pl.sct = (K % 512 == 0);
-  const int sms = sm_count(current_device());
   const int force_cs = env_int("DSPARK_QMM_CS", 0);
-  const int max_slots = std::max(1, env_int("DSPARK_QMM_SLOTS", 4));
-  const double bw_sm = 6.5e12 / sms;
-  const double t_fix = 2.5e-6;
+  const int max_slots = std::max(2, env_int("DSPARK_QMM_SLOTS", 8));
+  const int force_clusters = env_int("DSPARK_QMM_CLUSTERS", 0);
+  const double hbm = 6.5e12, sm_cap = 1.2e11;
   const int ntiles = (N + 127) / 128;
   double best = 1e30;
-  for (int cs = 1; cs <= 16; ++cs) {
+  for (int cs : {1, 2, 3, 4, 5, 6, 8, 10, 12, 16}) {
     if (force_cs && cs != force_cs) continue;
-    if (cs > 8 && cs != 16) continue;
     const int kslice = ((K + cs - 1) / cs + KSTG - 1) / KSTG * KSTG;
     if ((cs - 1) * kslice >= K) continue;
-    const int nst = (kslice + KSTG - 1) / KSTG;
-    int slots = std::min(nst, max_slots);
-    while (slots > 1 && tc_smem_bytes(bits, rt, kslice, slots) > kSmemBudget) --slots;
-    if (tc_smem_bytes(bits, rt, kslice, slots) > kSmemBudget) continue;
-    const int ctas = cs * ntiles;
-    const double wbytes = 128.0 * kslice * bits / 8.0;
-    const double per_sm = std::ceil(double(ctas) / sms);
-    double t = per_sm * wbytes / bw_sm + per_sm * t_fix;
-    if (slots < std::min(nst, 3)) t *= 1.0 + 0.25 * (std::min(nst, 3) - slots);
-    if (cs & (cs - 1)) t *= 1.15;  // clusters of 3/5/6 schedule poorly
-    t *= 1.0 + 0.01 * (cs - 1);
+    // the split depends on the shape and the row class only, so within a class a row's result
+    // never depends on how many rows ride with it
+    const int slots = std::min(max_slots, (kSmemBudget - tc_smem_bytes(bits, rt, kslice, 0)) /
+                                              tc_stage_bytes(bits));
+    if (slots < 2) continue;
+    const int smem = tc_planned_smem(bits, rt, kslice, slots);
+    int clusters = std::min(ntiles, tc_max_clusters(bits, rt, cs, smem));
+    if (force_clusters > 0) clusters = std::min(ntiles, force_clusters);
+    if (clusters < 1) continue;
+    const int waves = (ntiles + clusters - 1) / clusters;
+    const double tile_bytes = 128.0 * kslice * (bits / 8.0 + 4.0 / 64.0);
+    const double rate = std::min(sm_cap, hbm / (clusters * cs));
+    double t = waves * (tile_bytes / rate + 0.3e-6) + 1.5e-6 + kslice * 32.0 / 2e11;
+    if (slots < 3) t *= 1.15;
+    if (cs & (cs - 1)) t *= 1.05;  // odd cluster shapes pack less evenly into GPCs
     if (t < best) {
       best = t;
+      pl.nw = 8;  // 128-row tile
       pl.cs = cs;
       pl.kslice = kslice;
       pl.nslots = slots;
+      pl.clusters = clusters;
     }
   }
-  if (best >= 1e30) pl.nw = 0;
   return pl;
 }
 

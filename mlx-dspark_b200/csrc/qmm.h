@@ -59,6 +59,7 @@ struct QmmPlan {
   bool sct = true;  // scales/biases by TMA (needs K % 512 == 0)
   int rt = 2;       // row class the plan was made for (serves M <= 8 * rt)
   int engine = 1;   // 1: tcgen05 (TMEM operands, qmm_tc.cu); 0: mma.sync (qmm.cu)
+  int clusters = 0; // tcgen05: persistent clusters walking the tiles (0: one per cs SMs)
 };
 
 // TMA descriptors of the packed weights (128-byte swizzle, boxes of 32 words x tn rows) and,
@@ -68,7 +69,10 @@ bool tma_maps(const QmmParams& p, int tn, bool sct, CUtensorMap* wmap, CUtensorM
 // tcgen05 engine: geometry and launch (tile 128 rows).
 QmmPlan plan_tc(int N, int K, int bits, int rt);
 int run_tc(const QmmParams& p, int epi, const QmmPlan& pl, cudaStream_t s);
-int tc_smem_bytes(int bits, int rt, int kslice, int nslots);
+int tc_smem_bytes(int bits, int rt, int kslice, int nslots);  // layout incl. nslots stages
+int tc_stage_bytes(int bits);                                  // one ring stage
+int tc_planned_smem(int bits, int rt, int kslice, int nslots); // what a launch requests
+int tc_max_clusters(int bits, int rt, int cs, int smem);       // co-resident clusters
 
 // Geometry for [N, K] at `bits` serving up to 8*rt rows (rt = 2: M <= 16, rt = 4: M <= 32).
 // It depends on the weight shape and the row class only, so within a class a row's result

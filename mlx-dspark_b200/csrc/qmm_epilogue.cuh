@@ -11,14 +11,16 @@ namespace qmm {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
 
+// Run by `nwarps` warps starting at warp `warp0` of the CTA.
 template <int EPI, int TN, int PSTR>
 __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, int rank, int cs,
-                                         int ntile, int n0, int nwarps) {
+                                         int ntile, int n0, int nwarps, int warp0 = 0) {
   const int nthr = nwarps * 32;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tidx = int(threadIdx.x) - warp0 * 32;
+  const int warp = tidx >> 5, lane = tidx & 31;
   const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;  // rows m = rank + i*cs
   if constexpr (EPI == EPI_PLAIN) {
-    for (int idx = threadIdx.x; idx < nmine * (TN / 2); idx += nthr) {
+    for (int idx = tidx; idx < nmine * (TN / 2); idx += nthr) {
       const int mi = idx / (TN / 2), n2 = idx - mi * (TN / 2);
       const int m = rank + mi * cs;
       const int n = n0 + n2 * 2;
@@ -53,7 +55,7 @@ __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, i
   } else if constexpr (EPI == EPI_SWIGLU) {
     // tile rows: pairs of (32 gate rows, 32 up rows); act column = pair*32 + j
     constexpr int PAIRS = TN / 64;
-    for (int idx = threadIdx.x; idx < nmine * PAIRS * 32; idx += nthr) {
+    for (int idx = tidx; idx < nmine * PAIRS * 32; idx += nthr) {
       const int mi = idx / (PAIRS * 32), rem = idx - mi * (PAIRS * 32);
       const int pr = rem >> 5, j = rem & 31;
       const int m = rank + mi * cs;

@@ -2,24 +2,34 @@
 // (sm_100a). Same contract and numerics as qmm.cu (y[M,N] = x[M,K] . dequant(W)^T, MLX affine
 // 4/8-bit group 64, fp32 accumulation, per-group scale/bias fold), different engine:
 //
-//  * A CTA owns 128 weight rows (tile) x one split-K slice. A producer warp streams the packed
-//    weights and their scales/biases through a shared-memory ring with TMA (as in qmm.cu).
+//  * Persistent clusters. The grid is (cs, P): cs CTAs per cluster split K into cs slices, and
+//    P clusters (as many as fit on the GPU at once, never more than there are tiles) walk the
+//    128-row output tiles t = cluster, cluster + P, ... Each CTA stages its K-slice of x once
+//    and keeps it for every tile it visits; its producer warp streams the packed weights and
+//    their scales/biases through a shared-memory ring with TMA without a break between tiles.
 //  * Two consumer warpgroups alternate quantization groups. Thread t of a warpgroup owns weight
 //    row t: it dequantizes its row's 64 weights of the group in registers with the bf16
 //    magic-exponent trick (nibble | 0x4300 = 128 + q, exact) and writes them to tensor memory
 //    with tcgen05.st — the MMA's A operand lives in TMEM (lane = row, two bf16 per column).
-//  * x (the B operand, 16 or 32 rows) is staged once per CTA in shared memory in the UMMA
-//    canonical K-major no-swizzle layout (8-row x 16-byte core matrices), with k permuted inside
-//    each 8-block exactly as the magic extraction orders the weights.
+//  * x (the B operand, 16 or 32 rows) sits in shared memory in the UMMA canonical K-major
+//    no-swizzle layout (8-row x 16-byte core matrices), with k permuted inside each 8-block
+//    exactly as the magic extraction orders the weights.
 //  * One thread per warpgroup issues tcgen05.mma (M=128, N=16|32, K=16) into a per-group fp32
 //    accumulator in TMEM and commits to an mbarrier; the warpgroup reads the group's product P
 //    back with tcgen05.ld and folds acc += scale*P + (bias - MAGIC*scale)*sum_k x in registers
 //    while the tensor core works on the next group (accumulators double-buffered in TMEM).
 //  * 8-bit weights are two exact 4-bit planes (lo: 128+lo, hi: 256+16*hi), two MMAs per k16.
-//  * Split-K across a thread-block cluster, reduced through distributed shared memory in fixed
-//    rank order; epilogues shared with qmm.cu.
-// Every mbarrier wait is time-bounded; TMEM is always released before the CTA exits.
+//  * Split-K partial tiles are exchanged through distributed shared memory: each CTA publishes
+//    its partial tile (double-buffered) and signals every peer's "ready" mbarrier; each CTA
+//    sums its rows m = rank + i*cs over the cs partials in fixed rank order, signals "free",
+//    and runs the shared epilogue on them.
+// Every mbarrier wait is time-bounded (a failed wait records an error and the kernel drains
+// without further waits on other agents); TMEM is always released before the CTA exits.
 #include <algorithm>
+#include <cmath>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "common.cuh"
 #include "host_common.h"
@@ -31,12 +41,19 @@ namespace qmm {
 
 namespace tc {
 
-constexpr int TN = 128;          // weight rows per CTA (= MMA M)
+constexpr int TN = 128;          // weight rows per tile (= MMA M)
 constexpr int KSTG = 512;        // k per pipeline stage
 constexpr int GPS = KSTG / 64;   // groups per stage
-constexpr int NWG = 2;           // consumer warpgroups
-constexpr int NTHR = NWG * 128 + 32;
+constexpr int NWG = 2;           // dequantizing warpgroups (and as many folding warpgroups)
+constexpr int NX = 2 * NWG * 128;  // dequant + fold threads (they stage x together)
+constexpr int NF = NWG * 128;      // fold threads (tile end: split-K exchange, epilogue)
+constexpr int WARP_FOLD = NWG * 4;     // first fold warp
+constexpr int WARP_MMA = 2 * NWG * 4;  // the warp that issues the tensor-core MMAs
+constexpr int WARP_TMA = WARP_MMA + 1; // the producer warp
+constexpr int NTHR = (WARP_TMA + 1) * 32;
 constexpr int PSTR = TN + 4;
+constexpr int MAXA = 4;          // A buffers per warpgroup, at most
+constexpr int MAXD = 8;          // D buffers per warpgroup, at most
 
 template <int BITS>
 struct Tr;
@@ -53,9 +70,23 @@ struct Tr<8> {
   static constexpr int ACOLS = 64;    // low plane 32 + high plane 32
 };
 
+// Per warpgroup: A buffers (one group of dequantized weights each; the tensor core frees them
+// within a few hundred cycles) and D buffers (one group's fp32 product each; the fold warps free
+// them, and they must ride out the fold's work at the end of a tile), in half of TMEM.
+__host__ __device__ constexpr int nabuf(int bits) { return bits == 4 ? 4 : 2; }
+__host__ __device__ constexpr int ndbuf(int bits, int nm) {
+  return (256 - nabuf(bits) * (bits == 4 ? 32 : 64)) / nm < MAXD
+             ? (256 - nabuf(bits) * (bits == 4 ? 32 : 64)) / nm
+             : MAXD;
+}
+
 struct Layout {
   int ring, scs, bis, xs, sx, part, red, rs, bars, tmem, total;
 };
+
+__host__ __device__ inline int stage_bytes(int bits) {
+  return (bits == 4 ? Tr<4>::SB : Tr<8>::SB) * TN * 128 + 2 * TN * 16;
+}
 
 __host__ __device__ inline Layout layout(int bits, int rt, int kslice, int nslots) {
   const int sb = bits == 4 ? Tr<4>::SB : Tr<8>::SB;
@@ -73,30 +104,22 @@ __host__ __device__ inline Layout layout(int bits, int rt, int kslice, int nslot
   L.sx = off;
   off += (kslice / 64) * rp * 4;
   off = (off + 15) & ~15;
-  L.part = off;
-  off += rp * PSTR * 4;
+  L.part = off;                 // two partial-tile buffers
+  off += 2 * rp * PSTR * 4;
   L.red = off;
   off += rp * PSTR * 4;
   L.rs = off;
   off += 32 * 4;
   off = (off + 15) & ~15;
   L.bars = off;
-  off += (2 * nslots + 2 * NWG) * 8;
+  off += (2 * nslots + 2 * NWG * (MAXA + MAXD) + 4) * 8;
   L.tmem = off;
   off += 16;
   L.total = off + 1024;
   return L;
 }
 
-__host__ __device__ inline int tmem_cols(int bits, int rt) {
-  const int acols = bits == 4 ? Tr<4>::ACOLS : Tr<8>::ACOLS;
-  const int nm = rt <= 2 ? 16 : 32;
-  const int per_wg = 2 * acols + 2 * nm;
-  const int need = NWG * per_wg;
-  int c = 32;
-  while (c < need) c <<= 1;
-  return c;
-}
+constexpr int kTmemCols = 512;  // every configuration allocates all of it (one CTA per SM)
 
 // ------------------------------------------------------------------ tcgen05 helpers
 
@@ -124,6 +147,18 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+      "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
 
@@ -176,7 +211,30 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(128 >> 4) << 24);
 }
 
+__device__ __forceinline__ bool elect_one() {
+  uint32_t p = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(p));
+  return p != 0;
+}
+
 // ------------------------------------------------------------------ kernel
+//
+// Warp roles (one CTA per SM, 576 threads):
+//   warps 0..7   two dequantizing warpgroups: warpgroup w takes the groups gi = w, w+2, ...
+//                of every stage and writes them to its A buffers in TMEM
+//   warps 8..15  two folding warpgroups: warpgroup w reads the products of warpgroup w's
+//                groups from its D buffers and folds them into per-row accumulators. A tile's
+//                split-K exchange and epilogue are finished one tile later (after the next
+//                tile's groups), when the cluster peers have long published their partials
+//   warp 16      issues the MMAs (warp-uniform, one elected lane) and commits them
+//   warp 17      the TMA producer
+// Per warpgroup w, group i of that warpgroup uses A buffer i % NA and D buffer i % ND:
+//   afull[w][a]   4 dequant warps -> MMA warp   (A written)
+//   adone[w][a]   tcgen05.commit  -> dequant    (A free again)
+//   dfull[w][d]   tcgen05.commit  -> fold       (D ready)
+//   dempty[w][d]  4 fold warps    -> MMA warp   (D read)
 
 template <int BITS, int RT, int EPI, bool SCT>
 __global__ void __launch_bounds__(NTHR, 1)
@@ -191,6 +249,10 @@ __global__ void __launch_bounds__(NTHR, 1)
   constexpr int ACOLS = Tr<BITS>::ACOLS;
   constexpr float MAGIC = Tr<BITS>::MAGIC;
   constexpr uint32_t IDESC = idesc_bf16(NM);
+  constexpr int NA = nabuf(BITS);
+  constexpr int ND = ndbuf(BITS, NM);
+  constexpr int PER = NA * ACOLS + ND * NM;  // TMEM columns per warpgroup
+  static_assert(NWG * PER <= kTmemCols && ND >= 2, "TMEM budget");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -207,38 +269,57 @@ __global__ void __launch_bounds__(NTHR, 1)
   float* rsm = reinterpret_cast<float*>(smem + Lo.rs);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lo.bars);
   uint64_t* empty = full + S;
-  uint64_t* mmab = empty + S;                // [NWG][2]
+  uint64_t* afull = empty + S;               // [NWG][MAXA]
+  uint64_t* adone = afull + NWG * MAXA;      // [NWG][MAXA]
+  uint64_t* dfull = adone + NWG * MAXA;      // [NWG][MAXD]
+  uint64_t* dempty = dfull + NWG * MAXD;     // [NWG][MAXD]
+  uint64_t* ready = dempty + NWG * MAXD;     // [2] cluster: peers' partial tiles published
+  uint64_t* freeb = ready + 2;               // [2] cluster: peers done reading our partial
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lo.tmem);
 
   const int cs = p.cs;
   const int rank = blockIdx.x;
-  const int ntile = blockIdx.y;
-  const int n0 = ntile * TN;
+  const int ntiles = (p.N + TN - 1) / TN;
+  const int nclus = gridDim.y;
+  const int ntl = int(blockIdx.y) < ntiles ? (ntiles - int(blockIdx.y) + nclus - 1) / nclus : 0;
   const int kbase = rank * p.kslice;
   const int kvalid = min(p.kslice, p.K - kbase);
   const int nst = (kvalid + KSTG - 1) / KSTG;
   const int gslice = p.kslice / 64;
+  const int gfirst = kbase / 64;
+  const int ngroups = (kvalid + 63) / 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
-  constexpr int NC = NWG * 128;
-  const int ncols = tmem_cols(BITS, RT);
+  // groups of stage st: gl = st*GPS + gi for gi < ngs(st) (the last stage of a slice may be short)
+  auto ngs = [&](int st) { return max(0, min(GPS, min(ngroups, p.G - gfirst) - st * GPS)); };
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], NWG * 4);
+      mbar_init(&empty[s], 2 * NWG * 4);
     }
-    for (int i = 0; i < 2 * NWG; ++i) mbar_init(&mmab[i], 1);
+    for (int i = 0; i < NWG * MAXA; ++i) {
+      mbar_init(&afull[i], 4);
+      mbar_init(&adone[i], 1);
+    }
+    for (int i = 0; i < NWG * MAXD; ++i) {
+      mbar_init(&dfull[i], 1);
+      mbar_init(&dempty[i], 4);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ready[i], cs);
+      mbar_init(&freeb[i], cs);
+    }
     fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc(tmem_slot, ncols);
+  if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
-  __syncthreads();
+  if (cs > 1) cluster_sync_all(); else __syncthreads();  // peers' barriers exist before use
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_launch_dependents();
 
-  if (warp == NWG * 4) {
+  if (warp == WARP_TMA) {
     // ------------------------------------------------------------- producer warp
     if (lane == 0) {
       prefetch_tmap(&wmap);
@@ -248,29 +329,74 @@ __global__ void __launch_bounds__(NTHR, 1)
       }
       const uint64_t pol = l2_policy_evict_first();
       const uint32_t bytes = STG + (SCT ? 2 * SCB : 0);
-      for (int st = 0; st < nst; ++st) {
-        const int slot = st % S;
-        if (st >= S) {
-          if (!mbar_wait(&empty[slot], ((st / S) - 1) & 1, p.status, kErrWaitEmpty)) break;
-        }
-        mbar_arrive_expect_tx(&full[slot], bytes);
-        const int kk = kbase + st * KSTG;
-        const int w0 = kk * BITS / 32;
+      bool ok = true;
+      int issued = 0;
+      for (int j = 0; j < ntl && ok; ++j) {
+        const int n0 = (int(blockIdx.y) + j * nclus) * TN;
+        for (int st = 0; st < nst; ++st) {
+          const int g = j * nst + st;
+          const int slot = g % S;
+          if (g >= S && !mbar_wait(&empty[slot], ((g / S) - 1) & 1, p.status, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[slot], bytes);
+          const int kk = kbase + st * KSTG;
+          const int w0 = kk * BITS / 32;
 #pragma unroll
-        for (int b = 0; b < SB; ++b)
-          tma_load_2d(ring + slot * STG + b * BOX, &wmap, &full[slot], w0 + b * 32, n0, pol);
-        if (SCT) {
-          tma_load_2d(scs + slot * SCB, &smap, &full[slot], kk / 64, n0, pol);
-          tma_load_2d(bis + slot * SCB, &bmap, &full[slot], kk / 64, n0, pol);
+          for (int b = 0; b < SB; ++b)
+            tma_load_2d(ring + slot * STG + b * BOX, &wmap, &full[slot], w0 + b * 32, n0, pol);
+          if (SCT) {
+            tma_load_2d(scs + slot * SCB, &smap, &full[slot], kk / 64, n0, pol);
+            tma_load_2d(bis + slot * SCB, &bmap, &full[slot], kk / 64, n0, pol);
+          }
+          ++issued;
+        }
+      }
+      // never leave the CTA with copies in flight: wait (bounded) for the last ones issued
+      for (int g = max(0, issued - S); g < issued; ++g)
+        mbar_wait(&full[g % S], (g / S) & 1, p.status, kErrWaitFull);
+    }
+    __syncwarp();
+  } else if (warp == WARP_MMA) {
+    // ------------------------------------------------------------- MMA warp
+    static_assert(NWG == 2, "the MMA warp interleaves two warpgroups");
+    const uint64_t bd0 = smem_desc(smem_u32(xs), NM * 16, 128);
+    int cnt0 = 0, cnt1 = 0;  // groups issued per warpgroup (scalars: no local-memory array)
+    for (int j = 0; j < ntl; ++j) {
+      for (int st = 0; st < nst; ++st) {
+        const int ng = ngs(st);
+        for (int gi = 0; gi < ng; ++gi) {
+          const int gl = st * GPS + gi;
+          const int w = gi & 1;
+          const int i = w ? cnt1++ : cnt0++;
+          const int a = i % NA, ua = i / NA;
+          const int d = i % ND, ud = i / ND;
+          mbar_wait(&afull[w * MAXA + a], ua & 1, p.status, kErrWaitMma);
+          if (ud > 0) mbar_wait(&dempty[w * MAXD + d], (ud - 1) & 1, p.status, kErrWaitMma);
+          tc_fence_after();
+          const uint32_t ta = tmem + w * PER + a * ACOLS;
+          const uint32_t td = tmem + w * PER + NA * ACOLS + d * NM;
+          // the group's x: 8 blocks of 8 k at (gl*8 + blk) * NM * 16 bytes (descriptor units of 16)
+          const uint64_t bd = bd0 + uint64_t(gl * 8 * NM);
+          if (elect_one()) {
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {  // four k16 steps = 8 TMEM columns of A each
+              umma_ts(td, ta + 8 * s, bd + uint64_t(2 * s * NM), IDESC, s > 0 ? 1u : 0u);
+              if (BITS == 8) umma_ts(td, ta + 32 + 8 * s, bd + uint64_t(2 * s * NM), IDESC, 1u);
+            }
+            umma_commit(&adone[w * MAXA + a]);
+            umma_commit(&dfull[w * MAXD + d]);
+          }
+          __syncwarp();
         }
       }
     }
-    __syncwarp();
   } else {
-    // ------------------------------------------------------------- consumer warpgroups
+    // ------------------------------------------------------------- dequant + fold warpgroups
     pdl_wait();
     if (p.norm_w != nullptr) {
-      for (int m = warp; m < RP; m += NWG * 4) {
+      for (int m = warp; m < RP; m += NX / 32) {
         float ss = 0.f;
         if (m < p.M)
           for (int e = lane; e < p.ssq_n; e += 32) ss += __ldcg(&p.ssq_in[e * p.ssq_stride + m]);
@@ -278,242 +404,282 @@ __global__ void __launch_bounds__(NTHR, 1)
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         if (lane == 0) rsm[m] = m < p.M ? rsqrtf(ss / float(p.K) + p.eps) : 0.f;
       }
-      asm volatile("bar.sync 1, %0;" ::"n"(NC));
+      asm volatile("bar.sync 2, %0;" ::"n"(NX));
     }
-    // stage x in the UMMA K-major canonical layout: block j (8 k) of row m at (j*NM + m)*16,
-    // k order (0,4,1,5,2,6,3,7) for 4-bit, (0,2,1,3) per half-block for 8-bit
-    const int blocks = p.kslice / 8;
-    const int total = NM * blocks;
-    constexpr int XB = 8;
-    const bool nrm = p.norm_w != nullptr;
-    for (int base = tid; base < total; base += NC * XB) {
-      uint4 v[XB], w[XB];
+    // stage x once, in the UMMA K-major canonical layout: block j (8 k) of row m at
+    // (j*NM + m)*16, k order (0,4,1,5,2,6,3,7) for 4-bit, (0,2,1,3) per half-block for 8-bit
+    {
+      const int blocks = p.kslice / 8;
+      const int total = NM * blocks;
+      constexpr int XB = 4;
+      const bool nrm = p.norm_w != nullptr;
+      for (int base = tid; base < total; base += NX * XB) {
+        uint4 v[XB], w[XB];
 #pragma unroll
-      for (int u = 0; u < XB; ++u) {
-        const int idx = base + u * NC;
-        const int j = idx / NM, m = idx - j * NM;
-        v[u] = make_uint4(0u, 0u, 0u, 0u);
-        w[u] = v[u];
-        if (idx < total && m < p.M && j * 8 < kvalid) {
-          const int k = kbase + j * 8;
-          v[u] = __ldcg(reinterpret_cast<const uint4*>(p.x + (size_t)m * p.ldx + k));
-          if (nrm) w[u] = __ldg(reinterpret_cast<const uint4*>(p.norm_w + k));
+        for (int u = 0; u < XB; ++u) {
+          const int idx = base + u * NX;
+          const int j = idx / NM, m = idx - j * NM;
+          v[u] = make_uint4(0u, 0u, 0u, 0u);
+          w[u] = v[u];
+          if (idx < total && m < p.M && j * 8 < kvalid) {
+            const int k = kbase + j * 8;
+            v[u] = __ldcg(reinterpret_cast<const uint4*>(p.x + (size_t)m * p.ldx + k));
+            if (nrm) w[u] = __ldg(reinterpret_cast<const uint4*>(p.norm_w + k));
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < XB; ++u) {
+          const int idx = base + u * NX;
+          if (idx >= total) break;
+          const int j = idx / NM, m = idx - j * NM;
+          uint4 vv = v[u];
+          if (nrm && m < p.M) {
+            const float r = rsm[m];
+            uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
+            const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w[u]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
+                                  bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
+          }
+          uint4 o;
+          if (BITS == 4) {
+            o.x = __byte_perm(vv.x, vv.z, 0x5410);
+            o.y = __byte_perm(vv.x, vv.z, 0x7632);
+            o.z = __byte_perm(vv.y, vv.w, 0x5410);
+            o.w = __byte_perm(vv.y, vv.w, 0x7632);
+          } else {
+            o.x = __byte_perm(vv.x, vv.y, 0x5410);
+            o.y = __byte_perm(vv.x, vv.y, 0x7632);
+            o.z = __byte_perm(vv.z, vv.w, 0x5410);
+            o.w = __byte_perm(vv.z, vv.w, 0x7632);
+          }
+          *reinterpret_cast<uint4*>(xs + (j * NM + m) * 16) = o;
         }
       }
+      asm volatile("bar.sync 2, %0;" ::"n"(NX));
+      for (int idx = tid; idx < RP * gslice; idx += NX) {
+        const int g = idx / RP, m = idx - g * RP;
+        float s = 0.f;
 #pragma unroll
-      for (int u = 0; u < XB; ++u) {
-        const int idx = base + u * NC;
-        if (idx >= total) break;
-        const int j = idx / NM, m = idx - j * NM;
-        uint4 vv = v[u];
-        if (nrm && m < p.M) {
-          const float r = rsm[m];
-          uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
-          const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w[u]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
-                                bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
+        for (int b = 0; b < 8; ++b) {
+          const uint4 q = *reinterpret_cast<const uint4*>(xs + ((g * 8 + b) * NM + m) * 16);
+          s += (bf16_lo(q.x) + bf16_hi(q.x)) + (bf16_lo(q.y) + bf16_hi(q.y)) +
+               (bf16_lo(q.z) + bf16_hi(q.z)) + (bf16_lo(q.w) + bf16_hi(q.w));
         }
-        uint4 o;
-        if (BITS == 4) {
-          o.x = __byte_perm(vv.x, vv.z, 0x5410);
-          o.y = __byte_perm(vv.x, vv.z, 0x7632);
-          o.z = __byte_perm(vv.y, vv.w, 0x5410);
-          o.w = __byte_perm(vv.y, vv.w, 0x7632);
-        } else {
-          o.x = __byte_perm(vv.x, vv.y, 0x5410);
-          o.y = __byte_perm(vv.x, vv.y, 0x7632);
-          o.z = __byte_perm(vv.z, vv.w, 0x5410);
-          o.w = __byte_perm(vv.z, vv.w, 0x7632);
-        }
-        *reinterpret_cast<uint4*>(xs + (j * NM + m) * 16) = o;
+        sx[g * RP + m] = s;
       }
+      fence_proxy_async_smem();  // x becomes the tensor core's B operand (async proxy)
+      asm volatile("bar.sync 2, %0;" ::"n"(NX));
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(NC));
-    for (int idx = tid; idx < RP * gslice; idx += NC) {
-      const int g = idx / RP, m = idx - g * RP;
-      float s = 0.f;
-#pragma unroll
-      for (int b = 0; b < 8; ++b) {
-        const uint4 q = *reinterpret_cast<const uint4*>(xs + ((g * 8 + b) * NM + m) * 16);
-        s += (bf16_lo(q.x) + bf16_hi(q.x)) + (bf16_lo(q.y) + bf16_hi(q.y)) +
-             (bf16_lo(q.z) + bf16_hi(q.z)) + (bf16_lo(q.w) + bf16_hi(q.w));
-      }
-      sx[g * RP + m] = s;
-    }
-    fence_proxy_async_smem();  // x becomes the tensor core's B operand (async proxy)
-    asm volatile("bar.sync 1, %0;" ::"n"(NC));
 
-    const int wg = warp >> 2;                 // warpgroup
     const int row = tid & 127;                // weight row within the tile == TMEM lane
     const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
-    const uint32_t tm_a = tmem + wg * (2 * ACOLS + 2 * NM);   // this warpgroup's A buffers
-    const uint32_t tm_d = tm_a + 2 * ACOLS;                   // and accumulators
-    uint64_t* mb = mmab + wg * 2;
-    const uint32_t xs_a = smem_u32(xs);
     const uint32_t ring_a = smem_u32(ring);
-    const int gfirst = kbase / 64;
-    const int ngroups = (kvalid + 63) / 64;
+    bool ok = true;  // false once a wait on another agent ran out: drain without waiting
 
-    float acc[RP];
-#pragma unroll
-    for (int m = 0; m < RP; ++m) acc[m] = 0.f;
-    float pend_s = 0.f, pend_c = 0.f;  // scale / folded bias of the group in flight
-    int pend_gl = -1, nissued = 0;
-
-    auto fold_pending = [&]() {
-      if (pend_gl < 0) return;
-      const int b = (nissued - 1) & 1;
-      mbar_wait(&mb[b], ((nissued - 1) >> 1) & 1, p.status, kErrWaitFull);
-      tc_fence_after();
-      float d[NM];
-      tmem_ld16(tm_d + b * NM + lane_off, d);
-      if (NM == 32) tmem_ld16(tm_d + b * NM + 16 + lane_off, d + 16);
-      tmem_wait_ld();
-      const float* sxg = sx + pend_gl * RP;
-#pragma unroll
-      for (int m = 0; m < RP; ++m) acc[m] = fmaf(pend_s, d[m], fmaf(pend_c, sxg[m], acc[m]));
-      pend_gl = -1;
-    };
-
-    for (int st = 0; st < nst; ++st) {
-      const int slot = st % S;
-      mbar_wait(&full[slot], (st / S) & 1, p.status, kErrWaitFull);
-      const uint32_t wbase = ring_a + slot * STG;
-      uint4 sc8, bi8;
-      if (SCT) {
-        sc8 = lds128(smem_u32(scs + slot * SCB + row * 16));
-        bi8 = lds128(smem_u32(bis + slot * SCB + row * 16));
-      }
+    if (warp < WARP_FOLD) {
+      // --------------------------------------------------------- dequantizing warpgroup w
+      const int w = warp >> 2;
+      const uint32_t tab = tmem + w * PER + lane_off;
+      int i = 0;
+      for (int j = 0; j < ntl; ++j) {
+        for (int st = 0; st < nst; ++st) {
+          const int g = j * nst + st;
+          const int slot = g % S;
+          if (ok) ok = mbar_wait(&full[slot], (g / S) & 1, p.status, kErrWaitFull);
+          const uint32_t wbase = ring_a + slot * STG;
+          const int ng = ngs(st);
 #pragma unroll 1
-      for (int gi = wg; gi < GPS; gi += NWG) {
-        const int gl = st * GPS + gi;
-        if (gl >= ngroups || gfirst + gl >= p.G) break;
-        // ---- dequantize this row's 64 weights of group gl into the A buffer
-        const int abuf = nissued & 1;
-        const uint32_t ta = tm_a + abuf * ACOLS + lane_off;
-        if (BITS == 4) {
-          const int box = gi >> 2;
-          const int c0 = (gi & 3) * 2;
-          uint4 wv[2];
+          for (int gi = w; gi < ng; gi += NWG, ++i) {
+            const int a = i % NA, ua = i / NA;
+            // A buffer a is free once the MMAs of its previous use completed (the tensor core
+            // always finishes: wait even after a failure)
+            if (ua > 0) mbar_wait(&adone[w * MAXA + a], (ua - 1) & 1, p.status, kErrWaitMma);
+            tc_fence_after();
+            const uint32_t ta = tab + a * ACOLS;
+            if (BITS == 4) {
+              const int box = gi >> 2;
+              const int c0 = (gi & 3) * 2;
+              uint4 wv[2];
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-            wv[h] = lds128(wbase + box * BOX + row * 128 + (((c0 + h) ^ (row & 7)) << 4));
-          const uint32_t wd[8] = {wv[0].x, wv[0].y, wv[0].z, wv[0].w, wv[1].x, wv[1].y, wv[1].z, wv[1].w};
+              for (int h = 0; h < 2; ++h)
+                wv[h] = lds128(wbase + box * BOX + row * 128 + (((c0 + h) ^ (row & 7)) << 4));
+              const uint32_t wd[8] = {wv[0].x, wv[0].y, wv[0].z, wv[0].w,
+                                      wv[1].x, wv[1].y, wv[1].z, wv[1].w};
+              // word 2q+h, nibbles e and e+4 -> column 8q + 4h + e
+              uint32_t r[32];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {  // words 2q, 2q+1 -> columns 8q .. 8q+7
-            uint32_t r[8];
+              for (int q = 0; q < 4; ++q)
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
+                for (int h = 0; h < 2; ++h)
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
-                r[4 * h + i] = lop3_and_or(wd[2 * q + h] >> (4 * i), 0x000F000Fu, 0x43004300u);
-            tmem_st8(ta + 8 * q, r);
-          }
-        } else {
-          const int box = gi >> 1;
-          const int c0 = (gi & 1) * 4;
-          uint4 wv[4];
+                  for (int e = 0; e < 4; ++e)
+                    r[8 * q + 4 * h + e] =
+                        lop3_and_or(wd[2 * q + h] >> (4 * e), 0x000F000Fu, 0x43004300u);
+              tmem_st32(ta, r);
+            } else {
+              const int box = gi >> 1;
+              const int c0 = (gi & 1) * 4;
+              uint4 wv[4];
 #pragma unroll
-          for (int h = 0; h < 4; ++h)
-            wv[h] = lds128(wbase + box * BOX + row * 128 + (((c0 + h) ^ (row & 7)) << 4));
-          const uint32_t* wd = reinterpret_cast<const uint32_t*>(wv);
+              for (int h = 0; h < 4; ++h)
+                wv[h] = lds128(wbase + box * BOX + row * 128 + (((c0 + h) ^ (row & 7)) << 4));
+              const uint32_t* wd = reinterpret_cast<const uint32_t*>(wv);
+              // word 4q+h -> low columns 8q + 2h, +1 and high columns 32 + 8q + 2h, +1
+              uint32_t lo[32], hi[32];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {  // words 4q .. 4q+3 -> low columns 8q.., high 32+8q..
-            uint32_t lo[8], hi[8];
+              for (int q = 0; q < 4; ++q)
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              const uint32_t x = wd[4 * q + h];
-              lo[2 * h] = lop3_and_or(x, 0x000F000Fu, 0x43004300u);
-              lo[2 * h + 1] = lop3_and_or(x >> 8, 0x000F000Fu, 0x43004300u);
-              hi[2 * h] = lop3_and_or(x >> 1, 0x00780078u, 0x43804380u);
-              hi[2 * h + 1] = lop3_and_or(x >> 9, 0x00780078u, 0x43804380u);
+                for (int h = 0; h < 4; ++h) {
+                  const uint32_t x = wd[4 * q + h];
+                  lo[8 * q + 2 * h] = lop3_and_or(x, 0x000F000Fu, 0x43004300u);
+                  lo[8 * q + 2 * h + 1] = lop3_and_or(x >> 8, 0x000F000Fu, 0x43004300u);
+                  hi[8 * q + 2 * h] = lop3_and_or(x >> 1, 0x00780078u, 0x43804380u);
+                  hi[8 * q + 2 * h + 1] = lop3_and_or(x >> 9, 0x00780078u, 0x43804380u);
+                }
+              tmem_st32(ta, lo);
+              tmem_st32(ta + 32, hi);
             }
-            tmem_st8(ta + 8 * q, lo);
-            tmem_st8(ta + 32 + 8 * q, hi);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&afull[w * MAXA + a]);
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[slot]);
         }
-        tmem_wait_st();
-        tc_fence_before();
-        asm volatile("bar.sync %0, 128;" ::"r"(2 + wg));
-        // ---- one thread issues the group's MMAs, then commits to this buffer's barrier
-        if (row == 0) {
-          tc_fence_after();
-          const uint32_t td = tm_d + abuf * NM;
-          const uint32_t tab = tm_a + abuf * ACOLS;
-#pragma unroll
-          for (int s = 0; s < 4; ++s) {  // four k16 steps of the group
-            const uint32_t xaddr = xs_a + (gl * 8 + 2 * s) * NM * 16;
-            const uint64_t bd = smem_desc(xaddr, NM * 16, 128);
-            // one k16 step = 8 TMEM columns of A (two bf16 per column)
-            umma_ts(td, tab + 8 * s, bd, IDESC, s > 0 ? 1u : 0u);
-            if (BITS == 8) umma_ts(td, tab + 32 + 8 * s, bd, IDESC, 1u);
-          }
-          umma_commit(&mb[abuf]);
-        }
-        __syncwarp();
-        // ---- fold the previous group while this one runs on the tensor core
-        fold_pending();
-        float sa, ba;
-        if (SCT) {
-          // select by value: a runtime index into the uint4 would go through local memory
-          const int wi = gi >> 1;
-          const uint32_t ws = wi == 0 ? sc8.x : wi == 1 ? sc8.y : wi == 2 ? sc8.z : sc8.w;
-          const uint32_t wb = wi == 0 ? bi8.x : wi == 1 ? bi8.y : wi == 2 ? bi8.z : bi8.w;
-          sa = (gi & 1) ? bf16_hi(ws) : bf16_lo(ws);
-          ba = (gi & 1) ? bf16_hi(wb) : bf16_lo(wb);
-        } else {
-          const int nn = min(n0 + row, p.N - 1);
-          sa = bf2f(p.scales[(size_t)nn * p.G + gfirst + gl]);
-          ba = bf2f(p.biases[(size_t)nn * p.G + gfirst + gl]);
-        }
-        pend_s = sa;
-        pend_c = ba - MAGIC * sa;
-        pend_gl = gl;
-        ++nissued;
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
-    }
-    fold_pending();
-    // partial tile -> shared memory [m][row]; the two warpgroups add in fixed order
-    if (wg == 0) {
-#pragma unroll
-      for (int m = 0; m < RP; ++m) part[m * PSTR + row] = acc[m];
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(NC));
-    if (wg == 1) {
-#pragma unroll
-      for (int m = 0; m < RP; ++m) part[m * PSTR + row] += acc[m];
-    }
-    tc_fence_before();
-  }
+    } else {
+      // --------------------------------------------------------- folding warpgroup w
+      const int w = (warp - WARP_FOLD) >> 2;
+      const int ftid = tid - WARP_FOLD * 32;   // 0 .. NF-1
+      const uint32_t tdb = tmem + w * PER + NA * ACOLS + lane_off;
+      const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
 
-  // ------------------------------------------------------------- split-K reduction
+      // split-K exchange + epilogue of tile jj (its partial sits in part[jj & 1])
+      auto finish = [&](int jj) {
+        const int pbuf = jj & 1;
+        float* pb = part + pbuf * RP * PSTR;
+        const int t = int(blockIdx.y) + jj * nclus;
+        const float* src = pb;
+        if (cs > 1) {
+          if (ok) ok = mbar_wait_cluster(&ready[pbuf], (jj >> 1) & 1, p.status, kErrWaitCluster);
+          for (int idx = ftid; idx < nmine * (TN / 4); idx += NF) {
+            const int mi = idx / (TN / 4), n4 = idx - mi * (TN / 4);
+            const int m = rank + mi * cs;
+            const uint32_t a = smem_u32(&pb[m * PSTR + n4 * 4]);
+            float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int c = 0; c < cs; ++c) {
+              const float4 v = ld_dsmem_f4(mapa_shared(a, c));
+              s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+            }
+            *reinterpret_cast<float4*>(&red[m * PSTR + n4 * 4]) = s;
+          }
+          asm volatile("bar.sync 1, %0;" ::"n"(NF));
+          if (ftid == 0)
+            for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&freeb[pbuf], c);
+          src = red;
+        }
+        epilogue<EPI, TN, PSTR>(p, src, rank, cs, t, t * TN, NF / 32, WARP_FOLD);
+        asm volatile("bar.sync 1, %0;" ::"n"(NF));  // red reuse
+      };
+
+      float acc[RP];
+      int i = 0;
+      for (int j = 0; j < ntl; ++j) {
+        const int n0 = (int(blockIdx.y) + j * nclus) * TN;
+#pragma unroll
+        for (int m = 0; m < RP; ++m) acc[m] = 0.f;
+        for (int st = 0; st < nst; ++st) {
+          const int g = j * nst + st;
+          const int slot = g % S;
+          if (ok) ok = mbar_wait(&full[slot], (g / S) & 1, p.status, kErrWaitFull);
+          uint4 sc8, bi8;
+          if (SCT) {
+            sc8 = lds128(smem_u32(scs + slot * SCB + row * 16));
+            bi8 = lds128(smem_u32(bis + slot * SCB + row * 16));
+          }
+          const int ng = ngs(st);
+#pragma unroll 1
+          for (int gi = w; gi < ng; gi += NWG, ++i) {
+            const int gl = st * GPS + gi;
+            const int d = i % ND, ud = i / ND;
+            // the tensor core always finishes (its operands are local): wait even after a failure
+            mbar_wait(&dfull[w * MAXD + d], ud & 1, p.status, kErrWaitMma);
+            tc_fence_after();
+            float sa, ba;
+            if (SCT) {
+              // select by value: a runtime index into the uint4 would go through local memory
+              const int wi = gi >> 1;
+              const uint32_t ws = wi == 0 ? sc8.x : wi == 1 ? sc8.y : wi == 2 ? sc8.z : sc8.w;
+              const uint32_t wb = wi == 0 ? bi8.x : wi == 1 ? bi8.y : wi == 2 ? bi8.z : bi8.w;
+              sa = (gi & 1) ? bf16_hi(ws) : bf16_lo(ws);
+              ba = (gi & 1) ? bf16_hi(wb) : bf16_lo(wb);
+            } else {
+              const int nn = min(n0 + row, p.N - 1);
+              sa = bf2f(p.scales[(size_t)nn * p.G + gfirst + gl]);
+              ba = bf2f(p.biases[(size_t)nn * p.G + gfirst + gl]);
+            }
+            const float ca = ba - MAGIC * sa;
+            const float* sxg = sx + gl * RP;
+            // the product in 16-column halves (fewer live registers at 32 rows)
+#pragma unroll
+            for (int h = 0; h < NM / 16; ++h) {
+              float dv[16];
+              tmem_ld16(tdb + d * NM + 16 * h, dv);
+              tmem_wait_ld();
+              if (h == NM / 16 - 1) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&dempty[w * MAXD + d]);
+              }
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const int m = 16 * h + e;
+                if (m < RP) acc[m] = fmaf(sa, dv[e], fmaf(ca, sxg[m], acc[m]));
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+
+        // ---- partial tile -> part[j & 1] ([m][row]); the two warpgroups add in fixed order
+        const int pbuf = j & 1;
+        float* pb = part + pbuf * RP * PSTR;
+        // part[pbuf] last held tile j-2: finished (read locally) one tile ago; the peers must
+        // also be done reading it
+        if (cs > 1 && j >= 2 && ok)
+          ok = mbar_wait_cluster(&freeb[pbuf], ((j - 2) >> 1) & 1, p.status, kErrWaitCluster);
+        if (w == 0) {
+#pragma unroll
+          for (int m = 0; m < RP; ++m) pb[m * PSTR + row] = acc[m];
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(NF));
+        if (w == 1) {
+#pragma unroll
+          for (int m = 0; m < RP; ++m) pb[m * PSTR + row] += acc[m];
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(NF));
+        if (cs > 1 && ftid == 0) {  // publish to every CTA of the cluster
+          fence_acq_rel_cluster();
+          for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&ready[pbuf], c);
+        }
+        if (j >= 1) finish(j - 1);
+      }
+      if (ntl >= 1) finish(ntl - 1);
+    }
+  }
+  tc_fence_before();
+
+  // no CTA leaves while a peer may still read its partial tiles or arrive on its barriers
+  // (and every MMA has completed: the fold warps waited for the last ones)
   if (cs > 1) cluster_sync_all(); else __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, ncols);
+    tmem_dealloc(tmem, kTmemCols);
   }
-  const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
-  for (int idx = tid; idx < nmine * (TN / 4); idx += NTHR) {
-    const int mi = idx / (TN / 4), n4 = idx - mi * (TN / 4);
-    const int m = rank + mi * cs;
-    const uint32_t a = smem_u32(&part[m * PSTR + n4 * 4]);
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (cs > 1) {
-      for (int c = 0; c < cs; ++c) {
-        const float4 v = ld_dsmem_f4(mapa_shared(a, c));
-        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
-      }
-    } else {
-      s = *reinterpret_cast<const float4*>(&part[m * PSTR + n4 * 4]);
-    }
-    *reinterpret_cast<float4*>(&red[m * PSTR + n4 * 4]) = s;
-  }
-  if (cs > 1) cluster_sync_all(); else __syncthreads();
-  epilogue<EPI, TN, PSTR>(p, red, rank, cs, ntile, n0, NTHR / 32);
 }
 
 }  // namespace tc
@@ -524,32 +690,96 @@ int tc_smem_bytes(int bits, int rt, int kslice, int nslots) {
   return tc::layout(bits, rt, kslice, nslots).total;
 }
 
+// The dynamic shared memory a launch requests: at least enough that one CTA fills an SM, so
+// CTAs never share an SM's tensor memory (a CTA blocked in tcgen05.alloc could otherwise wait on
+// a co-resident CTA that waits on it through the cluster).
+static int tc_launch_smem(int bits, int rt, int kslice, int nslots) {
+  return std::max(tc::layout(bits, rt, kslice, nslots).total, 120 * 1024);
+}
+
+// Lets a kernel take up to the device's opt-in shared memory per block and clusters of 16.
+// (The cap is the same for every launch, so a later launch with a larger ring never finds a
+// smaller limit left by an earlier one.)
+template <typename Kern>
+static cudaError_t configure_tc(Kern kern) {
+  int optin = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin,
+                                         current_device());
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+}
+
 template <int BITS, int RT, int EPI, bool SCT>
 static int launch_tc(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream) {
   auto kern = tc::qmm_tc_kernel<BITS, RT, EPI, SCT>;
-  // Every CTA allocates its TMEM columns up front and a cluster's CTAs wait on one another,
-  // so the CTAs that can be resident on one SM must be able to hold their columns at the same
-  // time (else a CTA blocked in tcgen05.alloc could wait on a peer that waits on it). Pad the
-  // shared-memory request so at most 512 / ncols CTAs fit on an SM.
-  const int ncols = tc::tmem_cols(BITS, RT);
-  const int per_sm = 512 / ncols;
-  const int smem_floor = per_sm >= 4 ? 0 : (228 * 1024) / (per_sm + 1) + 1024;
-  const int smem = std::max(tc::layout(BITS, RT, pl.kslice, pl.nslots).total, smem_floor);
-  static int configured = 0;
-  if (smem > configured) {
-    DSPARK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                    "qmm_tc: set smem");
-    DSPARK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
-                    "qmm_tc: allow cluster 16");
-    configured = smem;
+  const int smem = tc_launch_smem(BITS, RT, pl.kslice, pl.nslots);
+  static bool configured = false;
+  if (!configured) {
+    DSPARK_CUDA_TRY(configure_tc(kern), "qmm_tc: set smem / cluster attributes");
+    configured = true;
   }
   CUtensorMap wmap, smap, bmap;
   if (!tma_maps(p, tc::TN, SCT, &wmap, &smap, &bmap)) return DSPARK_ERR_CUDA;
-  dim3 grid(pl.cs, (p.N + tc::TN - 1) / tc::TN);
+  const int ntiles = (p.N + tc::TN - 1) / tc::TN;
+  int nclus = pl.clusters > 0 ? pl.clusters : sm_count(current_device()) / pl.cs;
+  nclus = std::max(1, std::min(nclus, ntiles));
+  dim3 grid(pl.cs, nclus);
   DSPARK_CUDA_TRY(launch_ex(kern, grid, dim3(tc::NTHR), (size_t)smem, stream, pl.cs, true, wmap,
                             smap, bmap, p),
                   "qmm_tc: launch");
   return DSPARK_OK;
+}
+
+// Clusters of `cs` CTAs (each requesting `smem` bytes) that the device runs at once.
+int tc_max_clusters(int bits, int rt, int cs, int smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int>, int> cache;
+  const int dev = current_device();
+  const auto key = std::make_tuple(dev, bits, rt, cs, smem);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const int sms = sm_count(dev);
+  int n = sms / cs;
+  auto query = [&](auto kern) {
+    if (configure_tc(kern) != cudaSuccess) return;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cs, 1);
+    cfg.blockDim = dim3(tc::NTHR);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = cs;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int c = 0;
+    if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) == cudaSuccess && c > 0) n = c;
+  };
+  // occupancy depends on the launch shape only; any instance of the kernel answers for all
+  if (bits == 4) {
+    if (rt <= 1) query(tc::qmm_tc_kernel<4, 1, EPI_PLAIN, true>);
+    else if (rt <= 2) query(tc::qmm_tc_kernel<4, 2, EPI_PLAIN, true>);
+    else query(tc::qmm_tc_kernel<4, 4, EPI_PLAIN, true>);
+  } else {
+    if (rt <= 1) query(tc::qmm_tc_kernel<8, 1, EPI_PLAIN, true>);
+    else if (rt <= 2) query(tc::qmm_tc_kernel<8, 2, EPI_PLAIN, true>);
+    else query(tc::qmm_tc_kernel<8, 4, EPI_PLAIN, true>);
+  }
+  cudaGetLastError();  // a refused query leaves the estimate; clear its error
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = n;
+  return n;
+}
+
+int tc_stage_bytes(int bits) { return tc::stage_bytes(bits); }
+int tc_planned_smem(int bits, int rt, int kslice, int nslots) {
+  return tc_launch_smem(bits, rt, kslice, nslots);
 }
 
 template <int BITS, int EPI>
