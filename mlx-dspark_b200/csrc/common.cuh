@@ -225,6 +225,17 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   }
 }
 
+// (a0, a1) += (b0, b1) * (c0, c1): two independent round-to-nearest fp32 FMAs in one packed
+// instruction (sm_100), bit-identical to two fmaf calls.
+__device__ __forceinline__ void fma2(float& a0, float& a1, float b0, float b1, float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\tmov.b64 rc, {%4, %5};\n\t"
+      "fma.rn.f32x2 ra, rb, rc, ra;\n\t"
+      "mov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
 // ------------------------------------------------------------------ shared-memory vector loads
 
 __device__ __forceinline__ uint2 lds64(uint32_t addr) {

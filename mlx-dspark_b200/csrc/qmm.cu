@@ -603,7 +603,9 @@ QmmPlan plan_tc(int N, int K, int bits, int rt) {
   const int force_cs = env_int("DSPARK_QMM_CS", 0);
   const int max_slots = std::max(2, env_int("DSPARK_QMM_SLOTS", 8));
   const int force_clusters = env_int("DSPARK_QMM_CLUSTERS", 0);
-  const double hbm = 6.5e12, sm_cap = 1.2e11;
+  // measured on B200 (4-bit, 16 rows): one CTA streams ~16.5 GB/s through dequant + MMA + fold,
+  // and a tile costs ~2.2 us more (split-K exchange, epilogue, pipeline turn-around)
+  const double hbm = 6.5e12, sm_cap = 1.65e10 * (bits == 8 ? 2.0 : 1.0), t_tile = 2.2e-6;
   const int ntiles = (N + 127) / 128;
   double best = 1e30;
   for (int cs : {1, 2, 3, 4, 5, 6, 8, 10, 12, 16}) {
@@ -622,7 +624,7 @@ QmmPlan plan_tc(int N, int K, int bits, int rt) {
     const int waves = (ntiles + clusters - 1) / clusters;
     const double tile_bytes = 128.0 * kslice * (bits / 8.0 + 4.0 / 64.0);
     const double rate = std::min(sm_cap, hbm / (clusters * cs));
-    double t = waves * (tile_bytes / rate + 0.3e-6) + 1.5e-6 + kslice * 32.0 / 2e11;
+    double t = waves * (tile_bytes / rate + t_tile) + 1.5e-6 + kslice * 32.0 / 2e11;
     if (slots < 3) t *= 1.15;
     if (cs & (cs - 1)) t *= 1.05;  // odd cluster shapes pack less evenly into GPCs
     if (t < best) {

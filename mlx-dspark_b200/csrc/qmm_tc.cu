@@ -73,10 +73,13 @@ struct Tr<8> {
 // Per warpgroup: A buffers (one group of dequantized weights each; the tensor core frees them
 // within a few hundred cycles) and D buffers (one group's fp32 product each; the fold warps free
 // them, and they must ride out the fold's work at the end of a tile), in half of TMEM.
-__host__ __device__ constexpr int nabuf(int bits) { return bits == 4 ? 4 : 2; }
+// The roles hand over units of UG groups (two for 4-bit, one for 8-bit), so every barrier
+// round trip is paid once per 4 KB of weights per row block.
+__host__ __device__ constexpr int ugroups(int bits) { return bits == 4 ? 2 : 1; }
+__host__ __device__ constexpr int nabuf(int bits) { return 2; }
 __host__ __device__ constexpr int ndbuf(int bits, int nm) {
-  return (256 - nabuf(bits) * (bits == 4 ? 32 : 64)) / nm < MAXD
-             ? (256 - nabuf(bits) * (bits == 4 ? 32 : 64)) / nm
+  return (256 - nabuf(bits) * ugroups(bits) * (bits == 4 ? 32 : 64)) / (ugroups(bits) * nm) < MAXD
+             ? (256 - nabuf(bits) * ugroups(bits) * (bits == 4 ? 32 : 64)) / (ugroups(bits) * nm)
              : MAXD;
 }
 
@@ -222,12 +225,13 @@ __device__ __forceinline__ bool elect_one() {
 // ------------------------------------------------------------------ kernel
 //
 // Warp roles (one CTA per SM, 576 threads):
-//   warps 0..7   two dequantizing warpgroups: warpgroup w takes the groups gi = w, w+2, ...
-//                of every stage and writes them to its A buffers in TMEM
+//   warps 0..7   two dequantizing warpgroups: warpgroup w takes the units (UG groups) u = w,
+//                w+2, ... of every stage and writes them to its A buffers in TMEM. After the
+//                next tile's units they also finish a tile: split-K exchange and epilogue,
+//                when the cluster peers have long published their partials
 //   warps 8..15  two folding warpgroups: warpgroup w reads the products of warpgroup w's
-//                groups from its D buffers and folds them into per-row accumulators. A tile's
-//                split-K exchange and epilogue are finished one tile later (after the next
-//                tile's groups), when the cluster peers have long published their partials
+//                units from its D buffers, folds them into per-row accumulators and at the
+//                end of a tile publishes the CTA's partial tile
 //   warp 16      issues the MMAs (warp-uniform, one elected lane) and commits them
 //   warp 17      the TMA producer
 // Per warpgroup w, group i of that warpgroup uses A buffer i % NA and D buffer i % ND:
@@ -249,9 +253,12 @@ __global__ void __launch_bounds__(NTHR, 1)
   constexpr int ACOLS = Tr<BITS>::ACOLS;
   constexpr float MAGIC = Tr<BITS>::MAGIC;
   constexpr uint32_t IDESC = idesc_bf16(NM);
+  constexpr int UG = ugroups(BITS);
   constexpr int NA = nabuf(BITS);
   constexpr int ND = ndbuf(BITS, NM);
-  constexpr int PER = NA * ACOLS + ND * NM;  // TMEM columns per warpgroup
+  constexpr int AU = UG * ACOLS;             // TMEM columns of one unit's A
+  constexpr int DU = UG * NM;                // TMEM columns of one unit's D
+  constexpr int PER = NA * AU + ND * DU;     // TMEM columns per warpgroup
   static_assert(NWG * PER <= kTmemCols && ND >= 2, "TMEM budget");
 
   extern __shared__ uint8_t smem_raw[];
@@ -366,24 +373,31 @@ __global__ void __launch_bounds__(NTHR, 1)
     for (int j = 0; j < ntl; ++j) {
       for (int st = 0; st < nst; ++st) {
         const int ng = ngs(st);
-        for (int gi = 0; gi < ng; ++gi) {
-          const int gl = st * GPS + gi;
-          const int w = gi & 1;
+        const int nu = (ng + UG - 1) / UG;
+        for (int uu = 0; uu < nu; ++uu) {
+          const int w = uu & 1;
           const int i = w ? cnt1++ : cnt0++;
           const int a = i % NA, ua = i / NA;
           const int d = i % ND, ud = i / ND;
           mbar_wait(&afull[w * MAXA + a], ua & 1, p.status, kErrWaitMma);
           if (ud > 0) mbar_wait(&dempty[w * MAXD + d], (ud - 1) & 1, p.status, kErrWaitMma);
           tc_fence_after();
-          const uint32_t ta = tmem + w * PER + a * ACOLS;
-          const uint32_t td = tmem + w * PER + NA * ACOLS + d * NM;
-          // the group's x: 8 blocks of 8 k at (gl*8 + blk) * NM * 16 bytes (descriptor units of 16)
-          const uint64_t bd = bd0 + uint64_t(gl * 8 * NM);
+          const uint32_t ta = tmem + w * PER + a * AU;
+          const uint32_t td = tmem + w * PER + NA * AU + d * DU;
+          // group gl's x: 8 blocks of 8 k at (gl*8 + blk) * NM * 16 bytes (descriptor units of 16)
+          const uint64_t bd = bd0 + uint64_t((st * GPS + uu * UG) * 8 * NM);
+          const int nug = min(UG, ng - uu * UG);
           if (elect_one()) {
 #pragma unroll
-            for (int s = 0; s < 4; ++s) {  // four k16 steps = 8 TMEM columns of A each
-              umma_ts(td, ta + 8 * s, bd + uint64_t(2 * s * NM), IDESC, s > 0 ? 1u : 0u);
-              if (BITS == 8) umma_ts(td, ta + 32 + 8 * s, bd + uint64_t(2 * s * NM), IDESC, 1u);
+            for (int gg = 0; gg < UG; ++gg) {
+              if (gg < nug) {
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {  // four k16 steps = 8 TMEM columns of A each
+                  const uint64_t b = bd + uint64_t((gg * 8 + 2 * s) * NM);
+                  umma_ts(td + gg * NM, ta + gg * ACOLS + 8 * s, b, IDESC, s > 0 ? 1u : 0u);
+                  if (BITS == 8) umma_ts(td + gg * NM, ta + gg * ACOLS + 32 + 8 * s, b, IDESC, 1u);
+                }
+              }
             }
             umma_commit(&adone[w * MAXA + a]);
             umma_commit(&dfull[w * MAXD + d]);
@@ -482,6 +496,37 @@ __global__ void __launch_bounds__(NTHR, 1)
       // --------------------------------------------------------- dequantizing warpgroup w
       const int w = warp >> 2;
       const uint32_t tab = tmem + w * PER + lane_off;
+      const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
+      // split-K exchange + epilogue of tile jj (its partial sits in part[jj & 1] of every CTA
+      // of the cluster once ready[jj & 1] completed), run by the dequant warps one tile after
+      // the fold warps published it
+      auto finish = [&](int jj) {
+        const int pbuf = jj & 1;
+        float* pb = part + pbuf * RP * PSTR;
+        const int t = int(blockIdx.y) + jj * nclus;
+        if (ok) ok = mbar_wait_cluster(&ready[pbuf], (jj >> 1) & 1, p.status, kErrWaitCluster);
+        const float* src = pb;
+        if (cs > 1) {
+          for (int idx = tid; idx < nmine * (TN / 4); idx += NF) {
+            const int mi = idx / (TN / 4), n4 = idx - mi * (TN / 4);
+            const int m = rank + mi * cs;
+            const uint32_t a = smem_u32(&pb[m * PSTR + n4 * 4]);
+            float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int c = 0; c < cs; ++c) {
+              const float4 v = ld_dsmem_f4(mapa_shared(a, c));
+              s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+            }
+            *reinterpret_cast<float4*>(&red[m * PSTR + n4 * 4]) = s;
+          }
+          asm volatile("bar.sync 3, %0;" ::"n"(NF));
+          if (tid == 0)
+            for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&freeb[pbuf], c);
+          src = red;
+        }
+        epilogue<EPI, TN, PSTR>(p, src, rank, cs, t, t * TN, NF / 32, 0);
+        asm volatile("bar.sync 3, %0;" ::"n"(NF));  // red (or part) reads done
+        if (cs == 1 && tid == 0) mbar_arrive(&freeb[pbuf]);
+      };
       int i = 0;
       for (int j = 0; j < ntl; ++j) {
         for (int st = 0; st < nst; ++st) {
@@ -490,14 +535,19 @@ __global__ void __launch_bounds__(NTHR, 1)
           if (ok) ok = mbar_wait(&full[slot], (g / S) & 1, p.status, kErrWaitFull);
           const uint32_t wbase = ring_a + slot * STG;
           const int ng = ngs(st);
+          const int nu = (ng + UG - 1) / UG;
 #pragma unroll 1
-          for (int gi = w; gi < ng; gi += NWG, ++i) {
+          for (int uu = w; uu < nu; uu += NWG, ++i) {
             const int a = i % NA, ua = i / NA;
             // A buffer a is free once the MMAs of its previous use completed (the tensor core
             // always finishes: wait even after a failure)
             if (ua > 0) mbar_wait(&adone[w * MAXA + a], (ua - 1) & 1, p.status, kErrWaitMma);
             tc_fence_after();
-            const uint32_t ta = tab + a * ACOLS;
+#pragma unroll
+            for (int gg = 0; gg < UG; ++gg) {
+            const int gi = uu * UG + gg;
+            if (gi >= ng) break;
+            const uint32_t ta = tab + a * AU + gg * ACOLS;
             if (BITS == 4) {
               const int box = gi >> 2;
               const int c0 = (gi & 3) * 2;
@@ -541,6 +591,7 @@ __global__ void __launch_bounds__(NTHR, 1)
               tmem_st32(ta, lo);
               tmem_st32(ta + 32, hi);
             }
+            }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -549,42 +600,14 @@ __global__ void __launch_bounds__(NTHR, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[slot]);
         }
+        if (j >= 1) finish(j - 1);
       }
+      if (ntl >= 1) finish(ntl - 1);
     } else {
       // --------------------------------------------------------- folding warpgroup w
       const int w = (warp - WARP_FOLD) >> 2;
       const int ftid = tid - WARP_FOLD * 32;   // 0 .. NF-1
-      const uint32_t tdb = tmem + w * PER + NA * ACOLS + lane_off;
-      const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
-
-      // split-K exchange + epilogue of tile jj (its partial sits in part[jj & 1])
-      auto finish = [&](int jj) {
-        const int pbuf = jj & 1;
-        float* pb = part + pbuf * RP * PSTR;
-        const int t = int(blockIdx.y) + jj * nclus;
-        const float* src = pb;
-        if (cs > 1) {
-          if (ok) ok = mbar_wait_cluster(&ready[pbuf], (jj >> 1) & 1, p.status, kErrWaitCluster);
-          for (int idx = ftid; idx < nmine * (TN / 4); idx += NF) {
-            const int mi = idx / (TN / 4), n4 = idx - mi * (TN / 4);
-            const int m = rank + mi * cs;
-            const uint32_t a = smem_u32(&pb[m * PSTR + n4 * 4]);
-            float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int c = 0; c < cs; ++c) {
-              const float4 v = ld_dsmem_f4(mapa_shared(a, c));
-              s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
-            }
-            *reinterpret_cast<float4*>(&red[m * PSTR + n4 * 4]) = s;
-          }
-          asm volatile("bar.sync 1, %0;" ::"n"(NF));
-          if (ftid == 0)
-            for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&freeb[pbuf], c);
-          src = red;
-        }
-        epilogue<EPI, TN, PSTR>(p, src, rank, cs, t, t * TN, NF / 32, WARP_FOLD);
-        asm volatile("bar.sync 1, %0;" ::"n"(NF));  // red reuse
-      };
-
+      const uint32_t tdb = tmem + w * PER + NA * AU + lane_off;
       float acc[RP];
       int i = 0;
       for (int j = 0; j < ntl; ++j) {
@@ -601,13 +624,18 @@ __global__ void __launch_bounds__(NTHR, 1)
             bi8 = lds128(smem_u32(bis + slot * SCB + row * 16));
           }
           const int ng = ngs(st);
+          const int nu = (ng + UG - 1) / UG;
 #pragma unroll 1
-          for (int gi = w; gi < ng; gi += NWG, ++i) {
-            const int gl = st * GPS + gi;
+          for (int uu = w; uu < nu; uu += NWG, ++i) {
             const int d = i % ND, ud = i / ND;
             // the tensor core always finishes (its operands are local): wait even after a failure
             mbar_wait(&dfull[w * MAXD + d], ud & 1, p.status, kErrWaitMma);
             tc_fence_after();
+            const int nug = min(UG, ng - uu * UG);
+#pragma unroll
+            for (int gg = 0; gg < UG; ++gg) {
+            const int gi = uu * UG + gg;
+            const int gl = st * GPS + gi;
             float sa, ba;
             if (SCT) {
               // select by value: a runtime index into the uint4 would go through local memory
@@ -622,23 +650,33 @@ __global__ void __launch_bounds__(NTHR, 1)
               ba = bf2f(p.biases[(size_t)nn * p.G + gfirst + gl]);
             }
             const float ca = ba - MAGIC * sa;
-            const float* sxg = sx + gl * RP;
-            // the product in 16-column halves (fewer live registers at 32 rows)
+            const float4* sxg = reinterpret_cast<const float4*>(sx + (gi < ng ? gl : 0) * RP);
+            // the product in 16-column pieces (fewer live registers); D is released after the
+            // unit's last piece is in registers
 #pragma unroll
             for (int h = 0; h < NM / 16; ++h) {
               float dv[16];
-              tmem_ld16(tdb + d * NM + 16 * h, dv);
+              tmem_ld16(tdb + d * DU + gg * NM + 16 * h, dv);
               tmem_wait_ld();
-              if (h == NM / 16 - 1) {
+              if (gg == UG - 1 && h == NM / 16 - 1) {
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&dempty[w * MAXD + d]);
               }
+              if (gg < nug) {
 #pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                const int m = 16 * h + e;
-                if (m < RP) acc[m] = fmaf(sa, dv[e], fmaf(ca, sxg[m], acc[m]));
+                for (int e4 = 0; e4 < 4; ++e4) {
+                  const int m0 = 16 * h + 4 * e4;
+                  if (m0 < RP) {  // acc = fma(s, P, fma(c, sum x, acc)), two rows per instruction
+                    const float4 xs4 = sxg[m0 / 4];
+                    fma2(acc[m0 + 0], acc[m0 + 1], ca, ca, xs4.x, xs4.y);
+                    fma2(acc[m0 + 2], acc[m0 + 3], ca, ca, xs4.z, xs4.w);
+                    fma2(acc[m0 + 0], acc[m0 + 1], sa, sa, dv[4 * e4 + 0], dv[4 * e4 + 1]);
+                    fma2(acc[m0 + 2], acc[m0 + 3], sa, sa, dv[4 * e4 + 2], dv[4 * e4 + 3]);
+                  }
+                }
               }
+            }
             }
           }
           __syncwarp();
@@ -648,9 +686,9 @@ __global__ void __launch_bounds__(NTHR, 1)
         // ---- partial tile -> part[j & 1] ([m][row]); the two warpgroups add in fixed order
         const int pbuf = j & 1;
         float* pb = part + pbuf * RP * PSTR;
-        // part[pbuf] last held tile j-2: finished (read locally) one tile ago; the peers must
-        // also be done reading it
-        if (cs > 1 && j >= 2 && ok)
+        // part[pbuf] last held tile j-2: every CTA of the cluster (this one included) must be
+        // done reading it
+        if (j >= 2 && ok)
           ok = mbar_wait_cluster(&freeb[pbuf], ((j - 2) >> 1) & 1, p.status, kErrWaitCluster);
         if (w == 0) {
 #pragma unroll
@@ -662,13 +700,15 @@ __global__ void __launch_bounds__(NTHR, 1)
           for (int m = 0; m < RP; ++m) pb[m * PSTR + row] += acc[m];
         }
         asm volatile("bar.sync 1, %0;" ::"n"(NF));
-        if (cs > 1 && ftid == 0) {  // publish to every CTA of the cluster
-          fence_acq_rel_cluster();
-          for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&ready[pbuf], c);
+        if (ftid == 0) {  // publish to every CTA of the cluster
+          if (cs > 1) {
+            fence_acq_rel_cluster();
+            for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&ready[pbuf], c);
+          } else {
+            mbar_arrive(&ready[pbuf]);
+          }
         }
-        if (j >= 1) finish(j - 1);
       }
-      if (ntl >= 1) finish(ntl - 1);
     }
   }
   tc_fence_before();
