@@ -52,6 +52,15 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip e2e/roofline extras")
+    ap.add_argument("--micro", choices=["qmm", "attn"], default=None,
+                    help="run one kernel's microbench alone (ncu small cases)")
+    ap.add_argument("--rows", type=int, nargs="+", default=[1, 4, 8, 16])
+    ap.add_argument("--bits", type=int, default=4)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--copies", type=int, default=48)
+    ap.add_argument("--lengths", type=int, nargs="+", default=[1024, 4096, 16384, 32768])
+    ap.add_argument("--reps", type=int, default=10)
     return ap.parse_args()
 
 
@@ -280,6 +289,7 @@ def run_ours(args):
         out["e2e"] = e2e(vg, ids_all, nrej_all, args, world, dev)
         out["roofline"] = roofline(t, dev, pk)
         out["qmm_microbench"] = qmm_microbench(dev, pk)
+        out["attn_microbench"] = attn_microbench(dev, pk)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             out["cpu_baseline"] = {k: v for k, v in cpu_forward_sample(
@@ -354,26 +364,7 @@ def roofline(t, dev, pk) -> dict:
         for w in ws:
             skinny_qmm.qmm(x, w.wq, w.scales, w.biases, w.bits, out=out)
 
-    burst()
-    torch.cuda.synchronize()
-    side = torch.cuda.Stream(device=dev)
-    side.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(side):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=side):
-            burst()
-    torch.cuda.current_stream(dev).wait_stream(side)
-    for _ in range(3):
-        gr.replay()
-    torch.cuda.synchronize()
-    reps = 10
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        gr.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    per = e0.elapsed_time(e1) / (reps * len(ws)) / 1e3
+    per = _graph_time(burst, 10, dev) / len(ws)
     nbytes = _qmm_bytes(2 * cfg.intermediate, cfg.hidden, ROWS, cfg.bits)
     ach = nbytes / per / 1e9
     traffic = None
@@ -387,46 +378,110 @@ def roofline(t, dev, pk) -> dict:
             "peak_source": pk["src"]}
 
 
-def qmm_microbench(dev, pk) -> dict:
-    """K = N = 4096, 4-bit, M in {1, 4, 8, 16}; 48 distinct weight copies
-    (~450 MB, > 3x L2) rotated back to back inside a CUDA graph."""
+def _graph_time(burst, reps: int, dev) -> float:
+    """Seconds per replay of ``burst`` captured in a CUDA graph (3 untimed replays, then
+    ``reps`` timed back to back with CUDA events on the replay stream)."""
+    import torch
+
+    burst()
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            burst()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps / 1e3
+
+
+def qmm_microbench(dev, pk, rows=(1, 4, 8, 16), bits=4, n=4096, k=4096, copies=48,
+                   reps=10) -> dict:
+    """K = N = 4096, 4-bit, M in {1, 4, 8, 16}; ``copies`` distinct weight
+    copies (48: ~450 MB, > 3x L2) rotated back to back inside a CUDA graph."""
     import torch
 
     from mlx_dspark_b200 import quant, skinny_qmm
 
     g = torch.Generator(device=dev).manual_seed(0)
-    ws = [quant.random_qweight(4096, 4096, 4, device=dev, generator=g) for _ in range(48)]
+    ws = [quant.random_qweight(n, k, bits, device=dev, generator=g) for _ in range(copies)]
     res = {}
-    for M in (1, 4, 8, 16):
-        x = torch.randn((M, 4096), device=dev, generator=g).to(torch.bfloat16)
-        out = torch.empty((M, 4096), dtype=torch.bfloat16, device=dev)
+    for M in rows:
+        x = torch.randn((M, k), device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty((M, n), dtype=torch.bfloat16, device=dev)
 
         def burst():
             for w in ws:
-                skinny_qmm.qmm(x, w.wq, w.scales, w.biases, 4, out=out)
+                skinny_qmm.qmm(x, w.wq, w.scales, w.biases, bits, out=out)
 
-        burst()
-        side = torch.cuda.Stream(device=dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            gr = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gr, stream=side):
-                burst()
-        torch.cuda.current_stream(dev).wait_stream(side)
-        for _ in range(3):
-            gr.replay()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(10):
-            gr.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        per = e0.elapsed_time(e1) / (10 * len(ws)) / 1e3
-        gbs = _qmm_bytes(4096, 4096, M, 4) / per / 1e9
+        per = _graph_time(burst, reps, dev) / len(ws)
+        gbs = _qmm_bytes(n, k, M, bits) / per / 1e9
         res[f"M{M}"] = {"us": round(per * 1e6, 3), "gbs": round(gbs, 1),
                         "frac": round(gbs / pk["hbm_gbs"], 3)}
     return res
+
+
+def attn_microbench(dev, pk, lengths=(1024, 4096, 16384, 32768), reps=10) -> dict:
+    """GQA 32/8, head_dim 128, 16 causal query rows over a bf16 cache of
+    L keys, scale 1/sqrt(128); distinct K/V copies rotated so at least ~400 MB (> 3x L2) is
+    streamed per replay. Algorithmic bytes = K + V + q + out = 4096 L + 262144."""
+    import torch
+
+    from mlx_dspark_b200.multirow_attn import multirow_sdpa
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    res = {}
+    for L in lengths:
+        nbytes = 4096 * L + 262144
+        copies = max(3, -(-400_000_000 // nbytes))
+        q = torch.randn((1, 32, 16, 128), device=dev, generator=g).to(torch.bfloat16)
+        kv = [(torch.randn((1, 8, L, 128), device=dev, generator=g).to(torch.bfloat16),
+               torch.randn((1, 8, L, 128), device=dev, generator=g).to(torch.bfloat16))
+              for _ in range(copies)]
+        out = torch.empty_like(q)
+
+        def burst():
+            for k, v in kv:
+                multirow_sdpa(q, k, v, scale=128 ** -0.5, causal=True, out=out)
+
+        per = _graph_time(burst, reps, dev) / copies
+        gbs = nbytes / per / 1e9
+        res[f"L{L}"] = {"us": round(per * 1e6, 3), "gbs": round(gbs, 1),
+                        "frac": round(gbs / pk["hbm_gbs"], 3)}
+        del kv
+    return res
+
+
+def run_micro(args):
+    """``--micro qmm|attn``: one kernel's microbench alone (the small cases profiled with ncu).
+    Prints one JSON line."""
+    import torch
+
+    import mlx_dspark_b200  # noqa: F401
+    from mlx_dspark_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _lib.ensure_init(0)
+    pk = peaks()
+    if args.micro == "qmm":
+        r = qmm_microbench(dev, pk, rows=tuple(args.rows), bits=args.bits, n=args.n, k=args.k,
+                           copies=args.copies, reps=args.reps)
+        cfg = {"bits": args.bits, "n": args.n, "k": args.k, "copies": args.copies}
+    else:
+        r = attn_microbench(dev, pk, lengths=tuple(args.lengths), reps=args.reps)
+        cfg = {"hq": 32, "hk": 8, "qL": 16, "d": 128}
+    print(json.dumps({"micro": args.micro, "config": cfg, "peak_gbs": pk["hbm_gbs"],
+                      "peak_source": pk["src"], "result": r,
+                      "device_status": _lib.device_status(0)}), flush=True)
 
 
 # ----------------------------------------------------------------------------- reference arm
@@ -503,7 +558,9 @@ def run_reference(args):
 
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.micro:
+        run_micro(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -29,7 +29,9 @@
 //    for the next RMSNorm), SwiGLU on interleaved gate/up rows, and Qwen3 q/k RMSNorm + RoPE
 //    + KV-cache write. The prologue can apply RMSNorm to x while staging it.
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <tuple>
 #include <string>
 #include <unordered_map>
 
@@ -574,19 +576,84 @@ static int dispatch_rt(const QmmParams& p, const QmmPlan& pl, cudaStream_t s) {
 // split-K reduction), and a penalty for shallow pipelines.
 static QmmPlan plan_mma(int N, int K, int bits, int epi, int min_tn, int rt);
 
-static bool use_tc() {
+// Engine choice: DSPARK_QMM_IMPL = "st" (default: streaming), "tc" (tcgen05 / TMEM) or "mma"
+// (per-tile CTAs). Shapes an engine cannot serve fall through to the next one.
+static int impl_choice() {
   const char* v = std::getenv("DSPARK_QMM_IMPL");
-  return !(v != nullptr && std::string(v) == "mma");
+  if (v == nullptr) return 2;
+  const std::string s(v);
+  return s == "mma" ? 0 : s == "tc" ? 1 : 2;
 }
 
 QmmPlan plan(int N, int K, int bits, int epi, int min_tn, int rt) {
-  if (use_tc()) {
-    // shapes whose 32-row x slice and ring do not fit the tcgen05 engine's shared memory
-    // run on the mma.sync engine (the same contract, both hand-written CUDA)
-    const QmmPlan pl = plan_tc(N, K, bits, rt);
-    if (pl.nw > 0) return pl;
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int, int, int>, QmmPlan> cache;
+  const int impl = impl_choice();
+  const auto key = std::make_tuple(current_device(), N, K, bits, epi * 64 + min_tn, rt, impl);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
   }
-  return plan_mma(N, K, bits, epi, min_tn, rt);
+  QmmPlan pl;
+  pl.nw = 0;
+  if (impl == 2) pl = plan_st(N, K, bits, rt);
+  if (pl.nw == 0 && impl >= 1) pl = plan_tc(N, K, bits, rt);
+  // shapes whose x slice and ring fit neither persistent engine run on per-tile CTAs (the same
+  // contract, all hand-written CUDA)
+  if (pl.nw == 0) pl = plan_mma(N, K, bits, epi, min_tn, rt);
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = pl;
+  return pl;
+}
+
+// Streaming engine: choose the split-K factor cs (= cluster size), the ring depth and the
+// number of persistent clusters. Modelled as: every cluster walks ceil(tiles / clusters) tiles,
+// each CTA streaming 128 rows x K/cs of weights (+ scales/biases) at the smaller of a per-SM
+// streaming cap and its share of HBM bandwidth, plus a per-tile cost and a once-per-launch
+// start (x staging, first TMA bytes).
+QmmPlan plan_st(int N, int K, int bits, int rt) {
+  QmmPlan pl;
+  pl.engine = 2;
+  pl.nw = 0;
+  pl.rt = rt;
+  pl.sct = true;
+  if (K % 512) return pl;
+  const int force_cs = env_int("DSPARK_QMM_CS", 0);
+  const int max_slots = std::max(3, env_int("DSPARK_QMM_SLOTS", 8));
+  const int force_clusters = env_int("DSPARK_QMM_CLUSTERS", 0);
+  const double hbm = env_int("DSPARK_QMM_HBM_GBS", 6500) * 1e9;
+  const double sm_cap = env_int("DSPARK_QMM_SM_MBS", bits == 8 ? 60000 : 40000) * 1e6;
+  const double t_tile = env_int("DSPARK_QMM_TILE_NS", 300) * 1e-9;
+  const int mt = rt <= 1 ? 1 : rt <= 2 ? 2 : 4;
+  const int ntiles = (N + 127) / 128;
+  double best = 1e30;
+  for (int cs : {1, 2, 3, 4, 5, 6, 8, 10, 12, 16}) {
+    if (force_cs && cs != force_cs) continue;
+    const int kslice = ((K + cs - 1) / cs + 511) / 512 * 512;
+    if ((cs - 1) * kslice >= K) continue;
+    int slots = max_slots;
+    while (slots >= 3 && st_smem_bytes(bits, mt, kslice, slots) > 227 * 1024) --slots;
+    if (slots < 3) continue;
+    const int smem = st_smem_bytes(bits, mt, kslice, slots);
+    int clusters = std::min(ntiles, st_max_clusters(cs, smem));
+    if (force_clusters > 0) clusters = std::min(ntiles, force_clusters);
+    if (clusters < 1) continue;
+    const int waves = (ntiles + clusters - 1) / clusters;
+    const double tile_bytes = 128.0 * kslice * (bits / 8.0 + 4.0 / 64.0);
+    const double rate = std::min(sm_cap, hbm / (clusters * cs));
+    double t = waves * (tile_bytes / rate + t_tile) + 1.5e-6 + kslice * 2.0 * 8 * mt / 2e11;
+    if (cs & (cs - 1)) t *= 1.03;  // odd cluster shapes pack less evenly into GPCs
+    if (t < best) {
+      best = t;
+      pl.nw = 8;  // 128-row tile
+      pl.cs = cs;
+      pl.kslice = kslice;
+      pl.nslots = slots;
+      pl.clusters = clusters;
+    }
+  }
+  return pl;
 }
 
 // tcgen05 engine (persistent clusters): choose the split-K factor cs (= cluster size), the ring
@@ -711,9 +778,11 @@ int run(const QmmParams& p_in, int epi, const QmmPlan* plan_in, cudaStream_t str
     return fail(DSPARK_ERR_ARG, "qmm: plan made for %d rows used for M=%d", 8 * pl.rt, p.M);
   if (pl.sct && ((reinterpret_cast<uintptr_t>(p.scales) & 15) || (reinterpret_cast<uintptr_t>(p.biases) & 15)))
     pl.sct = false;
+  if (!pl.sct && pl.engine != 0) pl = plan_mma(p.N, p.K, p.bits, epi, epi == EPI_QKROPE ? 128 : 0, rt);
   p.kslice = pl.kslice;
   p.cs = pl.cs;
   p.nslots = pl.nslots;
+  if (pl.engine == 2) return run_st(p, epi, pl, stream);
   if (pl.engine == 1) return run_tc(p, epi, pl, stream);
   if (p.bits == 4) {
     switch (epi) {

@@ -58,7 +58,8 @@ struct QmmPlan {
   int nslots = 1;   // pipeline depth
   bool sct = true;  // scales/biases by TMA (needs K % 512 == 0)
   int rt = 2;       // row class the plan was made for (serves M <= 8 * rt)
-  int engine = 1;   // 1: tcgen05 (TMEM operands, qmm_tc.cu); 0: mma.sync (qmm.cu)
+  int engine = 2;   // 2: streaming (qmm_st.cu); 1: tcgen05 (TMEM operands, qmm_tc.cu);
+                    // 0: mma.sync per-tile CTAs (qmm.cu)
   int clusters = 0; // tcgen05: persistent clusters walking the tiles (0: one per cs SMs)
 };
 
@@ -73,6 +74,12 @@ int tc_smem_bytes(int bits, int rt, int kslice, int nslots);  // layout incl. ns
 int tc_stage_bytes(int bits);                                  // one ring stage
 int tc_planned_smem(int bits, int rt, int kslice, int nslots); // what a launch requests
 int tc_max_clusters(int bits, int rt, int cs, int smem);       // co-resident clusters
+
+// Streaming engine (qmm_st.cu): geometry and launch (tile 128 rows, K % 512 == 0).
+QmmPlan plan_st(int N, int K, int bits, int rt);
+int run_st(const QmmParams& p, int epi, const QmmPlan& pl, cudaStream_t s);
+int st_smem_bytes(int bits, int rt, int kslice, int nslots);
+int st_max_clusters(int cs, int smem);
 
 // Geometry for [N, K] at `bits` serving up to 8*rt rows (rt = 2: M <= 16, rt = 4: M <= 32).
 // It depends on the weight shape and the row class only, so within a class a row's result

@@ -1,0 +1,588 @@
+// K1, streaming engine: small-M affine-quantized matmul y[M,N] = x[M,K] . dequant(W)^T for
+// 1-32 rows (sm_100a). Same contract and numerics as qmm.cu / qmm_tc.cu (MLX affine 4/8-bit,
+// group 64, fp32 accumulation, per-group scale/bias fold, bf16 out) and the same epilogues.
+//
+// Why a third engine. At M <= 32 the product is ~64 flop per weight byte: HBM-bound by a
+// wide margin, and the tensor core is never the limit. What limits a CTA is how fast it can
+// turn packed weights into MMA operands and fold each group's product with its scale. This
+// engine keeps that chain — shared-memory load, dequantize, MMA, fold — inside each warp, so
+// the only synchronisation on the weight stream is the TMA ring itself:
+//
+//  * Persistent clusters (grid (cs, P)): the cs CTAs of a cluster split K; P clusters walk the
+//    128-row output tiles t = cluster, cluster + P, ... One producer warp streams each CTA's
+//    weights through a ring of 16 KB stages (one 128-byte x 128-row TMA box, 128-byte swizzle,
+//    L2 evict-first); every 8 groups the scales and biases ride on the same mbarrier. The
+//    producer never waits on the previous kernel (griddepcontrol.wait), so under programmatic
+//    dependent launch a kernel's first weight stages stream while its predecessor finishes.
+//  * Eight consumer warps, 16 weight rows each. Per group of 64 k a thread loads its rows' words
+//    (one 8- or 16-byte ld.shared each, conflict-free through a row permutation matched to the
+//    swizzle), dequantizes them with the bf16 magic-exponent trick (nibble | 0x4300 = 128 + q,
+//    exact; 8-bit as two exact nibble planes 128 + lo and 256 + 16 hi) straight into mma.m16n8k16
+//    A fragments (the weights are the 16-row A operand, x the 8-column B operand, so every
+//    weight is read once whatever M is), and folds the group's exact product P into fp32
+//    accumulators: acc += scale*P + (bias - MAGIC*scale) * sum_k x (packed f32x2 FMAs).
+//  * x (the CTA's K slice, <= 32 rows) is staged once per launch, k permuted inside each 8-block
+//    (4-bit) or 4-block (8-bit) exactly as the magic extraction orders the weights, so one
+//    16-byte load gives the B fragments of two k16 steps.
+//  * Four epilogue warps finish each tile while the consumers stream the next one: split-K
+//    partial tiles are exchanged through distributed shared memory (double-buffered, rows
+//    m = rank + i*cs reduced in fixed rank order: deterministic, and a row's result never
+//    depends on how many rows ride with it), then the shared epilogue runs on them.
+// Every mbarrier wait is time-bounded (a failed wait records an error in the device status word
+// and the kernel drains without further waits on other agents).
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "common.cuh"
+#include "host_common.h"
+#include "qmm.h"
+#include "qmm_epilogue.cuh"
+
+namespace dspark {
+namespace qmm {
+namespace st {
+
+constexpr int TN = 128;                 // weight rows per tile
+constexpr int NWC = 8;                  // consumer warps, 16 weight rows each
+constexpr int WARP_TMA = NWC;           // the producer warp
+constexpr int NWE = 4;                  // epilogue warps
+constexpr int WARP_EPI = NWC + 1;
+constexpr int NTHR = (NWC + 1 + NWE) * 32;
+constexpr int NC = NWC * 32;
+constexpr int NE = NWE * 32;
+constexpr int PSTR = TN + 4;            // fp32 row stride of partial / reduced tiles
+constexpr int STG = TN * 128;           // one stage: a 128-byte-wide box of 128 rows
+constexpr int SCB = TN * 16;            // 8 groups of bf16 scales (or biases) for 128 rows
+constexpr int KBLK = 512;               // k per scale block (8 groups)
+
+template <int BITS>
+struct Tr;
+template <>
+struct Tr<4> {
+  static constexpr int KB = 256;   // k per stage
+  static constexpr int GPS = 4;    // groups per stage
+  static constexpr int SPS = 2;    // stages per scale block
+  static constexpr float MAGIC = 128.0f;
+};
+template <>
+struct Tr<8> {
+  static constexpr int KB = 128;
+  static constexpr int GPS = 2;
+  static constexpr int SPS = 4;
+  static constexpr float MAGIC = 384.0f;  // 128 (low plane) + 256 (high plane)
+};
+
+// Scale-block slots: block b (stages b*SPS .. b*SPS+SPS-1) is reloaded into its slot only
+// after stage b*SPS + SPS - 1 has been consumed, which the weight ring guarantees when
+// SS * SPS >= S + SPS - 1.
+__host__ __device__ inline int scale_slots(int bits, int nslots) {
+  const int sps = bits == 4 ? 2 : 4;
+  return (nslots + 2 * sps - 2) / sps;
+}
+
+struct Layout {
+  int ring, sring, xs, sx, part, red, rs, bars, total;
+};
+
+__host__ __device__ inline int x_pitch(int kslice) { return kslice * 2 + 16; }
+
+__host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslots) {
+  const int rp = 8 * mt;
+  Layout L;
+  int off = 0;
+  L.ring = off;                      // 1024-byte aligned stages (128-byte swizzle atoms)
+  off += nslots * STG;
+  L.sring = off;
+  off += scale_slots(bits, nslots) * 2 * SCB;
+  L.xs = off;
+  off += rp * x_pitch(kslice);
+  off = (off + 15) & ~15;
+  L.sx = off;
+  off += (kslice / 64) * rp * 4;
+  off = (off + 15) & ~15;
+  L.part = off;
+  off += 2 * rp * PSTR * 4;
+  L.red = off;
+  off += rp * PSTR * 4;
+  L.rs = off;
+  off += 32 * 4;
+  off = (off + 15) & ~15;
+  L.bars = off;
+  off += (2 * nslots + 4) * 8;
+  L.total = off + 1024;  // slack to align the dynamic base to 1024 bytes
+  return L;
+}
+
+// Physical tile row of MMA row g (0..7) inside a 16-row group. The 128-byte swizzle stores
+// 16-byte chunk c of row r at chunk c ^ (r & 7); these permutations make the rows that one
+// shared-memory wavefront serves (4 rows for 8-byte loads, 2 rows for 16-byte loads) land on
+// disjoint chunks, so the weight loads are bank-conflict free.
+template <int BITS>
+__device__ __forceinline__ int row_perm(int g) {
+  return BITS == 4 ? (((g & 3) << 1) | (g >> 2)) : (((g & 1) << 2) | (g >> 1));
+}
+
+template <int BITS, int MT, int EPI>
+__global__ void __launch_bounds__(NTHR, 1)
+    qmm_st_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
+                  const __grid_constant__ CUtensorMap bmap, const QmmParams p) {
+  constexpr int RP = 8 * MT;
+  constexpr int KB = Tr<BITS>::KB;
+  constexpr int GPS = Tr<BITS>::GPS;
+  constexpr int SPS = Tr<BITS>::SPS;
+  constexpr float MAGIC = Tr<BITS>::MAGIC;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int S = p.nslots;
+  const int SS = scale_slots(BITS, S);
+  const Layout Lo = layout(BITS, MT, p.kslice, S);
+  uint8_t* ring = smem + Lo.ring;
+  uint8_t* sring = smem + Lo.sring;
+  uint8_t* xs = smem + Lo.xs;
+  float* sx = reinterpret_cast<float*>(smem + Lo.sx);
+  float* part = reinterpret_cast<float*>(smem + Lo.part);
+  float* red = reinterpret_cast<float*>(smem + Lo.red);
+  float* rsm = reinterpret_cast<float*>(smem + Lo.rs);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lo.bars);
+  uint64_t* empty = full + S;
+  uint64_t* ready = empty + S;   // [2] every cluster CTA published its partial tile
+  uint64_t* freeb = ready + 2;   // [2] every cluster CTA finished reading this CTA's partial
+
+  const int cs = p.cs;
+  const int rank = blockIdx.x;
+  const int ntiles = (p.N + TN - 1) / TN;
+  const int nclus = gridDim.y;
+  const int ntl = int(blockIdx.y) < ntiles ? (ntiles - int(blockIdx.y) + nclus - 1) / nclus : 0;
+  const int kbase = rank * p.kslice;
+  const int kvalid = min(p.kslice, p.K - kbase);
+  const int nsb = (kvalid + KBLK - 1) / KBLK;  // scale blocks per tile (K % 512 == 0)
+  const int nst = nsb * SPS;                    // stages per tile
+  const int gslice = p.kslice / 64;
+  const int XP = x_pitch(p.kslice);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = threadIdx.x;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NWC);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ready[i], cs);
+      mbar_init(&freeb[i], cs);
+    }
+    fence_mbar_init();
+  }
+  if (cs > 1) cluster_sync_all(); else __syncthreads();  // peers' barriers exist before use
+  pdl_launch_dependents();
+
+  bool ok = true;  // false once a wait on another agent ran out: drain without waiting
+  if (warp == WARP_TMA) {
+    // ------------------------------------------------------------- producer warp
+    if (lane == 0) {
+      prefetch_tmap(&wmap);
+      prefetch_tmap(&smap);
+      prefetch_tmap(&bmap);
+      const uint64_t pol = l2_policy_evict_first();
+      int issued = 0;
+      for (int j = 0; j < ntl && ok; ++j) {
+        const int n0 = (int(blockIdx.y) + j * nclus) * TN;
+        for (int st = 0; st < nst; ++st) {
+          const int g = j * nst + st;
+          const int slot = g % S;
+          if (g >= S && !mbar_wait(&empty[slot], ((g / S) - 1) & 1, p.status, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          const bool sblk = (st % SPS) == 0;
+          mbar_arrive_expect_tx(&full[slot], STG + (sblk ? 2 * SCB : 0));
+          const int kk = kbase + st * KB;
+          tma_load_2d(ring + slot * STG, &wmap, &full[slot], kk * BITS / 32, n0, pol);
+          if (sblk) {
+            const int ss = (j * nsb + st / SPS) % SS;
+            tma_load_2d(sring + ss * 2 * SCB, &smap, &full[slot], kk / 64, n0, pol);
+            tma_load_2d(sring + ss * 2 * SCB + SCB, &bmap, &full[slot], kk / 64, n0, pol);
+          }
+          ++issued;
+        }
+      }
+      // never leave the CTA with copies in flight: wait (bounded) for the last ones issued
+      for (int g = max(0, issued - S); g < issued; ++g)
+        mbar_wait(&full[g % S], (g / S) & 1, p.status, kErrWaitFull);
+    }
+    __syncwarp();
+  } else if (warp < NWC) {
+    // ------------------------------------------------------------- consumer warps
+    pdl_wait();  // x (and the RMSNorm statistics) come from the previous kernel
+    if (p.norm_w != nullptr) {
+      for (int m = warp; m < RP; m += NWC) {
+        float ss = 0.f;
+        if (m < p.M)
+          for (int e = lane; e < p.ssq_n; e += 32) ss += __ldcg(&p.ssq_in[e * p.ssq_stride + m]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) rsm[m] = m < p.M ? rsqrtf(ss / float(p.K) + p.eps) : 0.f;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(NC));
+    }
+    // stage the K slice of x: row m at xs + m*XP, k permuted inside each 8-block (4-bit:
+    // 0,4,1,5,2,6,3,7) or 4-block (8-bit: 0,2,1,3); zero rows beyond M and k beyond the slice
+    {
+      const int chunks = p.kslice / 8;
+      const int total = RP * chunks;
+      constexpr int XB = 4;
+      const bool nrm = p.norm_w != nullptr;
+      for (int base = tid; base < total; base += NC * XB) {
+        uint4 v[XB], w[XB];
+#pragma unroll
+        for (int u = 0; u < XB; ++u) {
+          const int idx = base + u * NC;
+          const int m = idx / chunks, c = idx - m * chunks;
+          v[u] = make_uint4(0u, 0u, 0u, 0u);
+          w[u] = v[u];
+          if (idx < total && m < p.M && c * 8 < kvalid) {
+            const int k = kbase + c * 8;
+            v[u] = __ldcg(reinterpret_cast<const uint4*>(p.x + (size_t)m * p.ldx + k));
+            if (nrm) w[u] = __ldg(reinterpret_cast<const uint4*>(p.norm_w + k));
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < XB; ++u) {
+          const int idx = base + u * NC;
+          if (idx >= total) break;
+          const int m = idx / chunks, c = idx - m * chunks;
+          uint4 vv = v[u];
+          if (nrm && m < p.M) {
+            const float r = rsm[m];
+            uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
+            const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w[u]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
+                                  bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
+          }
+          uint4 o;
+          if (BITS == 4) {
+            o.x = __byte_perm(vv.x, vv.z, 0x5410);
+            o.y = __byte_perm(vv.x, vv.z, 0x7632);
+            o.z = __byte_perm(vv.y, vv.w, 0x5410);
+            o.w = __byte_perm(vv.y, vv.w, 0x7632);
+          } else {
+            o.x = __byte_perm(vv.x, vv.y, 0x5410);
+            o.y = __byte_perm(vv.x, vv.y, 0x7632);
+            o.z = __byte_perm(vv.z, vv.w, 0x5410);
+            o.w = __byte_perm(vv.z, vv.w, 0x7632);
+          }
+          *reinterpret_cast<uint4*>(xs + m * XP + c * 16) = o;
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(NC));
+      // per-group sums of the staged (rounded) x, summed in a fixed order
+      for (int idx = tid; idx < RP * gslice; idx += NC) {
+        const int g = idx / RP, m = idx - g * RP;
+        float s = 0.f;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+          const uint4 q = *reinterpret_cast<const uint4*>(xs + m * XP + (g * 8 + b) * 16);
+          s += (bf16_lo(q.x) + bf16_hi(q.x)) + (bf16_lo(q.y) + bf16_hi(q.y)) +
+               (bf16_lo(q.z) + bf16_hi(q.z)) + (bf16_lo(q.w) + bf16_hi(q.w));
+        }
+        sx[g * RP + m] = s;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(NC));
+    }
+
+    const int g8 = lane >> 2, t4 = lane & 3;
+    const int r0 = warp * 16 + row_perm<BITS>(g8), r1 = r0 + 8;
+    const uint32_t ring_a = smem_u32(ring);
+    const uint32_t sring_a = smem_u32(sring);
+    // this thread's B fragments of group gl, n8 tile mt: 32 bytes at row (8*mt + g8), k = 16*t4
+    const uint32_t xa = smem_u32(xs) + uint32_t(g8 * XP + t4 * 32);
+    // swizzled byte offset of (row, logical 16-byte chunk c) inside a stage, plus lane part
+    auto wofs = [](int row, int c) { return uint32_t(row * 128 + ((c ^ (row & 7)) << 4)); };
+
+    for (int j = 0; j < ntl; ++j) {
+      float acc[MT][4];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[mt][i] = 0.f;
+
+      for (int sb = 0; sb < nsb; ++sb) {
+        uint4 sv0, sv1, bv0, bv1;  // 8 groups of scales / biases of rows r0, r1
+#pragma unroll
+        for (int si = 0; si < SPS; ++si) {
+          const int st = sb * SPS + si;
+          const int g = j * nst + st;
+          const int slot = g % S;
+          if (ok) ok = mbar_wait(&full[slot], (g / S) & 1, p.status, kErrWaitFull);
+          if (si == 0) {
+            const uint32_t sa = sring_a + uint32_t(((j * nsb + sb) % SS) * 2 * SCB);
+            sv0 = lds128(sa + r0 * 16);
+            sv1 = lds128(sa + r1 * 16);
+            bv0 = lds128(sa + SCB + r0 * 16);
+            bv1 = lds128(sa + SCB + r1 * 16);
+          }
+          const uint32_t wb = ring_a + uint32_t(slot * STG);
+#pragma unroll
+          for (int gi = 0; gi < GPS; ++gi) {
+            const int gl = st * GPS + gi;          // group inside the K slice
+            const int gb = si * GPS + gi;          // group inside the scale block (0..7)
+            // B fragments (x), two k16 steps per 16-byte load
+            uint32_t b[MT][4][2];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+              const uint32_t a = xa + uint32_t(mt * 8 * XP + gl * 128);
+              const uint4 q0 = lds128(a);
+              const uint4 q1 = lds128(a + 16);
+              b[mt][0][0] = q0.x; b[mt][0][1] = q0.y;
+              b[mt][1][0] = q0.z; b[mt][1][1] = q0.w;
+              b[mt][2][0] = q1.x; b[mt][2][1] = q1.y;
+              b[mt][3][0] = q1.z; b[mt][3][1] = q1.w;
+            }
+            float pr[MT][4];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+              for (int i = 0; i < 4; ++i) pr[mt][i] = 0.f;
+            if (BITS == 4) {
+              // 8 bytes of row r: group bytes 8*t4 .. 8*t4+7 = k 16*t4 .. 16*t4+15
+              const int c = gi * 2 + (t4 >> 1);
+              const uint32_t lo8 = uint32_t((t4 & 1) * 8);
+              const uint2 w0 = lds64(wb + wofs(r0, c) + lo8);
+              const uint2 w1 = lds64(wb + wofs(r1, c) + lo8);
+#pragma unroll
+              for (int s = 0; s < 4; ++s) {
+                const uint32_t x0 = (s < 2) ? w0.x : w0.y;
+                const uint32_t x1 = (s < 2) ? w1.x : w1.y;
+                const int e = 2 * (s & 1);
+                const uint32_t a0 = lop3_and_or(x0 >> (4 * e), 0x000F000Fu, 0x43004300u);
+                const uint32_t a2 = lop3_and_or(x0 >> (4 * e + 4), 0x000F000Fu, 0x43004300u);
+                const uint32_t a1 = lop3_and_or(x1 >> (4 * e), 0x000F000Fu, 0x43004300u);
+                const uint32_t a3 = lop3_and_or(x1 >> (4 * e + 4), 0x000F000Fu, 0x43004300u);
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+                  mma_bf16_16816(pr[mt], a0, a1, a2, a3, b[mt][s][0], b[mt][s][1]);
+              }
+            } else {
+              // 16 bytes of row r: group bytes 16*t4 .. 16*t4+15 = k 16*t4 .. 16*t4+15
+              const int c = gi * 4 + t4;
+              const uint4 w0 = lds128(wb + wofs(r0, c));
+              const uint4 w1 = lds128(wb + wofs(r1, c));
+              const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
+              const uint32_t wc[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+              for (int s = 0; s < 4; ++s) {
+                const uint32_t x0 = wa[s], x1 = wc[s];
+                // low nibble plane: (k0, k2) and (k1, k3) of the word's 4 bytes as 128 + lo
+                uint32_t a0 = lop3_and_or(x0, 0x000F000Fu, 0x43004300u);
+                uint32_t a2 = lop3_and_or(x0 >> 8, 0x000F000Fu, 0x43004300u);
+                uint32_t a1 = lop3_and_or(x1, 0x000F000Fu, 0x43004300u);
+                uint32_t a3 = lop3_and_or(x1 >> 8, 0x000F000Fu, 0x43004300u);
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+                  mma_bf16_16816(pr[mt], a0, a1, a2, a3, b[mt][s][0], b[mt][s][1]);
+                // high nibble plane as 256 + 16 hi
+                a0 = lop3_and_or(x0 >> 1, 0x00780078u, 0x43804380u);
+                a2 = lop3_and_or(x0 >> 9, 0x00780078u, 0x43804380u);
+                a1 = lop3_and_or(x1 >> 1, 0x00780078u, 0x43804380u);
+                a3 = lop3_and_or(x1 >> 9, 0x00780078u, 0x43804380u);
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+                  mma_bf16_16816(pr[mt], a0, a1, a2, a3, b[mt][s][0], b[mt][s][1]);
+              }
+            }
+            // fold: acc += s*P + (b - MAGIC*s) * sum_k x, rows r0 (i = 0,1) and r1 (i = 2,3)
+            const uint32_t ws0 = (gb >> 1) == 0 ? sv0.x : (gb >> 1) == 1 ? sv0.y : (gb >> 1) == 2 ? sv0.z : sv0.w;
+            const uint32_t ws1 = (gb >> 1) == 0 ? sv1.x : (gb >> 1) == 1 ? sv1.y : (gb >> 1) == 2 ? sv1.z : sv1.w;
+            const uint32_t wb0 = (gb >> 1) == 0 ? bv0.x : (gb >> 1) == 1 ? bv0.y : (gb >> 1) == 2 ? bv0.z : bv0.w;
+            const uint32_t wb1 = (gb >> 1) == 0 ? bv1.x : (gb >> 1) == 1 ? bv1.y : (gb >> 1) == 2 ? bv1.z : bv1.w;
+            const float s0 = (gb & 1) ? bf16_hi(ws0) : bf16_lo(ws0);
+            const float s1 = (gb & 1) ? bf16_hi(ws1) : bf16_lo(ws1);
+            const float c0 = ((gb & 1) ? bf16_hi(wb0) : bf16_lo(wb0)) - MAGIC * s0;
+            const float c1 = ((gb & 1) ? bf16_hi(wb1) : bf16_lo(wb1)) - MAGIC * s1;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+              const float2 xs2 = *reinterpret_cast<const float2*>(sx + gl * RP + mt * 8 + 2 * t4);
+              fma2(acc[mt][0], acc[mt][1], c0, c0, xs2.x, xs2.y);
+              fma2(acc[mt][2], acc[mt][3], c1, c1, xs2.x, xs2.y);
+              fma2(acc[mt][0], acc[mt][1], s0, s0, pr[mt][0], pr[mt][1]);
+              fma2(acc[mt][2], acc[mt][3], s1, s1, pr[mt][2], pr[mt][3]);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+      }
+
+      // ---- partial tile j -> part[j & 1] ([m][row])
+      const int pbuf = j & 1;
+      float* pb = part + pbuf * RP * PSTR;
+      // part[pbuf] last held tile j-2: every CTA of the cluster must be done reading it
+      if (j >= 2 && ok)
+        ok = mbar_wait_cluster(&freeb[pbuf], ((j - 2) >> 1) & 1, p.status, kErrWaitCluster);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const int m = mt * 8 + 2 * t4;
+        pb[m * PSTR + r0] = acc[mt][0];
+        pb[(m + 1) * PSTR + r0] = acc[mt][1];
+        pb[m * PSTR + r1] = acc[mt][2];
+        pb[(m + 1) * PSTR + r1] = acc[mt][3];
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(NC));
+      if (tid == 0) {  // publish to every CTA of the cluster
+        if (cs > 1) {
+          fence_acq_rel_cluster();
+          for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&ready[pbuf], c);
+        } else {
+          mbar_arrive(&ready[pbuf]);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue warps
+    pdl_wait();  // the epilogues read / write buffers of earlier kernels (residual, caches)
+    const int etid = tid - WARP_EPI * 32;
+    const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
+    for (int j = 0; j < ntl; ++j) {
+      const int pbuf = j & 1;
+      const int t = int(blockIdx.y) + j * nclus;
+      const float* pb = part + pbuf * RP * PSTR;
+      if (ok) ok = mbar_wait_cluster(&ready[pbuf], (j >> 1) & 1, p.status, kErrWaitCluster);
+      const float* src = pb;
+      if (cs > 1) {
+        for (int idx = etid; idx < nmine * (TN / 4); idx += NE) {
+          const int mi = idx / (TN / 4), n4 = idx - mi * (TN / 4);
+          const int m = rank + mi * cs;
+          const uint32_t a = smem_u32(&pb[m * PSTR + n4 * 4]);
+          float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int c = 0; c < cs; ++c) {
+            const float4 v = ld_dsmem_f4(mapa_shared(a, c));
+            s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+          }
+          *reinterpret_cast<float4*>(&red[m * PSTR + n4 * 4]) = s;
+        }
+        asm volatile("bar.sync 2, %0;" ::"n"(NE));
+        if (etid == 0)
+          for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&freeb[pbuf], c);
+        src = red;
+      }
+      epilogue<EPI, TN, PSTR>(p, src, rank, cs, t, t * TN, NWE, WARP_EPI);
+      asm volatile("bar.sync 2, %0;" ::"n"(NE));  // red (or part) reads done
+      if (cs == 1 && etid == 0) mbar_arrive(&freeb[pbuf]);
+    }
+  }
+
+  // no CTA leaves while a peer may still read its partial tiles or arrive on its barriers
+  if (cs > 1) cluster_sync_all(); else __syncthreads();
+}
+
+}  // namespace st
+
+// ----------------------------------------------------------------------------- host side
+
+int st_smem_bytes(int bits, int rt, int kslice, int nslots) {
+  return st::layout(bits, rt, kslice, nslots).total;
+}
+
+template <typename Kern>
+static cudaError_t configure_st(Kern kern) {
+  int optin = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin,
+                                         current_device());
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+}
+
+// Clusters of `cs` CTAs (each requesting `smem` bytes) that the device runs at once.
+int st_max_clusters(int cs, int smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int>, int> cache;
+  const int dev = current_device();
+  const auto key = std::make_tuple(dev, cs, smem);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int n = sm_count(dev) / cs;
+  // occupancy depends on the launch shape only; one instance answers for all
+  auto kern = st::qmm_st_kernel<4, 2, EPI_PLAIN>;
+  if (configure_st(kern) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cs, 1);
+    cfg.blockDim = dim3(st::NTHR);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = cs;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int c = 0;
+    if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) == cudaSuccess && c > 0) n = c;
+  }
+  cudaGetLastError();  // a refused query leaves the estimate; clear its error
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = n;
+  return n;
+}
+
+template <int BITS, int MT, int EPI>
+static int launch_st(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream) {
+  auto kern = st::qmm_st_kernel<BITS, MT, EPI>;
+  const int smem = st::layout(BITS, MT, pl.kslice, pl.nslots).total;
+  static bool configured = false;
+  if (!configured) {
+    DSPARK_CUDA_TRY(configure_st(kern), "qmm_st: set smem / cluster attributes");
+    configured = true;
+  }
+  CUtensorMap wmap, smap, bmap;
+  if (!tma_maps(p, st::TN, true, &wmap, &smap, &bmap)) return DSPARK_ERR_CUDA;
+  const int ntiles = (p.N + st::TN - 1) / st::TN;
+  int nclus = pl.clusters > 0 ? pl.clusters : sm_count(current_device()) / pl.cs;
+  nclus = std::max(1, std::min(nclus, ntiles));
+  DSPARK_CUDA_TRY(launch_ex(kern, dim3(pl.cs, nclus), dim3(st::NTHR), (size_t)smem, stream, pl.cs,
+                            true, wmap, smap, bmap, p),
+                  "qmm_st: launch");
+  return DSPARK_OK;
+}
+
+template <int BITS, int EPI>
+static int st_dispatch(const QmmParams& p, const QmmPlan& pl, cudaStream_t s) {
+  if (p.M <= 8) return launch_st<BITS, 1, EPI>(p, pl, s);
+  if (p.M <= 16) return launch_st<BITS, 2, EPI>(p, pl, s);
+  return launch_st<BITS, 4, EPI>(p, pl, s);
+}
+
+int run_st(const QmmParams& p, int epi, const QmmPlan& pl, cudaStream_t s) {
+  if (!pl.sct || p.K % st::KBLK)
+    return fail(DSPARK_ERR_UNSUPPORTED, "qmm_st: needs K %% 512 == 0 and 16-byte aligned scales");
+  if (pl.kslice % st::KBLK) return fail(DSPARK_ERR_ARG, "qmm_st: k slice %d", pl.kslice);
+  if (p.bits == 4) {
+    switch (epi) {
+      case EPI_PLAIN: return st_dispatch<4, EPI_PLAIN>(p, pl, s);
+      case EPI_RESID: return st_dispatch<4, EPI_RESID>(p, pl, s);
+      case EPI_SWIGLU: return st_dispatch<4, EPI_SWIGLU>(p, pl, s);
+      case EPI_QKROPE: return st_dispatch<4, EPI_QKROPE>(p, pl, s);
+    }
+  } else {
+    switch (epi) {
+      case EPI_PLAIN: return st_dispatch<8, EPI_PLAIN>(p, pl, s);
+      case EPI_RESID: return st_dispatch<8, EPI_RESID>(p, pl, s);
+      case EPI_SWIGLU: return st_dispatch<8, EPI_SWIGLU>(p, pl, s);
+      case EPI_QKROPE: return st_dispatch<8, EPI_QKROPE>(p, pl, s);
+    }
+  }
+  return fail(DSPARK_ERR_ARG, "qmm_st: bad epilogue %d", epi);
+}
+
+}  // namespace qmm
+}  // namespace dspark
