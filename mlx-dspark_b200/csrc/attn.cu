@@ -11,14 +11,19 @@
 // folded in); P is rounded to bf16 for the P.V product, as in the reference.
 //
 // B200 design: one CTA per (key split, batch row, KV head, row group). A producer warp
-// streams 64-key K/V tiles into a 3-slot shared-memory ring with bulk copies (one per
-// 16-byte-aligned cache row, so strided cache views need no copy) completing on mbarriers.
+// streams 64-key K/V tiles into a 3-slot shared-memory ring of padded rows with 16-byte
+// cp.async copies (coalesced across lanes; any 16-byte-aligned row stride, so strided cache
+// views need no copy; keys past the end zero-filled), completing on mbarriers. (Bulk copies
+// of single 256-byte rows measured ~1.3 TB/s device-wide on B200: too small per request.)
 // Consumer warps run Q.K^T and P.V on tensor cores (mma.m16n8k16, ldmatrix from padded
 // rows) with a flash-attention online softmax; warps that split a tile's keys merge in shared
 // memory, the key splits of a cluster merge through distributed shared memory, and (only
 // when more splits are needed than a cluster holds) cluster groups merge through a workspace.
 #include <algorithm>
 #include <cmath>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "attn.h"
 #include "common.cuh"
@@ -43,13 +48,33 @@ struct AttnSmem {
 };
 
 template <int D, int NRT, int KS>
-__host__ __device__ constexpr int attn_smem_bytes() {
+__host__ __device__ constexpr int attn_core_bytes() {
   // ring (reused after the key loop for the merge buffers) + merge stats + barriers
   constexpr int RPG = NRT * 16;
   constexpr int merge = KS * RPG * D * 4;
   constexpr int ring = AttnSmem<D>::RING;
   constexpr int body = ring > merge ? ring : merge;
   return body + (2 * KS + 2) * RPG * 4 + 2 * NSLOT * 8 + 128;
+}
+
+// Receive area of the cluster merge: split s of a cluster pushes row r (owned by CTA r % ns)
+// into slot [s][r / ns] of the owner, D accumulators then m and l (rows of D + 4 floats).
+// Sized for any ns <= 8: ns * ceil(RPG / ns) <= RPG + 7 rows.
+template <int D, int NRT>
+__host__ __device__ constexpr int attn_recv_bytes() {
+  return (NRT * 16 + 8) * (D + 4) * 4;
+}
+
+template <int D, int NRT, int KS>
+__host__ __device__ constexpr int attn_smem_bytes() {
+  return attn_core_bytes<D, NRT, KS>() + attn_recv_bytes<D, NRT>();
+}
+
+// 2^x by the hardware approximation (ex2.approx.ftz: ~2 ulp; exact 0 for -inf)
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ int64_t q_base(const AttnParams& p, int b, const int64_t sb,
@@ -70,7 +95,7 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
 
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
-  constexpr int BODY = attn_smem_bytes<D, NRT, KS>() - (2 * KS + 2) * RPG * 4 - 2 * NSLOT * 8 - 128;
+  constexpr int BODY = attn_core_bytes<D, NRT, KS>() - (2 * KS + 2) * RPG * 4 - 2 * NSLOT * 8 - 128;
   float* bufO = reinterpret_cast<float*>(smem);            // [KS][RPG][D] (aliases the ring)
   float* bufM = reinterpret_cast<float*>(smem + BODY);     // [KS][RPG]
   float* bufL = bufM + KS * RPG;                           // [KS][RPG]
@@ -78,6 +103,7 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
   float* finL = finM + RPG;                                // [RPG]
   uint64_t* full = reinterpret_cast<uint64_t*>(finL + RPG);
   uint64_t* empty = full + NSLOT;
+  float* recv = reinterpret_cast<float*>(smem + attn_core_bytes<D, NRT, KS>());
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sidx_c = blockIdx.x;                 // split within the cluster
@@ -89,17 +115,13 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
   const int b = bh / p.Hk;
   const int G = p.Hq / p.Hk;
 
-  // zero the ring once: keys past a split's end read finite zeros, never stale garbage
-  for (int i = threadIdx.x; i < AttnSmem<D>::RING / 16; i += blockDim.x)
-    reinterpret_cast<uint4*>(ring)[i] = make_uint4(0u, 0u, 0u, 0u);
   if (threadIdx.x == 0) {
     for (int s = 0; s < NSLOT; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 32);  // one asynchronous arrival per producer lane
       mbar_init(&empty[s], NC);
     }
     fence_mbar_init();
   }
-  fence_proxy_async_smem();
   __syncthreads();
   pdl_launch_dependents();
   pdl_wait();  // q and the freshly appended cache rows come from the previous kernel
@@ -116,25 +138,39 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
 
   if (warp == NC) {
     // ------------------------------------------------------------------ producer warp
-    for (int st = 0; st < nst; ++st) {
+    // 16-byte cp.async copies, lanes on consecutive chunks of a row (coalesced); keys past
+    // the split's end are zero-filled without a read, so masked keys always hold finite
+    // values. Each lane's copies of a stage complete on full[slot] (32 arrivals).
+    constexpr int CPR = D * 2 / 16;          // 16-byte chunks per row (16 or 8)
+    constexpr int RPI = 32 / CPR;            // rows per warp instruction (2 or 4)
+    const int rsub = lane / CPR, ch = lane % CPR;
+    const uint32_t ring_a = smem_u32(ring);
+    bool ok = true;
+    for (int st = 0; st < nst && ok; ++st) {
       const int slot = st % NSLOT;
-      if (st >= NSLOT) {
-        if (!mbar_wait(&empty[slot], ((st / NSLOT) - 1) & 1, p.status, kErrWaitKVEmpty)) break;
-      }
+      if (st >= NSLOT) ok = mbar_wait(&empty[slot], ((st / NSLOT) - 1) & 1, p.status, kErrWaitKVEmpty);
+      if (!ok) break;
       const int kt = k0 + st * KT;
-      const int nv = min(KT, kend - kt);
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], uint32_t(nv) * D * 2 * 2);
-      __syncwarp();
-      uint8_t* ks = ring + slot * STG;
-      uint8_t* vs = ks + KT * ROWB;
-      for (int r = lane; r < 2 * nv; r += 32) {
-        const int key = r >> 1;
-        if (r & 1)
-          bulk_load(vs + key * ROWB, vb_ptr + int64_t(kt + key) * p.v_ss, D * 2, &full[slot]);
-        else
-          bulk_load(ks + key * ROWB, kb_ptr + int64_t(kt + key) * p.k_ss, D * 2, &full[slot]);
+      uint32_t dk = ring_a + slot * STG + rsub * ROWB + ch * 16;
+      const bf16* kp = kb_ptr + int64_t(kt + rsub) * p.k_ss + ch * 8;
+      const bf16* vp = vb_ptr + int64_t(kt + rsub) * p.v_ss + ch * 8;
+      const int64_t kstep = int64_t(RPI) * p.k_ss, vstep = int64_t(RPI) * p.v_ss;
+      int key = kt + rsub;
+#pragma unroll 8
+      for (int i = 0; i < KT / RPI; ++i) {
+        const bool valid = key < kend;
+        cp_async_16_zfill(dk, valid ? kp : kb_ptr, valid);
+        cp_async_16_zfill(dk + KT * ROWB, valid ? vp : vb_ptr, valid);
+        dk += RPI * ROWB;
+        kp += kstep;
+        vp += vstep;
+        key += RPI;
       }
+      cp_async_mbar_arrive(&full[slot]);
     }
+    // never leave with copies in flight: wait (bounded) for this lane's last stages
+    for (int st = max(0, nst - NSLOT); st < nst && ok; ++st)
+      mbar_wait(&full[st % NSLOT], (st / NSLOT) & 1, p.status, kErrWaitKV);
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ consumer warps
@@ -178,9 +214,10 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
     const float sc = p.scale_log2;
     const uint32_t ring_a = smem_u32(ring);
 
+    bool ok = true;  // false once a wait ran out: finish without further waits
     for (int st = 0; st < nst; ++st) {
       const int slot = st % NSLOT;
-      mbar_wait(&full[slot], (st / NSLOT) & 1, p.status, kErrWaitKV);
+      if (ok) ok = mbar_wait(&full[slot], (st / NSLOT) & 1, p.status, kErrWaitKV);
       const uint32_t ks_a = ring_a + slot * STG;
       const uint32_t vs_a = ks_a + KT * ROWB;
       const int kt = k0 + st * KT;
@@ -223,16 +260,16 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
         const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        const float f0 = exp2f(m0 - mn0), f1 = exp2f(m1 - mn1);
+        const float f0 = fast_exp2(m0 - mn0), f1 = fast_exp2(m1 - mn1);
         m0 = mn0;
         m1 = mn1;
         float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          s[j][0] = exp2f(s[j][0] - mn0);
-          s[j][1] = exp2f(s[j][1] - mn0);
-          s[j][2] = exp2f(s[j][2] - mn1);
-          s[j][3] = exp2f(s[j][3] - mn1);
+          s[j][0] = fast_exp2(s[j][0] - mn0);
+          s[j][1] = fast_exp2(s[j][1] - mn0);
+          s[j][2] = fast_exp2(s[j][2] - mn1);
+          s[j][3] = fast_exp2(s[j][3] - mn1);
           ps0 += s[j][0] + s[j][1];
           ps1 += s[j][2] + s[j][3];
         }
@@ -295,7 +332,7 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
       float acc = 0.f, L = 0.f;
 #pragma unroll
       for (int k = 0; k < KS; ++k) {
-        const float w = exp2f(bufM[k * RPG + r] - M);
+        const float w = fast_exp2(bufM[k * RPG + r] - M);
         acc += w * bufO[k * RPG * D + idx];
         L += w * bufL[k * RPG + r];
       }
@@ -308,25 +345,43 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
   }
 
   // ------------------------------------------------------------------ split merge + store
-  if (p.ns > 1) cluster_sync_all(); else __syncthreads();
+  // Every split pushes each of its rows into the CTA of the cluster that owns the row
+  // (r % ns): plain stores into distributed shared memory, one cluster barrier, then each
+  // owner merges its rows from local shared memory (no round trips on remote loads).
   const int ns = p.ns;
+  const int ro = (RPG + ns - 1) / ns;  // rows owned per CTA
+  constexpr int RW = D + 4;            // receive row: D accumulators, m, l
+  __syncthreads();                     // bufO / finM / finL complete
+  if (ns > 1) {
+    const uint32_t rbase = smem_u32(recv);
+    for (int idx = threadIdx.x; idx < RPG * (D / 4 + 1); idx += blockDim.x) {
+      const int r = idx / (D / 4 + 1), c4 = idx - r * (D / 4 + 1);
+      const int owner = r % ns, rl = r / ns;
+      const uint32_t dst = mapa_shared(rbase + uint32_t(((sidx_c * ro + rl) * RW + c4 * 4) * 4), owner);
+      if (c4 < D / 4)
+        st_dsmem_f4(dst, *reinterpret_cast<const float4*>(&bufO[r * D + c4 * 4]));
+      else
+        st_dsmem_f4(dst, make_float4(finM[r], finL[r], 0.f, 0.f));
+    }
+    cluster_sync_all();  // pushes visible to their owners
+  }
   const int64_t ob = q_base(p, b, p.o_sb, p.o_si);
   const int nrows = G * qLb;
-  for (int idx = threadIdx.x; idx < RPG * (D / 4); idx += blockDim.x) {
-    const int r = idx / (D / 4), d4 = (idx % (D / 4)) * 4;
-    if ((r % ns) != sidx_c) continue;
+  for (int idx = threadIdx.x; idx < ro * (D / 4); idx += blockDim.x) {
+    const int rl = idx / (D / 4), d4 = (idx % (D / 4)) * 4;
+    const int r = ns > 1 ? sidx_c + rl * ns : rl;
+    if (r >= RPG) continue;
     const int prow = rg * RPG + r;
     if (prow >= nrows) continue;
     float M = -1e30f, Lsum = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (ns > 1) {
-      const uint32_t am = smem_u32(&finM[r]), al = smem_u32(&finL[r]);
-      const uint32_t ao = smem_u32(&bufO[r * D + d4]);
-      for (int c = 0; c < ns; ++c) M = fmaxf(M, ld_dsmem_f32(mapa_shared(am, c)));
+      for (int c = 0; c < ns; ++c) M = fmaxf(M, recv[(c * ro + rl) * RW + D]);
       for (int c = 0; c < ns; ++c) {
-        const float w = exp2f(ld_dsmem_f32(mapa_shared(am, c)) - M);
-        Lsum += w * ld_dsmem_f32(mapa_shared(al, c));
-        const float4 v = ld_dsmem_f4(mapa_shared(ao, c));
+        const float* src = recv + (c * ro + rl) * RW;
+        const float w = fast_exp2(src[D] - M);
+        Lsum += w * src[D + 1];
+        const float4 v = *reinterpret_cast<const float4*>(&src[d4]);
         acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
       }
     } else {
@@ -352,41 +407,122 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
       *reinterpret_cast<uint2*>(dst) = pk;
     }
   }
-  if (p.ns > 1) cluster_sync_all();
 }
 
-// Cross-cluster merge of the ng partials (only when ng > 1).
+// Cross-cluster merge of the ng partials (only when ng > 1): one warp per packed row, every
+// lane loads all ng partials of its D/32 columns at once (no dependent load chains).
+constexpr int kMergeRows = 8;  // rows (warps) per block
+
 template <int D>
-__global__ void attn_merge_kernel(const AttnParams p, int rpg) {
+__global__ void __launch_bounds__(kMergeRows * 32) attn_merge_kernel(const AttnParams p, int rpg) {
   pdl_launch_dependents();
   pdl_wait();
-  const int bhr = blockIdx.x;
+  constexpr int DPL = D / 32;  // columns per lane (4 or 2)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grow = blockIdx.x * kMergeRows + warp;  // (bhr, r) flattened
+  const int bhr = grow / rpg, r = grow - bhr * rpg;
+  if (bhr >= p.B * p.Hk * p.nrg) return;
   const int rg = bhr % p.nrg, bh = bhr / p.nrg;
   const int hk = bh % p.Hk, b = bh / p.Hk;
   const int G = p.Hq / p.Hk;
   const int qLb = p.q_len ? p.q_len[b] : p.qL;
-  const int nrows = G * qLb;
-  const int64_t ob = q_base(p, b, p.o_sb, p.o_si);
-  for (int idx = threadIdx.x; idx < rpg * D; idx += blockDim.x) {
-    const int r = idx / D, d = idx % D;
-    const int prow = rg * rpg + r;
-    if (prow >= nrows) continue;
-    const float* base = p.ws + (int64_t(bhr) * p.ng * rpg + r) * kWsRow<D>;
-    const int64_t gstride = int64_t(rpg) * kWsRow<D>;
-    float M = -1e30f;
-    for (int g = 0; g < p.ng; ++g) M = fmaxf(M, base[g * gstride + D]);
-    float acc = 0.f, L = 0.f;
-    for (int g = 0; g < p.ng; ++g) {
-      const float w = exp2f(base[g * gstride + D] - M);
-      acc += w * base[g * gstride + d];
-      L += w * base[g * gstride + D + 1];
+  const int prow = rg * rpg + r;
+  if (prow >= G * qLb) return;
+  const float* base = p.ws + (int64_t(bhr) * p.ng * rpg + r) * kWsRow<D>;
+  const int64_t gstride = int64_t(rpg) * kWsRow<D>;
+  // the partials' maxima: lane g holds group g's (m, l)
+  float mg = -1e30f, lg = 0.f;
+  if (lane < p.ng) {
+    const float2 ml = *reinterpret_cast<const float2*>(base + lane * gstride + D);
+    mg = ml.x;
+    lg = ml.y;
+  }
+  float M = mg;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float wl = lane < p.ng ? fast_exp2(mg - M) : 0.f;
+  float L = wl * lg;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  float acc[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+  for (int g = 0; g < p.ng; ++g) {
+    const float w = __shfl_sync(0xffffffffu, wl, g);
+    const float* src = base + g * gstride + lane * DPL;
+    if (DPL == 4) {
+      const float4 v = *reinterpret_cast<const float4*>(src);
+      acc[0] += w * v.x; acc[1] += w * v.y; acc[2 % DPL] += w * v.z; acc[3 % DPL] += w * v.w;
+    } else {
+      const float2 v = *reinterpret_cast<const float2*>(src);
+      acc[0] += w * v.x; acc[1] += w * v.y;
     }
-    const int h = hk * G + prow / qLb, i = prow % qLb;
-    p.o[ob + int64_t(h) * p.o_sh + int64_t(i) * p.o_si + d] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const int h = hk * G + prow / qLb, i = prow % qLb;
+  bf16* dst = p.o + q_base(p, b, p.o_sb, p.o_si) + int64_t(h) * p.o_sh + int64_t(i) * p.o_si + lane * DPL;
+  if (DPL == 4) {
+    uint2 pk;
+    pk.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+    pk.y = pack_bf16x2(acc[2 % DPL] * inv, acc[3 % DPL] * inv);
+    *reinterpret_cast<uint2*>(dst) = pk;
+  } else {
+    *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(acc[0] * inv, acc[1] * inv);
   }
 }
 
 // ------------------------------------------------------------------------------ host side
+
+// Clusters of `cs` CTAs of the attention kernel for (D, nrt, ks) that the device runs at once.
+template <int D, int NRT, int KS>
+static int max_clusters_t(int cs) {
+  auto kern = attn_kernel<D, NRT, KS>;
+  constexpr int smem = attn_smem_bytes<D, NRT, KS>();
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+      cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+    cudaGetLastError();
+    return sm_count(current_device()) / cs;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cs, 1, 1);
+  cfg.blockDim = dim3((NRT * KS + 1) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = cs;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int c = 0;
+  if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) != cudaSuccess || c <= 0) {
+    cudaGetLastError();
+    c = sm_count(current_device()) / cs;
+  }
+  return c;
+}
+
+static int max_clusters(int D, int nrt, int ks, int cs) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int>, int> cache;
+  const auto key = std::make_tuple(current_device(), D, nrt, ks, cs);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int n;
+  if (D == 64) {
+    n = nrt == 1 ? max_clusters_t<64, 1, 2>(cs) : nrt == 2 ? max_clusters_t<64, 2, 2>(cs)
+        : nrt == 4 ? max_clusters_t<64, 4, 2>(cs) : max_clusters_t<64, 8, 1>(cs);
+  } else {
+    n = nrt == 1 ? max_clusters_t<128, 1, 2>(cs) : nrt == 2 ? max_clusters_t<128, 2, 2>(cs)
+        : nrt == 4 ? max_clusters_t<128, 4, 2>(cs) : max_clusters_t<128, 8, 1>(cs);
+  }
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = n;
+  return n;
+}
 
 AttnPlan plan(int B, int Hq, int Hk, int qL, int D, int L) {
   AttnPlan pl;
@@ -400,16 +536,29 @@ AttnPlan plan(int B, int Hq, int Hk, int qL, int D, int L) {
   pl.nrt = nrt;
   pl.ks = nrt >= 8 ? 1 : 2;
   pl.nrg = (tiles + nrt - 1) / nrt;
-  const int sms = sm_count(current_device());
   const int heads = B * Hk * pl.nrg;
-  // total key splits: aim for ~one CTA per SM, each streaming >= 256 keys
-  int want = std::max(1, sms / std::max(1, heads));
-  want = std::min(want, std::max(1, L / 256));
+  // key splits per head: as many CTAs as run at once in a single wave (clusters of ns CTAs
+  // merge their splits through distributed shared memory; ns <= 8 portable sizes, chosen by
+  // how many such clusters the device co-schedules), each streaming >= 128 keys; cluster
+  // groups merge through the workspace
+  const int max_splits = std::max(1, L / 128);
   const int force = env_int("DSPARK_ATTN_SPLITS", 0);
-  if (force > 0) want = force;
-  int ns = std::min(want, 16);
-  if (ns > 8 && ns < 16) ns = 8;
-  int ng = (want + ns - 1) / ns;
+  int ns = 1, ng = 1;
+  if (force > 0) {
+    ns = std::min(force, 8);
+    ng = (force + ns - 1) / ns;
+  } else {
+    for (int c : {8, 6, 4, 3, 2}) {
+      if (c > max_splits) continue;
+      const int fit = max_clusters(D, nrt, pl.ks, c) / std::max(1, heads);  // clusters per head
+      if (fit < 1) continue;
+      const int g = std::max(1, std::min(fit, max_splits / c));
+      if (c * g > ns * ng) {
+        ns = c;
+        ng = g;
+      }
+    }
+  }
   int chunk = ((L + ns * ng - 1) / (ns * ng) + KT - 1) / KT * KT;
   chunk = std::max(chunk, KT);
   // drop splits that would start past the end
@@ -417,7 +566,7 @@ AttnPlan plan(int B, int Hq, int Hk, int qL, int D, int L) {
     if (ng > 1) --ng; else --ns;
   }
   pl.ns = std::max(1, ns);
-  pl.ng = std::max(1, ng);
+  pl.ng = std::max(1, std::min(ng, 32));  // the merge kernel holds one group per lane
   pl.chunk = ((L + pl.ns * pl.ng - 1) / (pl.ns * pl.ng) + KT - 1) / KT * KT;
   pl.chunk = std::max(pl.chunk, KT);
   return pl;
@@ -444,8 +593,9 @@ static int launch_attn(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) 
   dim3 block((NRT * KS + 1) * 32);
   DSPARK_CUDA_TRY(launch_ex(kern, grid, block, smem, s, pl.ns, true, p), "attn: launch");
   if (pl.ng > 1) {
-    DSPARK_CUDA_TRY(launch_ex(attn_merge_kernel<D>, dim3(p.B * p.Hk * pl.nrg), dim3(256), 0, s, 1,
-                              true, p, NRT * 16),
+    const int rows = p.B * p.Hk * pl.nrg * NRT * 16;
+    DSPARK_CUDA_TRY(launch_ex(attn_merge_kernel<D>, dim3((rows + kMergeRows - 1) / kMergeRows),
+                              dim3(kMergeRows * 32), 0, s, 1, true, p, NRT * 16),
                     "attn: merge launch");
   }
   return DSPARK_OK;
@@ -480,6 +630,7 @@ int run(AttnParams p, const AttnPlan* plan_in, cudaStream_t stream) {
   p.ns = pl.ns;
   p.ng = pl.ng;
   p.chunk = pl.chunk;
+  if (pl.ng > 32) return fail(DSPARK_ERR_UNSUPPORTED, "attn: at most 32 cluster groups (got %d)", pl.ng);
   if (pl.ng > 1 && p.ws == nullptr)
     return fail(DSPARK_ERR_ARG, "attn: this launch needs a workspace of %zu bytes",
                 workspace_bytes(pl, p.B, p.Hk, p.D));

@@ -136,6 +136,21 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// 16-byte global -> shared copy through L2 (cp.async.cg); when !valid nothing is read and the
+// 16 destination bytes are zero-filled.
+__device__ __forceinline__ void cp_async_16_zfill(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued so far has completed (the arrival
+// counts toward the barrier's expected count).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
 // ------------------------------------------------------------------ programmatic dependent launch
 
 // Block until the grids this launch depends on have completed and their writes are visible.
@@ -181,6 +196,18 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
+}
+
+// Store to shared memory of a CTA of this cluster (address from mapa_shared); asynchronous
+// for the issuing thread, ordered for readers by a later cluster barrier or release/acquire.
+__device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_dsmem_f4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
 }
 
 __device__ __forceinline__ void fence_acq_rel_cluster() {
@@ -254,10 +281,11 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
 
 // ------------------------------------------------------------------ tensor-core MMA (bf16)
 
-// D[16x8] += A[16x16] * B[16x8], bf16 operands, fp32 accumulate.
+// D[16x8] += A[16x16] * B[16x8], bf16 operands, fp32 accumulate. Register operands only (not
+// volatile), so the compiler may interleave it with the shared-memory loads of the next step.
 __device__ __forceinline__ void mma_bf16_16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2,
                                                uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])

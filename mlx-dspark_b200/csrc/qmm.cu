@@ -633,9 +633,9 @@ QmmPlan plan_st(int N, int K, int bits, int rt) {
     const int kslice = ((K + cs - 1) / cs + 511) / 512 * 512;
     if ((cs - 1) * kslice >= K) continue;
     int slots = max_slots;
-    while (slots >= 3 && st_smem_bytes(bits, mt, kslice, slots) > 227 * 1024) --slots;
+    while (slots >= 3 && st_smem_bytes(bits, mt, kslice, slots, cs) > 227 * 1024) --slots;
     if (slots < 3) continue;
-    const int smem = st_smem_bytes(bits, mt, kslice, slots);
+    const int smem = st_smem_bytes(bits, mt, kslice, slots, cs);
     int clusters = std::min(ntiles, st_max_clusters(cs, smem));
     if (force_clusters > 0) clusters = std::min(ntiles, force_clusters);
     if (clusters < 1) continue;

@@ -78,7 +78,7 @@ int tc_max_clusters(int bits, int rt, int cs, int smem);       // co-resident cl
 // Streaming engine (qmm_st.cu): geometry and launch (tile 128 rows, K % 512 == 0).
 QmmPlan plan_st(int N, int K, int bits, int rt);
 int run_st(const QmmParams& p, int epi, const QmmPlan& pl, cudaStream_t s);
-int st_smem_bytes(int bits, int rt, int kslice, int nslots);
+int st_smem_bytes(int bits, int rt, int kslice, int nslots, int cs);
 int st_max_clusters(int cs, int smem);
 
 // Geometry for [N, K] at `bits` serving up to 8*rt rows (rt = 2: M <= 16, rt = 4: M <= 32).

@@ -88,7 +88,11 @@ struct Layout {
 
 __host__ __device__ inline int x_pitch(int kslice) { return kslice * 2 + 16; }
 
-__host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslots) {
+// Rows of the split-K receive buffer: CTA c of the cluster owns rows m = c + i*cs; every CTA
+// pushes its partial rows into slot [rank][i] of the owner.
+__host__ __device__ inline int owned_rows(int rp, int cs) { return (rp + cs - 1) / cs; }
+
+__host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslots, int cs) {
   const int rp = 8 * mt;
   Layout L;
   int off = 0;
@@ -102,8 +106,8 @@ __host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslot
   L.sx = off;
   off += (kslice / 64) * rp * 4;
   off = (off + 15) & ~15;
-  L.part = off;
-  off += 2 * rp * PSTR * 4;
+  L.part = off;  // two receive buffers [cs][owned_rows][PSTR]
+  off += 2 * cs * owned_rows(rp, cs) * PSTR * 4;
   L.red = off;
   off += rp * PSTR * 4;
   L.rs = off;
@@ -139,7 +143,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                                              ~uintptr_t(1023));
   const int S = p.nslots;
   const int SS = scale_slots(BITS, S);
-  const Layout Lo = layout(BITS, MT, p.kslice, S);
+  const Layout Lo = layout(BITS, MT, p.kslice, S, p.cs);
   uint8_t* ring = smem + Lo.ring;
   uint8_t* sring = smem + Lo.sring;
   uint8_t* xs = smem + Lo.xs;
@@ -419,22 +423,33 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
       }
 
-      // ---- partial tile j -> part[j & 1] ([m][row])
+      // ---- partial tile j: push row m into receive buffer j & 1 of its owner (m % cs), slot
+      // [rank][m / cs] (local stores when cs == 1)
       const int pbuf = j & 1;
-      float* pb = part + pbuf * RP * PSTR;
-      // part[pbuf] last held tile j-2: every CTA of the cluster must be done reading it
+      const int ro = owned_rows(RP, cs);
+      // the owners' buffer pbuf last held tile j-2: every owner must be done reading it
       if (j >= 2 && ok)
         ok = mbar_wait_cluster(&freeb[pbuf], ((j - 2) >> 1) & 1, p.status, kErrWaitCluster);
+      const uint32_t pa = smem_u32(part + (pbuf * cs + rank) * ro * PSTR);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
-        const int m = mt * 8 + 2 * t4;
-        pb[m * PSTR + r0] = acc[mt][0];
-        pb[(m + 1) * PSTR + r0] = acc[mt][1];
-        pb[m * PSTR + r1] = acc[mt][2];
-        pb[(m + 1) * PSTR + r1] = acc[mt][3];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int m = mt * 8 + 2 * t4 + i;
+          const int owner = m % cs, ml = m / cs;
+          const uint32_t a0 = pa + uint32_t((ml * PSTR + r0) * 4);
+          const uint32_t a1 = pa + uint32_t((ml * PSTR + r1) * 4);
+          if (cs > 1) {
+            st_dsmem_f32(mapa_shared(a0, owner), acc[mt][i]);
+            st_dsmem_f32(mapa_shared(a1, owner), acc[mt][2 + i]);
+          } else {
+            part[(pbuf * ro + ml) * PSTR + r0] = acc[mt][i];
+            part[(pbuf * ro + ml) * PSTR + r1] = acc[mt][2 + i];
+          }
+        }
       }
       asm volatile("bar.sync 1, %0;" ::"n"(NC));
-      if (tid == 0) {  // publish to every CTA of the cluster
+      if (tid == 0) {  // publish to every owner of the cluster
         if (cs > 1) {
           fence_acq_rel_cluster();
           for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&ready[pbuf], c);
@@ -447,33 +462,33 @@ __global__ void __launch_bounds__(NTHR, 1)
     // ------------------------------------------------------------- epilogue warps
     pdl_wait();  // the epilogues read / write buffers of earlier kernels (residual, caches)
     const int etid = tid - WARP_EPI * 32;
+    const int ro = owned_rows(RP, cs);
     const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
     for (int j = 0; j < ntl; ++j) {
       const int pbuf = j & 1;
       const int t = int(blockIdx.y) + j * nclus;
-      const float* pb = part + pbuf * RP * PSTR;
+      const float* pb = part + pbuf * cs * ro * PSTR;
       if (ok) ok = mbar_wait_cluster(&ready[pbuf], (j >> 1) & 1, p.status, kErrWaitCluster);
-      const float* src = pb;
-      if (cs > 1) {
-        for (int idx = etid; idx < nmine * (TN / 4); idx += NE) {
-          const int mi = idx / (TN / 4), n4 = idx - mi * (TN / 4);
-          const int m = rank + mi * cs;
-          const uint32_t a = smem_u32(&pb[m * PSTR + n4 * 4]);
-          float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int c = 0; c < cs; ++c) {
-            const float4 v = ld_dsmem_f4(mapa_shared(a, c));
-            s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
-          }
-          *reinterpret_cast<float4*>(&red[m * PSTR + n4 * 4]) = s;
+      // sum the cs partials of each owned row in rank order (local shared memory)
+      for (int idx = etid; idx < nmine * (TN / 4); idx += NE) {
+        const int mi = idx / (TN / 4), n4 = idx - mi * (TN / 4);
+        const int m = rank + mi * cs;
+        float4 s = *reinterpret_cast<const float4*>(&pb[mi * PSTR + n4 * 4]);
+        for (int c = 1; c < cs; ++c) {
+          const float4 v = *reinterpret_cast<const float4*>(&pb[(c * ro + mi) * PSTR + n4 * 4]);
+          s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
         }
-        asm volatile("bar.sync 2, %0;" ::"n"(NE));
-        if (etid == 0)
-          for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&freeb[pbuf], c);
-        src = red;
+        *reinterpret_cast<float4*>(&red[m * PSTR + n4 * 4]) = s;
       }
-      epilogue<EPI, TN, PSTR>(p, src, rank, cs, t, t * TN, NWE, WARP_EPI);
-      asm volatile("bar.sync 2, %0;" ::"n"(NE));  // red (or part) reads done
-      if (cs == 1 && etid == 0) mbar_arrive(&freeb[pbuf]);
+      asm volatile("bar.sync 2, %0;" ::"n"(NE));
+      if (etid == 0) {  // every CTA may push its next partial into this buffer again
+        if (cs > 1)
+          for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&freeb[pbuf], c);
+        else
+          mbar_arrive(&freeb[pbuf]);
+      }
+      epilogue<EPI, TN, PSTR>(p, red, rank, cs, t, t * TN, NWE, WARP_EPI);
+      asm volatile("bar.sync 2, %0;" ::"n"(NE));  // red reads done
     }
   }
 
@@ -485,8 +500,8 @@ __global__ void __launch_bounds__(NTHR, 1)
 
 // ----------------------------------------------------------------------------- host side
 
-int st_smem_bytes(int bits, int rt, int kslice, int nslots) {
-  return st::layout(bits, rt, kslice, nslots).total;
+int st_smem_bytes(int bits, int rt, int kslice, int nslots, int cs) {
+  return st::layout(bits, rt, kslice, nslots, cs).total;
 }
 
 template <typename Kern>
@@ -538,7 +553,7 @@ int st_max_clusters(int cs, int smem) {
 template <int BITS, int MT, int EPI>
 static int launch_st(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream) {
   auto kern = st::qmm_st_kernel<BITS, MT, EPI>;
-  const int smem = st::layout(BITS, MT, pl.kslice, pl.nslots).total;
+  const int smem = st::layout(BITS, MT, pl.kslice, pl.nslots, pl.cs).total;
   static bool configured = false;
   if (!configured) {
     DSPARK_CUDA_TRY(configure_st(kern), "qmm_st: set smem / cluster attributes");
