@@ -93,6 +93,22 @@ int dspark_verify_attn(const void* q, const int64_t q_strides[3], const void* k,
                        const int64_t o_strides[3], void* workspace, size_t ws_bytes,
                        void* stream);
 
+/* dspark_verify_attn for callers that cannot allocate device memory (no workspace argument).
+ * This entry point has no counterpart in the reference: it exists for code that is being
+ * captured into a CUDA graph (where cudaMalloc is not allowed), for plugins whose host runtime
+ * owns all device memory and passes only input and output buffers, and for paths that must not
+ * let an allocation or a cudaFree stall the device. Its scratch is a static 4 MiB device array
+ * per GPU (held until exit); shapes whose workspace (dspark_verify_attn_workspace) exceeds it
+ * fail with DSPARK_ERR_UNSUPPORTED. The first call on a device looks up that array's device
+ * address, so make it before any stream capture. Calls share the array: calls that overlap on
+ * the GPU race. Nothing is allocated and nothing needs clearing between calls. */
+int dspark_verify_attn_noalloc(const void* q, const int64_t q_strides[3], const void* k,
+                               const int64_t k_strides[3], const void* v,
+                               const int64_t v_strides[3], int B, int Hq, int Hk, int qL, int D,
+                               int L, const int32_t* kv_len, float scale, int causal,
+                               const uint32_t* tree_anc, void* out, const int64_t o_strides[3],
+                               void* stream);
+
 /* Launch geometry of dspark_verify_attn for a shape (mirrors multirow_attn.plan,
  * src/mlx_dspark/multirow_attn.py:204-220): out[0] 16-row tiles per CTA, out[1] warps
  * splitting each K/V tile, out[2] row groups, out[3] key splits merged in a cluster, out[4]

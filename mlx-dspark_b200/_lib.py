@@ -75,6 +75,8 @@ _SIGS = {
     "dspark_qmm_plan": (i32, [i32, i32, i32, P_int, P_int, P_int, P_int]),
     "dspark_verify_attn": (i32, [vp, P_i64, vp, P_i64, vp, P_i64, i32, i32, i32, i32, i32, i32,
                                  vp, f32, i32, vp, vp, P_i64, vp, sz, vp]),
+    "dspark_verify_attn_noalloc": (i32, [vp, P_i64, vp, P_i64, vp, P_i64, i32, i32, i32, i32, i32,
+                                         i32, vp, f32, i32, vp, vp, P_i64, vp]),
     "dspark_verify_attn_workspace": (sz, [i32, i32, i32, i32, i32, i32]),
     "dspark_verify_attn_plan": (i32, [i32, i32, i32, i32, i32, i32, P_int]),
     "dspark_verify_attn_ragged": (i32, [vp, i64, i64, vp, i64, i64, vp, i64, i64, vp, vp, vp, vp,
