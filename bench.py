@@ -348,6 +348,18 @@ def _qmm_bytes(n, k, m, bits):
     return n * k * bits // 8 + n * (k // 64) * 4 + m * k * 2 + m * n * 2
 
 
+def _profiled_traffic():
+    """DRAM bytes (read + write) per launch of the roofline kernel, from the committed ncu
+    summary of the same kernel and shape (profiles/qmm_st_gate_up_4bit_m16.md)."""
+    import re
+
+    f = ROOT / "profiles" / "qmm_st_gate_up_4bit_m16.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic per launch\) \| ([\d,]+) bytes", f.read_text())
+    return int(m.group(1).replace(",", "")) if m else None
+
+
 def roofline(t, dev, pk) -> dict:
     """Dominant kernel: the gate/up QMM (N = 24576, K = 4096, 16 rows). Back-to-back launches
     over all 36 layers' weights (2 GB, no L2 reuse), CUDA events on the launching stream."""
@@ -367,13 +379,9 @@ def roofline(t, dev, pk) -> dict:
     per = _graph_time(burst, 10, dev) / len(ws)
     nbytes = _qmm_bytes(2 * cfg.intermediate, cfg.hidden, ROWS, cfg.bits)
     ach = nbytes / per / 1e9
-    traffic = None
-    tf = ROOT / "profiles" / "qmm_gate_up_traffic.json"
-    if tf.exists():
-        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
-    return {"kernel": "dspark qmm_kernel (gate/up 24576x4096, 4-bit, 16 rows)", "bound": "hbm",
+    return {"kernel": "qmm_st_kernel<4, 2, EPI> (gate/up 24576x4096, 4-bit, 16 rows)", "bound": "hbm",
             "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-            "frac": round(ach / pk["hbm_gbs"], 3), "traffic": traffic,
+            "frac": round(ach / pk["hbm_gbs"], 3), "traffic": _profiled_traffic(),
             "algorithmic_bytes_per_launch": nbytes, "us_per_launch": round(per * 1e6, 2),
             "peak_source": pk["src"]}
 

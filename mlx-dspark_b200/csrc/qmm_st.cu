@@ -83,7 +83,7 @@ __host__ __device__ inline int scale_slots(int bits, int nslots) {
 }
 
 struct Layout {
-  int ring, sring, xs, sx, part, red, rs, bars, total;
+  int ring, sring, xs, nw, sx, part, red, rs, bars, total;
 };
 
 __host__ __device__ inline int x_pitch(int kslice) { return kslice * 2 + 16; }
@@ -103,6 +103,8 @@ __host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslot
   L.xs = off;
   off += rp * x_pitch(kslice);
   off = (off + 15) & ~15;
+  L.nw = off;  // the K slice of the RMSNorm weight (fused-norm prologue)
+  off += kslice * 2;
   L.sx = off;
   off += (kslice / 64) * rp * 4;
   off = (off + 15) & ~15;
@@ -114,7 +116,7 @@ __host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslot
   off += 32 * 4;
   off = (off + 15) & ~15;
   L.bars = off;
-  off += (2 * nslots + 4) * 8;
+  off += (2 * nslots + 5) * 8;
   L.total = off + 1024;  // slack to align the dynamic base to 1024 bytes
   return L;
 }
@@ -155,6 +157,8 @@ __global__ void __launch_bounds__(NTHR, 1)
   uint64_t* empty = full + S;
   uint64_t* ready = empty + S;   // [2] every cluster CTA published its partial tile
   uint64_t* freeb = ready + 2;   // [2] every cluster CTA finished reading this CTA's partial
+  uint64_t* xbar = freeb + 2;    // the x slice (and norm weights) landed
+  uint8_t* nws = smem + Lo.nw;
 
   const int cs = p.cs;
   const int rank = blockIdx.x;
@@ -165,7 +169,6 @@ __global__ void __launch_bounds__(NTHR, 1)
   const int kvalid = min(p.kslice, p.K - kbase);
   const int nsb = (kvalid + KBLK - 1) / KBLK;  // scale blocks per tile (K % 512 == 0)
   const int nst = nsb * SPS;                    // stages per tile
-  const int gslice = p.kslice / 64;
   const int XP = x_pitch(p.kslice);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
@@ -179,6 +182,7 @@ __global__ void __launch_bounds__(NTHR, 1)
       mbar_init(&ready[i], cs);
       mbar_init(&freeb[i], cs);
     }
+    mbar_init(xbar, 1);
     fence_mbar_init();
   }
   if (cs > 1) cluster_sync_all(); else __syncthreads();  // peers' barriers exist before use
@@ -222,7 +226,23 @@ __global__ void __launch_bounds__(NTHR, 1)
   } else if (warp < NWC) {
     // ------------------------------------------------------------- consumer warps
     pdl_wait();  // x (and the RMSNorm statistics) come from the previous kernel
-    if (p.norm_w != nullptr) {
+    const bool nrm = p.norm_w != nullptr;
+    const int chunks = p.kslice / 8;
+    const int vchunks = kvalid / 8;
+    // the K slice of x lands by bulk copies, one per row (and one for the norm weights), all in
+    // flight at once; rows past M are zeroed meanwhile
+    if (tid == 0) {
+      const uint32_t bytes = uint32_t(kvalid) * 2;
+      mbar_arrive_expect_tx(xbar, bytes * uint32_t(p.M + (nrm ? 1 : 0)));
+      for (int m = 0; m < p.M; ++m)
+        bulk_load(xs + m * XP, p.x + (size_t)m * p.ldx + kbase, bytes, xbar);
+      if (nrm) bulk_load(nws, p.norm_w + kbase, bytes, xbar);
+    }
+    for (int idx = tid; idx < (RP - p.M) * chunks; idx += NC) {
+      const int m = p.M + idx / chunks, c = idx % chunks;
+      *reinterpret_cast<uint4*>(xs + m * XP + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (nrm) {
       for (int m = warp; m < RP; m += NWC) {
         float ss = 0.f;
         if (m < p.M)
@@ -231,74 +251,52 @@ __global__ void __launch_bounds__(NTHR, 1)
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         if (lane == 0) rsm[m] = m < p.M ? rsqrtf(ss / float(p.K) + p.eps) : 0.f;
       }
-      asm volatile("bar.sync 1, %0;" ::"n"(NC));
     }
-    // stage the K slice of x: row m at xs + m*XP, k permuted inside each 8-block (4-bit:
-    // 0,4,1,5,2,6,3,7) or 4-block (8-bit: 0,2,1,3); zero rows beyond M and k beyond the slice
-    {
-      const int chunks = p.kslice / 8;
-      const int total = RP * chunks;
-      constexpr int XB = 4;
-      const bool nrm = p.norm_w != nullptr;
-      for (int base = tid; base < total; base += NC * XB) {
-        uint4 v[XB], w[XB];
+    asm volatile("bar.sync 1, %0;" ::"n"(NC));
+    if (ok) ok = mbar_wait(xbar, 0, p.status, kErrWaitFull);
+    // in place: apply the norm (x * rs * w rounded to bf16) and permute k inside each 8-block
+    // (4-bit: 0,4,1,5,2,6,3,7) or 4-block (8-bit: 0,2,1,3) as the magic extraction orders weights
+    for (int idx = tid; idx < p.M * vchunks; idx += NC) {
+      const int m = idx / vchunks, c = idx - m * vchunks;
+      uint4 vv = *reinterpret_cast<const uint4*>(xs + m * XP + c * 16);
+      if (nrm) {
+        const float r = rsm[m];
+        const uint4 w = *reinterpret_cast<const uint4*>(nws + c * 16);
+        uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
+        const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w);
 #pragma unroll
-        for (int u = 0; u < XB; ++u) {
-          const int idx = base + u * NC;
-          const int m = idx / chunks, c = idx - m * chunks;
-          v[u] = make_uint4(0u, 0u, 0u, 0u);
-          w[u] = v[u];
-          if (idx < total && m < p.M && c * 8 < kvalid) {
-            const int k = kbase + c * 8;
-            v[u] = __ldcg(reinterpret_cast<const uint4*>(p.x + (size_t)m * p.ldx + k));
-            if (nrm) w[u] = __ldg(reinterpret_cast<const uint4*>(p.norm_w + k));
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < XB; ++u) {
-          const int idx = base + u * NC;
-          if (idx >= total) break;
-          const int m = idx / chunks, c = idx - m * chunks;
-          uint4 vv = v[u];
-          if (nrm && m < p.M) {
-            const float r = rsm[m];
-            uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
-            const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w[u]);
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
-                                  bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
-          }
-          uint4 o;
-          if (BITS == 4) {
-            o.x = __byte_perm(vv.x, vv.z, 0x5410);
-            o.y = __byte_perm(vv.x, vv.z, 0x7632);
-            o.z = __byte_perm(vv.y, vv.w, 0x5410);
-            o.w = __byte_perm(vv.y, vv.w, 0x7632);
-          } else {
-            o.x = __byte_perm(vv.x, vv.y, 0x5410);
-            o.y = __byte_perm(vv.x, vv.y, 0x7632);
-            o.z = __byte_perm(vv.z, vv.w, 0x5410);
-            o.w = __byte_perm(vv.z, vv.w, 0x7632);
-          }
-          *reinterpret_cast<uint4*>(xs + m * XP + c * 16) = o;
-        }
+        for (int e = 0; e < 4; ++e)
+          pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
+                              bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
       }
-      asm volatile("bar.sync 1, %0;" ::"n"(NC));
-      // per-group sums of the staged (rounded) x, summed in a fixed order
-      for (int idx = tid; idx < RP * gslice; idx += NC) {
-        const int g = idx / RP, m = idx - g * RP;
-        float s = 0.f;
-#pragma unroll
-        for (int b = 0; b < 8; ++b) {
-          const uint4 q = *reinterpret_cast<const uint4*>(xs + m * XP + (g * 8 + b) * 16);
-          s += (bf16_lo(q.x) + bf16_hi(q.x)) + (bf16_lo(q.y) + bf16_hi(q.y)) +
-               (bf16_lo(q.z) + bf16_hi(q.z)) + (bf16_lo(q.w) + bf16_hi(q.w));
-        }
-        sx[g * RP + m] = s;
+      uint4 o;
+      if (BITS == 4) {
+        o.x = __byte_perm(vv.x, vv.z, 0x5410);
+        o.y = __byte_perm(vv.x, vv.z, 0x7632);
+        o.z = __byte_perm(vv.y, vv.w, 0x5410);
+        o.w = __byte_perm(vv.y, vv.w, 0x7632);
+      } else {
+        o.x = __byte_perm(vv.x, vv.y, 0x5410);
+        o.y = __byte_perm(vv.x, vv.y, 0x7632);
+        o.z = __byte_perm(vv.z, vv.w, 0x5410);
+        o.w = __byte_perm(vv.z, vv.w, 0x7632);
       }
-      asm volatile("bar.sync 1, %0;" ::"n"(NC));
+      *reinterpret_cast<uint4*>(xs + m * XP + c * 16) = o;
     }
+    asm volatile("bar.sync 1, %0;" ::"n"(NC));
+    // per-group sums of the staged (rounded) x, summed in a fixed order
+    for (int idx = tid; idx < RP * (kvalid / 64); idx += NC) {
+      const int g = idx / RP, m = idx - g * RP;
+      float s = 0.f;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        const uint4 q = *reinterpret_cast<const uint4*>(xs + m * XP + (g * 8 + b) * 16);
+        s += (bf16_lo(q.x) + bf16_hi(q.x)) + (bf16_lo(q.y) + bf16_hi(q.y)) +
+             (bf16_lo(q.z) + bf16_hi(q.z)) + (bf16_lo(q.w) + bf16_hi(q.w));
+      }
+      sx[g * RP + m] = s;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(NC));
 
     const int g8 = lane >> 2, t4 = lane & 3;
     const int r0 = warp * 16 + row_perm<BITS>(g8), r1 = r0 + 8;
