@@ -177,6 +177,15 @@ __device__ __forceinline__ void cluster_sync_all() {
           : "memory");
 }
 
+// Split cluster barrier: every thread arrives once (after its CTA's barriers are initialized)
+// and waits before its first access to another CTA's shared memory or barriers.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
@@ -264,6 +273,12 @@ __device__ __forceinline__ void fma2(float& a0, float& a1, float b0, float b1, f
 }
 
 // ------------------------------------------------------------------ shared-memory vector loads
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
 
 __device__ __forceinline__ uint2 lds64(uint32_t addr) {
   uint2 v;

@@ -622,6 +622,7 @@ QmmPlan plan_st(int N, int K, int bits, int rt) {
   const int force_cs = env_int("DSPARK_QMM_CS", 0);
   const int max_slots = std::max(3, env_int("DSPARK_QMM_SLOTS", 8));
   const int force_clusters = env_int("DSPARK_QMM_CLUSTERS", 0);
+  pl.tcmma = env_int("DSPARK_QMM_ST_TC", 0) != 0;  // tcgen05 consumers measured slower
   const double hbm = env_int("DSPARK_QMM_HBM_GBS", 6500) * 1e9;
   const double sm_cap = env_int("DSPARK_QMM_SM_MBS", bits == 8 ? 60000 : 40000) * 1e6;
   const double t_tile = env_int("DSPARK_QMM_TILE_NS", 300) * 1e-9;
@@ -633,9 +634,9 @@ QmmPlan plan_st(int N, int K, int bits, int rt) {
     const int kslice = ((K + cs - 1) / cs + 511) / 512 * 512;
     if ((cs - 1) * kslice >= K) continue;
     int slots = max_slots;
-    while (slots >= 3 && st_smem_bytes(bits, mt, kslice, slots, cs) > 227 * 1024) --slots;
+    while (slots >= 3 && st_smem_bytes(bits, mt, kslice, slots, cs, pl.tcmma) > 227 * 1024) --slots;
     if (slots < 3) continue;
-    const int smem = st_smem_bytes(bits, mt, kslice, slots, cs);
+    const int smem = st_smem_bytes(bits, mt, kslice, slots, cs, pl.tcmma);
     int clusters = std::min(ntiles, st_max_clusters(cs, smem));
     if (force_clusters > 0) clusters = std::min(ntiles, force_clusters);
     if (clusters < 1) continue;

@@ -61,6 +61,7 @@ struct QmmPlan {
   int engine = 2;   // 2: streaming (qmm_st.cu); 1: tcgen05 (TMEM operands, qmm_tc.cu);
                     // 0: mma.sync per-tile CTAs (qmm.cu)
   int clusters = 0; // tcgen05: persistent clusters walking the tiles (0: one per cs SMs)
+  bool tcmma = false; // streaming engine: tcgen05 MMA consumers (else mma.sync consumers)
 };
 
 // TMA descriptors of the packed weights (128-byte swizzle, boxes of 32 words x tn rows) and,
@@ -78,7 +79,7 @@ int tc_max_clusters(int bits, int rt, int cs, int smem);       // co-resident cl
 // Streaming engine (qmm_st.cu): geometry and launch (tile 128 rows, K % 512 == 0).
 QmmPlan plan_st(int N, int K, int bits, int rt);
 int run_st(const QmmParams& p, int epi, const QmmPlan& pl, cudaStream_t s);
-int st_smem_bytes(int bits, int rt, int kslice, int nslots, int cs);
+int st_smem_bytes(int bits, int rt, int kslice, int nslots, int cs, bool tc);
 int st_max_clusters(int cs, int smem);
 
 // Geometry for [N, K] at `bits` serving up to 8*rt rows (rt = 2: M <= 16, rt = 4: M <= 32).

@@ -39,6 +39,7 @@
 #include "host_common.h"
 #include "qmm.h"
 #include "qmm_epilogue.cuh"
+#include "tcgen05.cuh"
 
 namespace dspark {
 namespace qmm {
@@ -56,6 +57,8 @@ constexpr int PSTR = TN + 4;            // fp32 row stride of partial / reduced 
 constexpr int STG = TN * 128;           // one stage: a 128-byte-wide box of 128 rows
 constexpr int SCB = TN * 16;            // 8 groups of bf16 scales (or biases) for 128 rows
 constexpr int KBLK = 512;               // k per scale block (8 groups)
+constexpr int kTcBuf = 4;               // tcgen05 A/D buffer pairs per warpgroup, at most
+constexpr int kTcBars = 2 * kTcBuf;     // their completion barriers, two warpgroups
 
 template <int BITS>
 struct Tr;
@@ -83,7 +86,7 @@ __host__ __device__ inline int scale_slots(int bits, int nslots) {
 }
 
 struct Layout {
-  int ring, sring, xs, nw, sx, part, red, rs, bars, total;
+  int ring, sring, xs, nw, sx, part, red, xch, rs, bars, total;
 };
 
 __host__ __device__ inline int x_pitch(int kslice) { return kslice * 2 + 16; }
@@ -92,7 +95,10 @@ __host__ __device__ inline int x_pitch(int kslice) { return kslice * 2 + 16; }
 // pushes its partial rows into slot [rank][i] of the owner.
 __host__ __device__ inline int owned_rows(int rp, int cs) { return (rp + cs - 1) / cs; }
 
-__host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslots, int cs) {
+// x rows the tcgen05 MMA reads as its N dimension (zero padded): 16 or 32
+__host__ __device__ inline int tc_rows(int mt) { return mt <= 2 ? 16 : 32; }
+
+__host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslots, int cs, bool tc) {
   const int rp = 8 * mt;
   Layout L;
   int off = 0;
@@ -100,8 +106,8 @@ __host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslot
   off += nslots * STG;
   L.sring = off;
   off += scale_slots(bits, nslots) * 2 * SCB;
-  L.xs = off;
-  off += rp * x_pitch(kslice);
+  L.xs = off;  // row-major rows of XP bytes (mma.sync), or 8-k blocks of tc_rows rows (tcgen05)
+  off += tc ? (kslice / 8) * tc_rows(mt) * 16 : rp * x_pitch(kslice);
   off = (off + 15) & ~15;
   L.nw = off;  // the K slice of the RMSNorm weight (fused-norm prologue)
   off += kslice * 2;
@@ -112,11 +118,13 @@ __host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslot
   off += 2 * cs * owned_rows(rp, cs) * PSTR * 4;
   L.red = off;
   off += rp * PSTR * 4;
+  L.xch = off;  // k-half exchange: 2 row groups x mt x 4 accumulators x 128 threads
+  off += 2 * mt * 4 * 128 * 4;
   L.rs = off;
   off += 32 * 4;
   off = (off + 15) & ~15;
   L.bars = off;
-  off += (2 * nslots + 5) * 8;
+  off += (2 * nslots + 5 + kTcBars) * 8 + 16;  // + tcgen05 completion barriers, TMEM slot
   L.total = off + 1024;  // slack to align the dynamic base to 1024 bytes
   return L;
 }
@@ -130,7 +138,224 @@ __device__ __forceinline__ int row_perm(int g) {
   return BITS == 4 ? (((g & 3) << 1) | (g >> 2)) : (((g & 1) << 2) | (g >> 1));
 }
 
-template <int BITS, int MT, int EPI>
+// tcgen05 consumers (two warpgroups of 4 warps; warpgroup wg takes the groups gi = wg, wg + 2, ...
+// of every stage). Thread t of a warpgroup owns tile row t == TMEM lane t: it dequantizes its
+// row's 64 weights of a group into registers and writes them to an A buffer in tensor memory
+// (one tcgen05.st); after a warpgroup barrier one elected thread issues the group's MMAs
+// (M = 128 rows, N = the staged x rows, K = 16 per instruction; x is read by the tensor core from
+// shared memory) into a D buffer and commits them to an mbarrier. With two A/D buffer pairs the
+// thread folds group q-2's product (acc += scale*P + (bias - MAGIC*scale)*sum_k x, in fp32, in
+// issue order) while the tensor core works on group q-1. The k halves of the two warpgroups are
+// summed at the tile end (warpgroup 0 + warpgroup 1) and pushed like the mma.sync partials.
+template <int BITS, int MT>
+__device__ __forceinline__ void consume_tc(const QmmParams& p, uint8_t* ring, uint8_t* sring,
+                                           uint8_t* xs, const float* sx, float* part, float* xch,
+                                           uint64_t* full, uint64_t* empty, uint64_t* ready,
+                                           uint64_t* freeb, uint64_t* tcbar, uint32_t tmem,
+                                           int ntl, int nsb, int nst, int S, int SS, int cs,
+                                           int rank, bool& ok) {
+  constexpr int RP = 8 * MT;
+  constexpr int NM = MT <= 2 ? 16 : 32;            // MMA N
+  constexpr int GPS = Tr<BITS>::GPS;
+  constexpr int SPS = Tr<BITS>::SPS;
+  constexpr int GH = GPS / 2;                      // groups per warpgroup per stage
+  constexpr float MAGIC = Tr<BITS>::MAGIC;
+  constexpr int ACOLS = BITS == 4 ? 32 : 64;       // TMEM columns of one group's A
+  // A/D buffer pairs per warpgroup. A warpgroup takes exactly 4 groups per scale block
+  // (SPS * GH == 4), so with NB dividing 4 the buffer of every group is a compile-time index.
+  constexpr int NB = BITS == 4 ? 4 : 2;
+  static_assert(SPS * GH == 4 && 4 % NB == 0, "buffer rotation");
+  constexpr int PER = NB * ACOLS + NB * NM;        // TMEM columns per warpgroup
+  constexpr uint32_t IDESC = tcg::idesc_bf16(NM);
+  static_assert(2 * PER <= 512, "TMEM budget");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = threadIdx.x;
+  const int wg = warp >> 2, wq = warp & 3;
+  const int row = wq * 32 + lane;                  // tile row == TMEM lane
+  const uint32_t lane_off = uint32_t(wq * 32) << 16;
+  const uint32_t ta = tmem + uint32_t(wg * PER) + lane_off;   // A buffers
+  const uint32_t td = ta + NB * ACOLS;                        // D buffers
+  const uint64_t bd0 = tcg::smem_desc(smem_u32(xs), NM * 16, 128);
+  static_assert(NB <= kTcBuf, "completion barriers per warpgroup");
+  uint64_t* mdone = tcbar + wg * kTcBuf;
+  const uint32_t ring_a = smem_u32(ring);
+  const uint32_t sring_a = smem_u32(sring);
+  const int nclus = gridDim.y;
+  int q = 0;  // groups this warpgroup has issued (continuous over tiles: barrier phases)
+
+  for (int j = 0; j < ntl; ++j) {
+    float acc[RP];
+#pragma unroll
+    for (int m = 0; m < RP; ++m) acc[m] = 0.f;
+    const int q0 = q;
+    // fold state of the buffers: scale, bias - MAGIC*scale, group index (compile-time indexed)
+    float fs[NB], fc[NB];
+    int fg[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      fs[b] = 0.f;
+      fc[b] = 0.f;
+      fg[b] = 0;
+    }
+    auto fold = [&](int qq, int b) {  // b == qq % NB, a compile-time constant at every call
+      // the tensor core always finishes (its operands are local): wait even after a failure
+      mbar_wait(&mdone[b], (qq / NB) & 1, p.status, kErrWaitMma);
+      tcg::tc_fence_after();
+      float d[NM];
+      tcg::tmem_ld16(td + uint32_t(b * NM), d);
+      if (NM == 32) tcg::tmem_ld16(td + uint32_t(b * NM + 16), d + 16);
+      tcg::tmem_wait_ld();
+      const float s = fs[b], c = fc[b];
+      const float* X = sx + fg[b] * RP;
+#pragma unroll
+      for (int m = 0; m < RP; m += 4) {
+        const float4 x4 = *reinterpret_cast<const float4*>(X + m);
+        fma2(acc[m], acc[m + 1], c, c, x4.x, x4.y);
+        fma2(acc[m + 2], acc[m + 3], c, c, x4.z, x4.w);
+        fma2(acc[m], acc[m + 1], s, s, d[m], d[m + 1]);
+        fma2(acc[m + 2], acc[m + 3], s, s, d[m + 2], d[m + 3]);
+      }
+    };
+
+    for (int sb = 0; sb < nsb; ++sb) {
+      uint4 sv4 = make_uint4(0u, 0u, 0u, 0u), bv4 = sv4;
+#pragma unroll
+      for (int si = 0; si < SPS; ++si) {
+        const int st = sb * SPS + si;
+        const int g = j * nst + st;
+        const int slot = g % S;
+        if (ok) ok = mbar_wait(&full[slot], (g / S) & 1, p.status, kErrWaitFull);
+        if (si == 0) {  // this row's scales / biases of the block's 8 groups
+          const uint32_t sa = sring_a + uint32_t(((j * nsb + sb) % SS) * 2 * SCB) + uint32_t(row * 16);
+          sv4 = lds128(sa);
+          bv4 = lds128(sa + SCB);
+        }
+        const uint32_t wrow = ring_a + uint32_t(slot * STG + row * 128);
+#pragma unroll
+        for (int gg = 0; gg < GH; ++gg) {
+          const int gi = wg + 2 * gg;          // group inside the stage
+          const int gl = st * GPS + gi;        // group inside the K slice
+          const int gb = si * GPS + gi;        // group inside the scale block
+          // this row's scale and bias of the group (word gb/2 of the block, selected by value)
+          const int wsel = gb >> 1;
+          const uint32_t sw = wsel == 0 ? sv4.x : wsel == 1 ? sv4.y : wsel == 2 ? sv4.z : sv4.w;
+          const uint32_t bw = wsel == 0 ? bv4.x : wsel == 1 ? bv4.y : wsel == 2 ? bv4.z : bv4.w;
+          const float sv = (gb & 1) ? bf16_hi(sw) : bf16_lo(sw);
+          const float cv = ((gb & 1) ? bf16_hi(bw) : bf16_lo(bw)) - MAGIC * sv;
+          const int b = (si * GH + gg) % NB;  // == q % NB (q advances by 4 per scale block)
+          // the row's packed words of the group (8 for 4-bit, 16 for 8-bit)
+          constexpr int NWD = BITS == 4 ? 8 : 16;
+          uint32_t wd[NWD];
+#pragma unroll
+          for (int h = 0; h < NWD / 4; ++h) {
+            const uint4 v = lds128(wrow + uint32_t((((NWD / 4 * gi + h) ^ (row & 7))) << 4));
+            wd[4 * h + 0] = v.x; wd[4 * h + 1] = v.y; wd[4 * h + 2] = v.z; wd[4 * h + 3] = v.w;
+          }
+          // buffer b held group q-NB: fold it (if it belongs to this tile) before reuse
+          if (q - NB >= q0) fold(q - NB, b);
+          // dequantize into the A buffer (magic-exponent bf16, exact)
+          uint32_t r[32];
+          if (BITS == 4) {
+            // word 2u+h, nibbles e and e+4 -> column 8u + 4h + e
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  r[8 * u + 4 * h + e] = lop3_and_or(wd[2 * u + h] >> (4 * e), 0x000F000Fu, 0x43004300u);
+            tcg::tmem_st32(ta + uint32_t(b * ACOLS), r);
+          } else {
+            // word 4u+h -> columns 8u + 2h, +1 of the low plane, then of the high plane
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                r[8 * u + 2 * h] = lop3_and_or(wd[4 * u + h], 0x000F000Fu, 0x43004300u);
+                r[8 * u + 2 * h + 1] = lop3_and_or(wd[4 * u + h] >> 8, 0x000F000Fu, 0x43004300u);
+              }
+            tcg::tmem_st32(ta + uint32_t(b * ACOLS), r);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                r[8 * u + 2 * h] = lop3_and_or(wd[4 * u + h] >> 1, 0x00780078u, 0x43804380u);
+                r[8 * u + 2 * h + 1] = lop3_and_or(wd[4 * u + h] >> 9, 0x00780078u, 0x43804380u);
+              }
+            tcg::tmem_st32(ta + uint32_t(b * ACOLS + 32), r);
+          }
+          tcg::tmem_wait_st();
+          tcg::tc_fence_before();
+          asm volatile("bar.sync %0, 128;" ::"r"(3 + wg));
+          if (wq == 0) {
+            if (tcg::elect_one()) {
+              tcg::tc_fence_after();
+              const uint32_t dd = td - lane_off + uint32_t(b * NM);
+              const uint32_t aa = ta - lane_off + uint32_t(b * ACOLS);
+#pragma unroll
+              for (int s = 0; s < 4; ++s) {
+                const uint64_t bdesc = bd0 + uint64_t((gl * 8 + 2 * s) * NM);
+                tcg::umma_ts(dd, aa + 8 * s, bdesc, IDESC, s > 0 ? 1u : 0u);
+                if (BITS == 8) tcg::umma_ts(dd, aa + 32 + 8 * s, bdesc, IDESC, 1u);
+              }
+              tcg::umma_commit(&mdone[b]);
+            }
+            __syncwarp();
+          }
+          fs[b] = sv;
+          fc[b] = cv;
+          fg[b] = gl;
+          ++q;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+    }
+    // the tile's last groups (q is a multiple of 4 here, so group q - NB + i sits in buffer i)
+#pragma unroll
+    for (int i = 0; i < NB; ++i)
+      if (q - NB + i >= q0) fold(q - NB + i, i);
+
+    // ---- the warpgroups' k halves meet (fixed order: warpgroup 0 + warpgroup 1)
+    if (wg == 1) {
+#pragma unroll
+      for (int m = 0; m < RP; ++m) xch[m * 128 + row] = acc[m];
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(NC));
+    const int pbuf = j & 1;
+    const int ro = owned_rows(RP, cs);
+    if (j == 0 && cs > 1) cluster_wait();  // peers' buffers and barriers exist
+    // the owners' buffer pbuf last held tile j-2: every owner must be done reading it
+    if (j >= 2 && ok)
+      ok = mbar_wait_cluster(&freeb[pbuf], ((j - 2) >> 1) & 1, p.status, kErrWaitCluster);
+    if (wg == 0) {
+      const uint32_t pa = smem_u32(part + (pbuf * cs + rank) * ro * PSTR);
+#pragma unroll
+      for (int m = 0; m < RP; ++m) {
+        const float v = acc[m] + xch[m * 128 + row];
+        const int owner = m % cs, ml = m / cs;
+        if (cs > 1)
+          st_dsmem_f32(mapa_shared(pa + uint32_t((ml * PSTR + row) * 4), owner), v);
+        else
+          part[(pbuf * ro + ml) * PSTR + row] = v;
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(NC));  // pushes issued; the exchange buffer is free
+    if (warp == 0 && lane < cs) {
+      if (cs > 1) {
+        fence_acq_rel_cluster();
+        mbar_arrive_cluster(&ready[pbuf], lane);
+      } else {
+        mbar_arrive(&ready[pbuf]);
+      }
+    }
+    (void)nclus;
+    (void)tid;
+  }
+  if (ntl == 0 && cs > 1) cluster_wait();
+}
+
+template <int BITS, int MT, int EPI, bool TC>
 __global__ void __launch_bounds__(NTHR, 1)
     qmm_st_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                   const __grid_constant__ CUtensorMap bmap, const QmmParams p) {
@@ -145,7 +370,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                                              ~uintptr_t(1023));
   const int S = p.nslots;
   const int SS = scale_slots(BITS, S);
-  const Layout Lo = layout(BITS, MT, p.kslice, S, p.cs);
+  const Layout Lo = layout(BITS, MT, p.kslice, S, p.cs, TC);
   uint8_t* ring = smem + Lo.ring;
   uint8_t* sring = smem + Lo.sring;
   uint8_t* xs = smem + Lo.xs;
@@ -153,11 +378,14 @@ __global__ void __launch_bounds__(NTHR, 1)
   float* part = reinterpret_cast<float*>(smem + Lo.part);
   float* red = reinterpret_cast<float*>(smem + Lo.red);
   float* rsm = reinterpret_cast<float*>(smem + Lo.rs);
+  float* xch = reinterpret_cast<float*>(smem + Lo.xch);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lo.bars);
   uint64_t* empty = full + S;
   uint64_t* ready = empty + S;   // [2] every cluster CTA published its partial tile
   uint64_t* freeb = ready + 2;   // [2] every cluster CTA finished reading this CTA's partial
   uint64_t* xbar = freeb + 2;    // the x slice (and norm weights) landed
+  uint64_t* tcbar = xbar + 1;    // [2 warpgroups][kTcBuf buffers] tcgen05 MMA completion
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tcbar + kTcBars);
   uint8_t* nws = smem + Lo.nw;
 
   const int cs = p.cs;
@@ -183,9 +411,18 @@ __global__ void __launch_bounds__(NTHR, 1)
       mbar_init(&freeb[i], cs);
     }
     mbar_init(xbar, 1);
+    for (int i = 0; i < kTcBars; ++i) mbar_init(&tcbar[i], 1);
     fence_mbar_init();
   }
-  if (cs > 1) cluster_sync_all(); else __syncthreads();  // peers' barriers exist before use
+  if constexpr (TC) {
+    if (warp == 0) tcg::tmem_alloc(tmem_slot, 512);
+    tcg::tc_fence_before();
+  }
+  __syncthreads();  // this CTA's barriers exist; the producer may start at once
+  if constexpr (TC) tcg::tc_fence_after();
+  // peers touch this CTA's barriers only after the cluster barrier completes: every thread
+  // arrives now and waits right before its first remote access
+  if (cs > 1) cluster_arrive();
   pdl_launch_dependents();
 
   bool ok = true;  // false once a wait on another agent ran out: drain without waiting
@@ -223,24 +460,46 @@ __global__ void __launch_bounds__(NTHR, 1)
         mbar_wait(&full[g % S], (g / S) & 1, p.status, kErrWaitFull);
     }
     __syncwarp();
+    if (cs > 1) cluster_wait();
   } else if (warp < NWC) {
     // ------------------------------------------------------------- consumer warps
     pdl_wait();  // x (and the RMSNorm statistics) come from the previous kernel
     const bool nrm = p.norm_w != nullptr;
     const int chunks = p.kslice / 8;
     const int vchunks = kvalid / 8;
-    // the K slice of x lands by bulk copies, one per row (and one for the norm weights), all in
-    // flight at once; rows past M are zeroed meanwhile
-    if (tid == 0) {
-      const uint32_t bytes = uint32_t(kvalid) * 2;
-      mbar_arrive_expect_tx(xbar, bytes * uint32_t(p.M + (nrm ? 1 : 0)));
-      for (int m = 0; m < p.M; ++m)
-        bulk_load(xs + m * XP, p.x + (size_t)m * p.ldx + kbase, bytes, xbar);
-      if (nrm) bulk_load(nws, p.norm_w + kbase, bytes, xbar);
+    constexpr int NMX = TC ? (MT <= 2 ? 16 : 32) : RP;  // staged x rows
+    // x chunk (row m, 8-k block c): row-major for the mma.sync consumers, 8-k blocks of NMX rows
+    // (the UMMA K-major canonical layout) for the tcgen05 consumers
+    auto xoff = [&](int m, int c) { return TC ? (c * NMX + m) * 16 : m * XP + c * 16; };
+    if constexpr (!TC) {
+      // the K slice of x lands by bulk copies, one per row (and one for the norm weights), all
+      // in flight at once; rows past M are zeroed meanwhile
+      if (tid == 0) {
+        const uint32_t bytes = uint32_t(kvalid) * 2;
+        mbar_arrive_expect_tx(xbar, bytes * uint32_t(p.M + (nrm ? 1 : 0)));
+        for (int m = 0; m < p.M; ++m)
+          bulk_load(xs + m * XP, p.x + (size_t)m * p.ldx + kbase, bytes, xbar);
+        if (nrm) bulk_load(nws, p.norm_w + kbase, bytes, xbar);
+      }
+    } else {
+      // 16-byte copies straight into the canonical places, all in flight at once
+      const uint32_t xa0 = smem_u32(xs);
+      for (int idx = tid; idx < p.M * vchunks; idx += NC) {
+        const int m = idx / vchunks, c = idx - m * vchunks;
+        cp_async_16_zfill(xa0 + uint32_t(xoff(m, c)), p.x + (size_t)m * p.ldx + kbase + c * 8, true);
+      }
+      if (nrm)
+        for (int c = tid; c < vchunks; c += NC)
+          cp_async_16_zfill(smem_u32(nws) + uint32_t(c * 16), p.norm_w + kbase + c * 8, true);
+      asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    for (int idx = tid; idx < (RP - p.M) * chunks; idx += NC) {
+    for (int idx = tid; idx < (NMX - p.M) * chunks; idx += NC) {
       const int m = p.M + idx / chunks, c = idx % chunks;
-      *reinterpret_cast<uint4*>(xs + m * XP + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(xs + xoff(m, c)) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    for (int idx = tid; idx < (RP - p.M) * (kvalid / 64); idx += NC) {
+      const int g = idx / (RP - p.M), m = p.M + idx % (RP - p.M);
+      sx[g * RP + m] = 0.f;
     }
     if (nrm) {
       for (int m = warp; m < RP; m += NWC) {
@@ -252,89 +511,115 @@ __global__ void __launch_bounds__(NTHR, 1)
         if (lane == 0) rsm[m] = m < p.M ? rsqrtf(ss / float(p.K) + p.eps) : 0.f;
       }
     }
+    if constexpr (TC) asm volatile("cp.async.wait_all;" ::: "memory");
     asm volatile("bar.sync 1, %0;" ::"n"(NC));
-    if (ok) ok = mbar_wait(xbar, 0, p.status, kErrWaitFull);
-    // in place: apply the norm (x * rs * w rounded to bf16) and permute k inside each 8-block
-    // (4-bit: 0,4,1,5,2,6,3,7) or 4-block (8-bit: 0,2,1,3) as the magic extraction orders weights
-    for (int idx = tid; idx < p.M * vchunks; idx += NC) {
-      const int m = idx / vchunks, c = idx - m * vchunks;
-      uint4 vv = *reinterpret_cast<const uint4*>(xs + m * XP + c * 16);
-      if (nrm) {
-        const float r = rsm[m];
-        const uint4 w = *reinterpret_cast<const uint4*>(nws + c * 16);
-        uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
-        const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w);
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
-                              bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
-      }
-      uint4 o;
-      if (BITS == 4) {
-        o.x = __byte_perm(vv.x, vv.z, 0x5410);
-        o.y = __byte_perm(vv.x, vv.z, 0x7632);
-        o.z = __byte_perm(vv.y, vv.w, 0x5410);
-        o.w = __byte_perm(vv.y, vv.w, 0x7632);
-      } else {
-        o.x = __byte_perm(vv.x, vv.y, 0x5410);
-        o.y = __byte_perm(vv.x, vv.y, 0x7632);
-        o.z = __byte_perm(vv.z, vv.w, 0x5410);
-        o.w = __byte_perm(vv.z, vv.w, 0x7632);
-      }
-      *reinterpret_cast<uint4*>(xs + m * XP + c * 16) = o;
+    if constexpr (!TC) {
+      if (ok) ok = mbar_wait(xbar, 0, p.status, kErrWaitFull);
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(NC));
-    // per-group sums of the staged (rounded) x, summed in a fixed order
-    for (int idx = tid; idx < RP * (kvalid / 64); idx += NC) {
-      const int g = idx / RP, m = idx - g * RP;
-      float s = 0.f;
+    // in place: apply the norm (x * rs * w rounded to bf16), permute k inside each 8-block
+    // (4-bit: 0,4,1,5,2,6,3,7) or 4-block (8-bit: 0,2,1,3) as the magic extraction orders the
+    // weights, and sum each group of 64: the 8 chunks of a group sit on 8 consecutive lanes
+    // (chunk counts are multiples of 8) and reduce by shuffles in a fixed order
+    for (int base = 0; base < p.M * vchunks; base += NC) {
+      const int idx = base + tid;
+      const bool live = idx < p.M * vchunks;
+      const int m = live ? idx / vchunks : 0, c = live ? idx - m * vchunks : 0;
+      float part = 0.f;
+      if (live) {
+        uint4 vv = *reinterpret_cast<const uint4*>(xs + xoff(m, c));
+        if (nrm) {
+          const float r = rsm[m];
+          const uint4 w = *reinterpret_cast<const uint4*>(nws + c * 16);
+          uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
+          const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w);
 #pragma unroll
-      for (int b = 0; b < 8; ++b) {
-        const uint4 q = *reinterpret_cast<const uint4*>(xs + m * XP + (g * 8 + b) * 16);
-        s += (bf16_lo(q.x) + bf16_hi(q.x)) + (bf16_lo(q.y) + bf16_hi(q.y)) +
-             (bf16_lo(q.z) + bf16_hi(q.z)) + (bf16_lo(q.w) + bf16_hi(q.w));
+          for (int e = 0; e < 4; ++e)
+            pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
+                                bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
+        }
+        part = (bf16_lo(vv.x) + bf16_hi(vv.x)) + (bf16_lo(vv.y) + bf16_hi(vv.y)) +
+               (bf16_lo(vv.z) + bf16_hi(vv.z)) + (bf16_lo(vv.w) + bf16_hi(vv.w));
+        uint4 o;
+        if (BITS == 4) {
+          o.x = __byte_perm(vv.x, vv.z, 0x5410);
+          o.y = __byte_perm(vv.x, vv.z, 0x7632);
+          o.z = __byte_perm(vv.y, vv.w, 0x5410);
+          o.w = __byte_perm(vv.y, vv.w, 0x7632);
+        } else {
+          o.x = __byte_perm(vv.x, vv.y, 0x5410);
+          o.y = __byte_perm(vv.x, vv.y, 0x7632);
+          o.z = __byte_perm(vv.z, vv.w, 0x5410);
+          o.w = __byte_perm(vv.z, vv.w, 0x7632);
+        }
+        *reinterpret_cast<uint4*>(xs + xoff(m, c)) = o;
       }
-      sx[g * RP + m] = s;
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      part += __shfl_xor_sync(0xffffffffu, part, 4);
+      if (live && (c & 7) == 0) sx[(c >> 3) * RP + m] = part;
     }
+    if constexpr (TC) fence_proxy_async_smem();  // x becomes the tensor core's B operand
     asm volatile("bar.sync 1, %0;" ::"n"(NC));
 
+    if constexpr (TC) {
+      consume_tc<BITS, MT>(p, ring, sring, xs, sx, part, xch, full, empty, ready, freeb, tcbar,
+                           *tmem_slot, ntl, nsb, nst, S, SS, cs, rank, ok);
+    } else {
+
+    // Warp w owns 32 tile rows (two 16-row MMA groups sharing one set of x fragments) and one
+    // k half of every stage (GH of its GPS groups); the two halves are summed at the tile end.
+    constexpr int GH = GPS / 2;
+    const int half = warp >> 2, wr = warp & 3;
     const int g8 = lane >> 2, t4 = lane & 3;
-    const int r0 = warp * 16 + row_perm<BITS>(g8), r1 = r0 + 8;
+    int rows[2][2];
+#pragma unroll
+    for (int rg = 0; rg < 2; ++rg) {
+      rows[rg][0] = wr * 32 + rg * 16 + row_perm<BITS>(g8);
+      rows[rg][1] = rows[rg][0] + 8;
+    }
     const uint32_t ring_a = smem_u32(ring);
     const uint32_t sring_a = smem_u32(sring);
     // this thread's B fragments of group gl, n8 tile mt: 32 bytes at row (8*mt + g8), k = 16*t4
     const uint32_t xa = smem_u32(xs) + uint32_t(g8 * XP + t4 * 32);
-    // swizzled byte offset of (row, logical 16-byte chunk c) inside a stage, plus lane part
+    // swizzled byte offset of (row, logical 16-byte chunk c) inside a stage
     auto wofs = [](int row, int c) { return uint32_t(row * 128 + ((c ^ (row & 7)) << 4)); };
 
     for (int j = 0; j < ntl; ++j) {
-      float acc[MT][4];
+      float acc[2][MT][4];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
+      for (int rg = 0; rg < 2; ++rg)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[mt][i] = 0.f;
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[rg][mt][i] = 0.f;
 
       for (int sb = 0; sb < nsb; ++sb) {
-        uint4 sv0, sv1, bv0, bv1;  // 8 groups of scales / biases of rows r0, r1
 #pragma unroll
         for (int si = 0; si < SPS; ++si) {
           const int st = sb * SPS + si;
           const int g = j * nst + st;
           const int slot = g % S;
           if (ok) ok = mbar_wait(&full[slot], (g / S) & 1, p.status, kErrWaitFull);
-          if (si == 0) {
-            const uint32_t sa = sring_a + uint32_t(((j * nsb + sb) % SS) * 2 * SCB);
-            sv0 = lds128(sa + r0 * 16);
-            sv1 = lds128(sa + r1 * 16);
-            bv0 = lds128(sa + SCB + r0 * 16);
-            bv1 = lds128(sa + SCB + r1 * 16);
-          }
+          // scales / biases of this stage's groups for the thread's 4 rows: one 32-bit word
+          // (two consecutive groups) per row
+          const int gw = (si * GPS + half * GH) & ~1;  // first group of the word
+          const uint32_t sa = sring_a + uint32_t(((j * nsb + sb) % SS) * 2 * SCB) + uint32_t(gw * 2);
+          uint32_t sw[2][2], bw[2][2];
+#pragma unroll
+          for (int rg = 0; rg < 2; ++rg)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              sw[rg][h] = lds32(sa + rows[rg][h] * 16);
+              bw[rg][h] = lds32(sa + SCB + rows[rg][h] * 16);
+            }
           const uint32_t wb = ring_a + uint32_t(slot * STG);
 #pragma unroll
-          for (int gi = 0; gi < GPS; ++gi) {
-            const int gl = st * GPS + gi;          // group inside the K slice
-            const int gb = si * GPS + gi;          // group inside the scale block (0..7)
-            // B fragments (x), two k16 steps per 16-byte load
+          for (int gg = 0; gg < GH; ++gg) {
+            const int gi = half * GH + gg;     // group inside the stage
+            const int gl = st * GPS + gi;      // group inside the K slice
+            // which half of the scale word holds this group
+            const bool hi16 = ((si * GPS + gi) & 1) != 0;
+            // B fragments (x), two k16 steps per 16-byte load, shared by both row groups
             uint32_t b[MT][4][2];
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
@@ -346,74 +631,74 @@ __global__ void __launch_bounds__(NTHR, 1)
               b[mt][2][0] = q1.x; b[mt][2][1] = q1.y;
               b[mt][3][0] = q1.z; b[mt][3][1] = q1.w;
             }
-            float pr[MT][4];
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
+            for (int rg = 0; rg < 2; ++rg) {
+              const int r0 = rows[rg][0], r1 = rows[rg][1];
+              float pr[MT][4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) pr[mt][i] = 0.f;
-            if (BITS == 4) {
-              // 8 bytes of row r: group bytes 8*t4 .. 8*t4+7 = k 16*t4 .. 16*t4+15
-              const int c = gi * 2 + (t4 >> 1);
-              const uint32_t lo8 = uint32_t((t4 & 1) * 8);
-              const uint2 w0 = lds64(wb + wofs(r0, c) + lo8);
-              const uint2 w1 = lds64(wb + wofs(r1, c) + lo8);
+              for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-              for (int s = 0; s < 4; ++s) {
-                const uint32_t x0 = (s < 2) ? w0.x : w0.y;
-                const uint32_t x1 = (s < 2) ? w1.x : w1.y;
-                const int e = 2 * (s & 1);
-                const uint32_t a0 = lop3_and_or(x0 >> (4 * e), 0x000F000Fu, 0x43004300u);
-                const uint32_t a2 = lop3_and_or(x0 >> (4 * e + 4), 0x000F000Fu, 0x43004300u);
-                const uint32_t a1 = lop3_and_or(x1 >> (4 * e), 0x000F000Fu, 0x43004300u);
-                const uint32_t a3 = lop3_and_or(x1 >> (4 * e + 4), 0x000F000Fu, 0x43004300u);
+                for (int i = 0; i < 4; ++i) pr[mt][i] = 0.f;
+              if (BITS == 4) {
+                // 8 bytes of each row: group bytes 8*t4 .. 8*t4+7 = k 16*t4 .. 16*t4+15
+                const int c = gi * 2 + (t4 >> 1);
+                const uint32_t lo8 = uint32_t((t4 & 1) * 8);
+                const uint2 w0 = lds64(wb + wofs(r0, c) + lo8);
+                const uint2 w1 = lds64(wb + wofs(r1, c) + lo8);
 #pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
-                  mma_bf16_16816(pr[mt], a0, a1, a2, a3, b[mt][s][0], b[mt][s][1]);
+                for (int s = 0; s < 4; ++s) {
+                  const uint32_t x0 = (s < 2) ? w0.x : w0.y;
+                  const uint32_t x1 = (s < 2) ? w1.x : w1.y;
+                  const int e = 2 * (s & 1);
+                  const uint32_t a0 = lop3_and_or(x0 >> (4 * e), 0x000F000Fu, 0x43004300u);
+                  const uint32_t a2 = lop3_and_or(x0 >> (4 * e + 4), 0x000F000Fu, 0x43004300u);
+                  const uint32_t a1 = lop3_and_or(x1 >> (4 * e), 0x000F000Fu, 0x43004300u);
+                  const uint32_t a3 = lop3_and_or(x1 >> (4 * e + 4), 0x000F000Fu, 0x43004300u);
+#pragma unroll
+                  for (int mt = 0; mt < MT; ++mt)
+                    mma_bf16_16816(pr[mt], a0, a1, a2, a3, b[mt][s][0], b[mt][s][1]);
+                }
+              } else {
+                // 16 bytes of each row: group bytes 16*t4 .. 16*t4+15 = k 16*t4 .. 16*t4+15
+                const int c = gi * 4 + t4;
+                const uint4 w0 = lds128(wb + wofs(r0, c));
+                const uint4 w1 = lds128(wb + wofs(r1, c));
+                const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
+                const uint32_t wc[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                  const uint32_t x0 = wa[s], x1 = wc[s];
+                  // low nibble plane: (k0, k2) and (k1, k3) of the word's 4 bytes as 128 + lo
+                  uint32_t a0 = lop3_and_or(x0, 0x000F000Fu, 0x43004300u);
+                  uint32_t a2 = lop3_and_or(x0 >> 8, 0x000F000Fu, 0x43004300u);
+                  uint32_t a1 = lop3_and_or(x1, 0x000F000Fu, 0x43004300u);
+                  uint32_t a3 = lop3_and_or(x1 >> 8, 0x000F000Fu, 0x43004300u);
+#pragma unroll
+                  for (int mt = 0; mt < MT; ++mt)
+                    mma_bf16_16816(pr[mt], a0, a1, a2, a3, b[mt][s][0], b[mt][s][1]);
+                  // high nibble plane as 256 + 16 hi
+                  a0 = lop3_and_or(x0 >> 1, 0x00780078u, 0x43804380u);
+                  a2 = lop3_and_or(x0 >> 9, 0x00780078u, 0x43804380u);
+                  a1 = lop3_and_or(x1 >> 1, 0x00780078u, 0x43804380u);
+                  a3 = lop3_and_or(x1 >> 9, 0x00780078u, 0x43804380u);
+#pragma unroll
+                  for (int mt = 0; mt < MT; ++mt)
+                    mma_bf16_16816(pr[mt], a0, a1, a2, a3, b[mt][s][0], b[mt][s][1]);
+                }
               }
-            } else {
-              // 16 bytes of row r: group bytes 16*t4 .. 16*t4+15 = k 16*t4 .. 16*t4+15
-              const int c = gi * 4 + t4;
-              const uint4 w0 = lds128(wb + wofs(r0, c));
-              const uint4 w1 = lds128(wb + wofs(r1, c));
-              const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
-              const uint32_t wc[4] = {w1.x, w1.y, w1.z, w1.w};
+              // fold: acc += s*P + (b - MAGIC*s) * sum_k x, rows r0 (i = 0,1) and r1 (i = 2,3)
+              const float s0 = hi16 ? bf16_hi(sw[rg][0]) : bf16_lo(sw[rg][0]);
+              const float s1 = hi16 ? bf16_hi(sw[rg][1]) : bf16_lo(sw[rg][1]);
+              const float c0 = (hi16 ? bf16_hi(bw[rg][0]) : bf16_lo(bw[rg][0])) - MAGIC * s0;
+              const float c1 = (hi16 ? bf16_hi(bw[rg][1]) : bf16_lo(bw[rg][1])) - MAGIC * s1;
 #pragma unroll
-              for (int s = 0; s < 4; ++s) {
-                const uint32_t x0 = wa[s], x1 = wc[s];
-                // low nibble plane: (k0, k2) and (k1, k3) of the word's 4 bytes as 128 + lo
-                uint32_t a0 = lop3_and_or(x0, 0x000F000Fu, 0x43004300u);
-                uint32_t a2 = lop3_and_or(x0 >> 8, 0x000F000Fu, 0x43004300u);
-                uint32_t a1 = lop3_and_or(x1, 0x000F000Fu, 0x43004300u);
-                uint32_t a3 = lop3_and_or(x1 >> 8, 0x000F000Fu, 0x43004300u);
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
-                  mma_bf16_16816(pr[mt], a0, a1, a2, a3, b[mt][s][0], b[mt][s][1]);
-                // high nibble plane as 256 + 16 hi
-                a0 = lop3_and_or(x0 >> 1, 0x00780078u, 0x43804380u);
-                a2 = lop3_and_or(x0 >> 9, 0x00780078u, 0x43804380u);
-                a1 = lop3_and_or(x1 >> 1, 0x00780078u, 0x43804380u);
-                a3 = lop3_and_or(x1 >> 9, 0x00780078u, 0x43804380u);
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
-                  mma_bf16_16816(pr[mt], a0, a1, a2, a3, b[mt][s][0], b[mt][s][1]);
+              for (int mt = 0; mt < MT; ++mt) {
+                const float2 xs2 = *reinterpret_cast<const float2*>(sx + gl * RP + mt * 8 + 2 * t4);
+                fma2(acc[rg][mt][0], acc[rg][mt][1], c0, c0, xs2.x, xs2.y);
+                fma2(acc[rg][mt][2], acc[rg][mt][3], c1, c1, xs2.x, xs2.y);
+                fma2(acc[rg][mt][0], acc[rg][mt][1], s0, s0, pr[mt][0], pr[mt][1]);
+                fma2(acc[rg][mt][2], acc[rg][mt][3], s1, s1, pr[mt][2], pr[mt][3]);
               }
-            }
-            // fold: acc += s*P + (b - MAGIC*s) * sum_k x, rows r0 (i = 0,1) and r1 (i = 2,3)
-            const uint32_t ws0 = (gb >> 1) == 0 ? sv0.x : (gb >> 1) == 1 ? sv0.y : (gb >> 1) == 2 ? sv0.z : sv0.w;
-            const uint32_t ws1 = (gb >> 1) == 0 ? sv1.x : (gb >> 1) == 1 ? sv1.y : (gb >> 1) == 2 ? sv1.z : sv1.w;
-            const uint32_t wb0 = (gb >> 1) == 0 ? bv0.x : (gb >> 1) == 1 ? bv0.y : (gb >> 1) == 2 ? bv0.z : bv0.w;
-            const uint32_t wb1 = (gb >> 1) == 0 ? bv1.x : (gb >> 1) == 1 ? bv1.y : (gb >> 1) == 2 ? bv1.z : bv1.w;
-            const float s0 = (gb & 1) ? bf16_hi(ws0) : bf16_lo(ws0);
-            const float s1 = (gb & 1) ? bf16_hi(ws1) : bf16_lo(ws1);
-            const float c0 = ((gb & 1) ? bf16_hi(wb0) : bf16_lo(wb0)) - MAGIC * s0;
-            const float c1 = ((gb & 1) ? bf16_hi(wb1) : bf16_lo(wb1)) - MAGIC * s1;
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-              const float2 xs2 = *reinterpret_cast<const float2*>(sx + gl * RP + mt * 8 + 2 * t4);
-              fma2(acc[mt][0], acc[mt][1], c0, c0, xs2.x, xs2.y);
-              fma2(acc[mt][2], acc[mt][3], c1, c1, xs2.x, xs2.y);
-              fma2(acc[mt][0], acc[mt][1], s0, s0, pr[mt][0], pr[mt][1]);
-              fma2(acc[mt][2], acc[mt][3], s1, s1, pr[mt][2], pr[mt][3]);
             }
           }
           __syncwarp();
@@ -421,45 +706,74 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
       }
 
+      // ---- the k halves meet: warps of half 1 hand their sums to the half-0 warp of the same
+      // rows (fixed order: half 0 + half 1)
+      constexpr int NACC = 2 * MT * 4;
+      if (half == 1) {
+#pragma unroll
+        for (int rg = 0; rg < 2; ++rg)
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              xch[((rg * MT + mt) * 4 + i) * 128 + wr * 32 + lane] = acc[rg][mt][i];
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(NC));
+      static_assert(NACC <= 32, "exchange buffer");
+
       // ---- partial tile j: push row m into receive buffer j & 1 of its owner (m % cs), slot
       // [rank][m / cs] (local stores when cs == 1)
       const int pbuf = j & 1;
       const int ro = owned_rows(RP, cs);
+      if (j == 0 && cs > 1) cluster_wait();  // peers' buffers and barriers exist
       // the owners' buffer pbuf last held tile j-2: every owner must be done reading it
       if (j >= 2 && ok)
         ok = mbar_wait_cluster(&freeb[pbuf], ((j - 2) >> 1) & 1, p.status, kErrWaitCluster);
-      const uint32_t pa = smem_u32(part + (pbuf * cs + rank) * ro * PSTR);
+      if (half == 0) {
+        const uint32_t pa = smem_u32(part + (pbuf * cs + rank) * ro * PSTR);
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
+        for (int rg = 0; rg < 2; ++rg) {
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int m = mt * 8 + 2 * t4 + i;
-          const int owner = m % cs, ml = m / cs;
-          const uint32_t a0 = pa + uint32_t((ml * PSTR + r0) * 4);
-          const uint32_t a1 = pa + uint32_t((ml * PSTR + r1) * 4);
-          if (cs > 1) {
-            st_dsmem_f32(mapa_shared(a0, owner), acc[mt][i]);
-            st_dsmem_f32(mapa_shared(a1, owner), acc[mt][2 + i]);
-          } else {
-            part[(pbuf * ro + ml) * PSTR + r0] = acc[mt][i];
-            part[(pbuf * ro + ml) * PSTR + r1] = acc[mt][2 + i];
+          for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              acc[rg][mt][i] += xch[((rg * MT + mt) * 4 + i) * 128 + wr * 32 + lane];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const int m = mt * 8 + 2 * t4 + i;
+              const int owner = m % cs, ml = m / cs;
+              const int r0 = rows[rg][0], r1 = rows[rg][1];
+              const uint32_t a0 = pa + uint32_t((ml * PSTR + r0) * 4);
+              const uint32_t a1 = pa + uint32_t((ml * PSTR + r1) * 4);
+              if (cs > 1) {
+                st_dsmem_f32(mapa_shared(a0, owner), acc[rg][mt][i]);
+                st_dsmem_f32(mapa_shared(a1, owner), acc[rg][mt][2 + i]);
+              } else {
+                part[(pbuf * ro + ml) * PSTR + r0] = acc[rg][mt][i];
+                part[(pbuf * ro + ml) * PSTR + r1] = acc[rg][mt][2 + i];
+              }
+            }
           }
         }
       }
-      asm volatile("bar.sync 1, %0;" ::"n"(NC));
-      if (tid == 0) {  // publish to every owner of the cluster
+      asm volatile("bar.sync 1, %0;" ::"n"(NC));  // pushes issued; the exchange buffer is free
+      // publish to every owner of the cluster: lane c of warp 0 releases to CTA c
+      if (warp == 0 && lane < cs) {
         if (cs > 1) {
           fence_acq_rel_cluster();
-          for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&ready[pbuf], c);
+          mbar_arrive_cluster(&ready[pbuf], lane);
         } else {
           mbar_arrive(&ready[pbuf]);
         }
       }
     }
+    if (ntl == 0 && cs > 1) cluster_wait();
+    }  // mma.sync consumers
   } else {
     // ------------------------------------------------------------- epilogue warps
     pdl_wait();  // the epilogues read / write buffers of earlier kernels (residual, caches)
     const int etid = tid - WARP_EPI * 32;
+    if (cs > 1) cluster_wait();  // peers' barriers exist before the first remote arrive
     const int ro = owned_rows(RP, cs);
     const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
     for (int j = 0; j < ntl; ++j) {
@@ -479,9 +793,10 @@ __global__ void __launch_bounds__(NTHR, 1)
         *reinterpret_cast<float4*>(&red[m * PSTR + n4 * 4]) = s;
       }
       asm volatile("bar.sync 2, %0;" ::"n"(NE));
-      if (etid == 0) {  // every CTA may push its next partial into this buffer again
+      // every CTA may push its next partial into this buffer again (lane c -> CTA c)
+      if (etid < cs) {
         if (cs > 1)
-          for (int c = 0; c < cs; ++c) mbar_arrive_cluster(&freeb[pbuf], c);
+          mbar_arrive_cluster(&freeb[pbuf], etid);
         else
           mbar_arrive(&freeb[pbuf]);
       }
@@ -492,14 +807,21 @@ __global__ void __launch_bounds__(NTHR, 1)
 
   // no CTA leaves while a peer may still read its partial tiles or arrive on its barriers
   if (cs > 1) cluster_sync_all(); else __syncthreads();
+  if constexpr (TC) {
+    if (warp == 0) {
+      tcg::tc_fence_after();
+      tcg::tmem_dealloc(*tmem_slot, 512);
+    }
+  }
 }
 
 }  // namespace st
 
 // ----------------------------------------------------------------------------- host side
 
-int st_smem_bytes(int bits, int rt, int kslice, int nslots, int cs) {
-  return st::layout(bits, rt, kslice, nslots, cs).total;
+int st_smem_bytes(int bits, int rt, int kslice, int nslots, int cs, bool tc) {
+  // at least enough that one CTA fills an SM: CTAs never share an SM's tensor memory
+  return std::max(st::layout(bits, rt, kslice, nslots, cs, tc).total, tc ? 120 * 1024 : 0);
 }
 
 template <typename Kern>
@@ -526,7 +848,7 @@ int st_max_clusters(int cs, int smem) {
   }
   int n = sm_count(dev) / cs;
   // occupancy depends on the launch shape only; one instance answers for all
-  auto kern = st::qmm_st_kernel<4, 2, EPI_PLAIN>;
+  auto kern = st::qmm_st_kernel<4, 2, EPI_PLAIN, false>;
   if (configure_st(kern) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cs, 1);
@@ -548,10 +870,10 @@ int st_max_clusters(int cs, int smem) {
   return n;
 }
 
-template <int BITS, int MT, int EPI>
+template <int BITS, int MT, int EPI, bool TC>
 static int launch_st(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream) {
-  auto kern = st::qmm_st_kernel<BITS, MT, EPI>;
-  const int smem = st::layout(BITS, MT, pl.kslice, pl.nslots, pl.cs).total;
+  auto kern = st::qmm_st_kernel<BITS, MT, EPI, TC>;
+  const int smem = st_smem_bytes(BITS, MT, pl.kslice, pl.nslots, pl.cs, TC);
   static bool configured = false;
   if (!configured) {
     DSPARK_CUDA_TRY(configure_st(kern), "qmm_st: set smem / cluster attributes");
@@ -570,9 +892,14 @@ static int launch_st(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream)
 
 template <int BITS, int EPI>
 static int st_dispatch(const QmmParams& p, const QmmPlan& pl, cudaStream_t s) {
-  if (p.M <= 8) return launch_st<BITS, 1, EPI>(p, pl, s);
-  if (p.M <= 16) return launch_st<BITS, 2, EPI>(p, pl, s);
-  return launch_st<BITS, 4, EPI>(p, pl, s);
+  if (pl.tcmma) {
+    if (p.M <= 8) return launch_st<BITS, 1, EPI, true>(p, pl, s);
+    if (p.M <= 16) return launch_st<BITS, 2, EPI, true>(p, pl, s);
+    return launch_st<BITS, 4, EPI, true>(p, pl, s);
+  }
+  if (p.M <= 8) return launch_st<BITS, 1, EPI, false>(p, pl, s);
+  if (p.M <= 16) return launch_st<BITS, 2, EPI, false>(p, pl, s);
+  return launch_st<BITS, 4, EPI, false>(p, pl, s);
 }
 
 int run_st(const QmmParams& p, int epi, const QmmPlan& pl, cudaStream_t s) {
