@@ -164,7 +164,8 @@ int dspark_argmax(const void* logits, int64_t ld, int R, int V, int32_t* tt, voi
  * target's argmax (cumprod(drafts == tt[:cap]).sum(), src/mlx_dspark/generate.py:1548-1550,
  * batched src/mlx_dspark/batch_engine.py:684-686); next_tok[b] = tt[cu_rows[b] + n] (the
  * bonus token); if lens != NULL, lens[b] -= cap - n (the rollback of the rejected tail,
- * src/mlx_dspark/batch_engine.py:692-705). */
+ * src/mlx_dspark/batch_engine.py:692-705). A request with no rows this step (an idle slot)
+ * gets n_accept = 0, next_tok = -1 and keeps its length. */
 int dspark_accept(const int32_t* tt, const int32_t* ids, const int32_t* cu_rows, int B,
                   int32_t* n_accept, int32_t* next_tok, int32_t* lens, void* stream);
 
@@ -235,14 +236,15 @@ typedef struct {
   int kv_cap;              /* positions per request slot */
 } dspark_model;
 
-/* Caller-owned device buffers for one verify forward of up to r_max rows. */
+/* Caller-owned device buffers for one verify forward of up to rows_cap packed rows (h, xq,
+ * attn, act and the logits hold rows_cap rows; the statistics buffers 1024 * rows_cap floats). */
 typedef struct {
   void* h;          /* bf16 [r_max, hidden] residual stream */
   void* xq;         /* bf16 [r_max, n_heads*head_dim] roped queries */
   void* attn;       /* bf16 [r_max, n_heads*head_dim] attention output */
   void* act;        /* bf16 [r_max, intermediate] SwiGLU output */
-  float* ssq_a;     /* fp32 [1024 * 32] RMSNorm partial statistics */
-  float* ssq_b;     /* fp32 [1024 * 32] */
+  float* ssq_a;     /* fp32 [1024 * rows_cap] RMSNorm partial statistics */
+  float* ssq_b;     /* fp32 [1024 * rows_cap] */
   float* inv_freq;  /* fp32 [head_dim/2] RoPE frequencies (filled by the forward) */
   int32_t* row_pos; /* int32 [r_max] absolute positions */
   int64_t* row_kv;  /* int64 [r_max] element offset of each row's cache slot */
@@ -252,6 +254,7 @@ typedef struct {
   int64_t* kv_off;     /* int64 [B] cache slot offset per request */
   void* attn_ws;    /* attention workspace (may be NULL) */
   size_t attn_ws_bytes;
+  int rows_cap;     /* rows the buffers hold (0: 32) */
 } dspark_fwd_buffers;
 
 /* One verify forward (Target.verify -> _body_mlxlm + head, src/mlx_dspark/target.py:642,
@@ -261,7 +264,9 @@ typedef struct {
  * -> RMSNorm -> lm_head QMM -> logits [R, vocab] (row stride ld_logits).
  * The packing arrays in `buf` (row_pos, row_kv, kv_len, row_start, q_len, kv_off) must be
  * filled for the step (dspark_pack_ragged, or dspark_verify_prepare for one request).
- * L_max / qL_max bound the requests' key counts / block rows. R <= 32. */
+ * L_max / qL_max bound the requests' key counts / block rows (qL_max <= 32). R <= rows_cap:
+ * a step of many requests (the batch engine) runs every projection in launches of 32 rows
+ * (each re-reads the weights) and the attention over all requests at once. */
 int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf,
                           const int32_t* ids, int R, int B, int qL_max, int L_max,
                           void* logits, int64_t ld_logits, void* stream);

@@ -60,7 +60,7 @@ class FwdBuffers(C.Structure):
     _fields_ = [("h", vp), ("xq", vp), ("attn", vp), ("act", vp), ("ssq_a", vp), ("ssq_b", vp),
                 ("inv_freq", vp), ("row_pos", vp), ("row_kv", vp), ("kv_len", vp),
                 ("row_start", vp), ("q_len", vp), ("kv_off", vp), ("attn_ws", vp),
-                ("attn_ws_bytes", sz)]
+                ("attn_ws_bytes", sz), ("rows_cap", i32)]
 
 
 _SIGS = {

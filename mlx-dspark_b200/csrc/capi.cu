@@ -1,6 +1,7 @@
 // C ABI (include/dspark.h): argument checking, host utilities, and the verify-forward layer
 // loop that chains the fused kernels on one stream (graph-capturable, programmatic
 // dependent launch between consecutive kernels).
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdlib>
@@ -408,7 +409,9 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf, 
                           void* stream) {
   if (!m || !buf || !ids || !logits || !m->layers) return fail(DSPARK_ERR_ARG, "forward: null");
   if (m->head_dim != 128) return fail(DSPARK_ERR_UNSUPPORTED, "forward: head_dim %d (needs 128)", m->head_dim);
-  if (R < 1 || R > 32) return fail(DSPARK_ERR_UNSUPPORTED, "forward: R=%d rows (1..32)", R);
+  const int rows_cap = buf->rows_cap > 0 ? buf->rows_cap : 32;
+  if (R < 1 || R > rows_cap) return fail(DSPARK_ERR_UNSUPPORTED, "forward: R=%d rows (1..%d)", R, rows_cap);
+  if (qL_max < 1 || qL_max > 32) return fail(DSPARK_ERR_UNSUPPORTED, "forward: qL_max=%d (1..32)", qL_max);
   if (m->hidden % 512 || m->intermediate % 512)
     return fail(DSPARK_ERR_UNSUPPORTED, "forward: hidden / intermediate must be multiples of 512");
   cudaStream_t s = as_stream(stream);
@@ -418,7 +421,8 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf, 
   bf16* xq = static_cast<bf16*>(buf->xq);
   bf16* at = static_cast<bf16*>(buf->attn);
   bf16* act = static_cast<bf16*>(buf->act);
-  constexpr int kSsqStride = 32;
+  const int kSsqStride = rows_cap;  // statistics entry e of row m at e * kSsqStride + m
+  constexpr int kChunk = 32;        // rows per projection launch
 
   DSPARK_TRY(ops::fill_inv_freq(buf->inv_freq, D, m->rope_theta, s));
   DSPARK_TRY(ops::embed(ids, R, m->embed.wq, static_cast<const bf16*>(m->embed.scales),
@@ -430,26 +434,27 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf, 
   for (int l = 0; l < m->n_layers; ++l) {
     const dspark_layer& L = m->layers[l];
     // fused QKV projection + input RMSNorm + q/k RMSNorm + RoPE + cache write
-    {
+    for (int r0 = 0; r0 < R; r0 += kChunk) {
+      const int mr = std::min(kChunk, R - r0);
       qmm::QmmParams p;
-      p.x = h; p.ldx = H; p.M = R; p.K = H; p.N = L.qkv.N; p.bits = L.qkv.bits;
+      p.x = h + int64_t(r0) * H; p.ldx = H; p.M = mr; p.K = H; p.N = L.qkv.N; p.bits = L.qkv.bits;
       p.wq = L.qkv.wq;
       p.scales = static_cast<const bf16*>(L.qkv.scales);
       p.biases = static_cast<const bf16*>(L.qkv.biases);
       p.norm_w = static_cast<const bf16*>(L.in_norm);
-      p.ssq_in = ssq_cur; p.ssq_n = ssq_n; p.ssq_stride = kSsqStride; p.eps = m->rms_eps;
+      p.ssq_in = ssq_cur + r0; p.ssq_n = ssq_n; p.ssq_stride = kSsqStride; p.eps = m->rms_eps;
       p.hq = Hq; p.hk = Hk;
       p.qnorm = static_cast<const bf16*>(L.q_norm);
       p.knorm = static_cast<const bf16*>(L.k_norm);
       p.inv_freq = buf->inv_freq;
-      p.qout = xq; p.ldq = int64_t(Hq) * D;
+      p.qout = xq + int64_t(r0) * Hq * D; p.ldq = int64_t(Hq) * D;
       p.kcache = static_cast<bf16*>(L.k_cache);
       p.vcache = static_cast<bf16*>(L.v_cache);
       p.k_sh = m->k_sh; p.k_ss = m->k_ss; p.v_sh = m->v_sh; p.v_ss = m->v_ss;
       p.kv_cap = m->kv_cap;
-      p.row_pos = buf->row_pos; p.row_kv = buf->row_kv;
+      p.row_pos = buf->row_pos + r0; p.row_kv = buf->row_kv + r0;
       p.out = xq; p.ldo = 0;
-      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_QKROPE, R);
+      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_QKROPE, mr);
       DSPARK_TRY(qmm::run(p, qmm::EPI_QKROPE, &pl, s));
     }
     // verify attention over each request's cache slot
@@ -474,58 +479,65 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf, 
       DSPARK_TRY(attn::run(a, &apl, s));
     }
     // O projection + residual (in place on h) + statistics for the post-attention norm
-    int ssq_n_b;
-    {
+    int ssq_n_b = 0;
+    for (int r0 = 0; r0 < R; r0 += kChunk) {
+      const int mr = std::min(kChunk, R - r0);
       qmm::QmmParams p;
-      p.x = at; p.ldx = int64_t(Hq) * D; p.M = R; p.K = Hq * D; p.N = L.o.N; p.bits = L.o.bits;
+      p.x = at + int64_t(r0) * Hq * D; p.ldx = int64_t(Hq) * D; p.M = mr; p.K = Hq * D;
+      p.N = L.o.N; p.bits = L.o.bits;
       p.wq = L.o.wq;
       p.scales = static_cast<const bf16*>(L.o.scales);
       p.biases = static_cast<const bf16*>(L.o.biases);
-      p.resid = h; p.ldr = H; p.out = h; p.ldo = H;
-      p.ssq_out = buf->ssq_b; p.ssq_stride = kSsqStride;
-      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_RESID, R);
+      p.resid = h + int64_t(r0) * H; p.ldr = H; p.out = h + int64_t(r0) * H; p.ldo = H;
+      p.ssq_out = buf->ssq_b + r0; p.ssq_stride = kSsqStride;
+      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_RESID, mr);
       ssq_n_b = pl.nw > 0 ? (p.N + 16 * pl.nw - 1) / (16 * pl.nw) : 0;  // run() rejects nw == 0
       DSPARK_TRY(qmm::run(p, qmm::EPI_RESID, &pl, s));
     }
     // gate/up projection + post-attention RMSNorm + SwiGLU
-    {
+    for (int r0 = 0; r0 < R; r0 += kChunk) {
+      const int mr = std::min(kChunk, R - r0);
       qmm::QmmParams p;
-      p.x = h; p.ldx = H; p.M = R; p.K = H; p.N = L.gate_up.N; p.bits = L.gate_up.bits;
+      p.x = h + int64_t(r0) * H; p.ldx = H; p.M = mr; p.K = H; p.N = L.gate_up.N;
+      p.bits = L.gate_up.bits;
       p.wq = L.gate_up.wq;
       p.scales = static_cast<const bf16*>(L.gate_up.scales);
       p.biases = static_cast<const bf16*>(L.gate_up.biases);
       p.norm_w = static_cast<const bf16*>(L.post_norm);
-      p.ssq_in = buf->ssq_b; p.ssq_n = ssq_n_b; p.ssq_stride = kSsqStride; p.eps = m->rms_eps;
-      p.out = act; p.ldo = I; p.n_act = I;
-      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_SWIGLU, R);
+      p.ssq_in = buf->ssq_b + r0; p.ssq_n = ssq_n_b; p.ssq_stride = kSsqStride; p.eps = m->rms_eps;
+      p.out = act + int64_t(r0) * I; p.ldo = I; p.n_act = I;
+      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_SWIGLU, mr);
       DSPARK_TRY(qmm::run(p, qmm::EPI_SWIGLU, &pl, s));
     }
     // down projection + residual + statistics for the next input norm
-    {
+    for (int r0 = 0; r0 < R; r0 += kChunk) {
+      const int mr = std::min(kChunk, R - r0);
       qmm::QmmParams p;
-      p.x = act; p.ldx = I; p.M = R; p.K = I; p.N = L.down.N; p.bits = L.down.bits;
+      p.x = act + int64_t(r0) * I; p.ldx = I; p.M = mr; p.K = I; p.N = L.down.N; p.bits = L.down.bits;
       p.wq = L.down.wq;
       p.scales = static_cast<const bf16*>(L.down.scales);
       p.biases = static_cast<const bf16*>(L.down.biases);
-      p.resid = h; p.ldr = H; p.out = h; p.ldo = H;
-      p.ssq_out = buf->ssq_a; p.ssq_stride = kSsqStride;
-      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_RESID, R);
+      p.resid = h + int64_t(r0) * H; p.ldr = H; p.out = h + int64_t(r0) * H; p.ldo = H;
+      p.ssq_out = buf->ssq_a + r0; p.ssq_stride = kSsqStride;
+      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_RESID, mr);
       ssq_n = pl.nw > 0 ? (p.N + 16 * pl.nw - 1) / (16 * pl.nw) : 0;  // run() rejects nw == 0
-      ssq_cur = buf->ssq_a;
       DSPARK_TRY(qmm::run(p, qmm::EPI_RESID, &pl, s));
     }
+    ssq_cur = buf->ssq_a;
   }
   // final RMSNorm + lm_head
-  {
+  for (int r0 = 0; r0 < R; r0 += kChunk) {
+    const int mr = std::min(kChunk, R - r0);
     qmm::QmmParams p;
-    p.x = h; p.ldx = H; p.M = R; p.K = H; p.N = m->lm_head.N; p.bits = m->lm_head.bits;
+    p.x = h + int64_t(r0) * H; p.ldx = H; p.M = mr; p.K = H; p.N = m->lm_head.N;
+    p.bits = m->lm_head.bits;
     p.wq = m->lm_head.wq;
     p.scales = static_cast<const bf16*>(m->lm_head.scales);
     p.biases = static_cast<const bf16*>(m->lm_head.biases);
     p.norm_w = static_cast<const bf16*>(m->final_norm);
-    p.ssq_in = ssq_cur; p.ssq_n = ssq_n; p.ssq_stride = kSsqStride; p.eps = m->rms_eps;
-    p.out = static_cast<bf16*>(logits); p.ldo = ld_logits;
-    qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_PLAIN, R);
+    p.ssq_in = ssq_cur + r0; p.ssq_n = ssq_n; p.ssq_stride = kSsqStride; p.eps = m->rms_eps;
+    p.out = static_cast<bf16*>(logits) + int64_t(r0) * ld_logits; p.ldo = ld_logits;
+    qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_PLAIN, mr);
     DSPARK_TRY(qmm::run(p, qmm::EPI_PLAIN, &pl, s));
   }
   return DSPARK_OK;

@@ -141,6 +141,11 @@ __global__ void accept_kernel(const int32_t* tt, const int32_t* ids, const int32
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   const int r0 = cu[b], r1 = cu[b + 1];
+  if (r1 <= r0) {  // an idle slot (no rows this step): nothing accepted, length unchanged
+    if (n_accept) n_accept[b] = 0;
+    if (next_tok) next_tok[b] = -1;
+    return;
+  }
   const int cap = r1 - r0 - 1;
   int n = 0;
   while (n < cap && ids[r0 + 1 + n] == tt[r0 + n]) ++n;

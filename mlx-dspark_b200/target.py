@@ -93,13 +93,31 @@ class Target:
     """Random-init Qwen3-shaped target with a per-slot KV pool and fused verify forward."""
 
     def __init__(self, cfg: Qwen3Config, *, device="cuda", seed: int = 0, kv_cap: int = 4096,
-                 slots: int = 1, max_rows: int = 32, std: float = 0.02):
+                 slots: int = 1, max_rows: int = 32, std: float = 0.02,
+                 slot_caps: list[int] | None = None):
+        """``slot_caps`` (one capacity per slot) switches the KV pools to a position-major
+        layout ``[sum(caps), Hk, D]`` where slot b owns positions ``[off_b, off_b + cap_b)``:
+        requests of very different lengths then share the pool without each reserving the
+        longest one's room. Without it every slot holds ``kv_cap`` positions
+        (``[slots, Hk, kv_cap, D]``). A slot's cached length must stay within its capacity
+        (the forward's cache write only bounds positions by the largest capacity)."""
         self.cfg = cfg
         self.device = torch.device(device)
         require_cuda(torch.empty(1, device=self.device))
-        self.kv_cap = int(kv_cap)
-        self.slots = int(slots)
         self.max_rows = int(max_rows)
+        if slot_caps is not None:
+            self.slot_caps = [int(c) for c in slot_caps]
+            self.slots = len(self.slot_caps)
+            self.kv_cap = max(self.slot_caps)
+            self.position_major = True
+            self._slot_base = [0]
+            for c in self.slot_caps[:-1]:
+                self._slot_base.append(self._slot_base[-1] + c)
+        else:
+            self.kv_cap = int(kv_cap)
+            self.slots = int(slots)
+            self.slot_caps = [self.kv_cap] * self.slots
+            self.position_major = False
         g = torch.Generator(device=self.device).manual_seed(seed)
         H, D, Hq, Hk, I = cfg.hidden, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads, cfg.intermediate
         bits = cfg.bits
@@ -123,10 +141,8 @@ class Target:
                 "down": rq(H, I),
                 "in_norm": norm_w(H), "post_norm": norm_w(H),
                 "q_norm": norm_w(D), "k_norm": norm_w(D),
-                "k_cache": torch.zeros((self.slots, Hk, self.kv_cap, D), dtype=torch.bfloat16,
-                                       device=dev),
-                "v_cache": torch.zeros((self.slots, Hk, self.kv_cap, D), dtype=torch.bfloat16,
-                                       device=dev),
+                "k_cache": self._pool(),
+                "v_cache": self._pool(),
             }
             self.layers.append(layer)
         self.final_norm = norm_w(H)
@@ -136,8 +152,30 @@ class Target:
 
     # ----------------------------------------------------------------- C structs / buffers
 
+    def _pool(self) -> torch.Tensor:
+        D, Hk = self.cfg.head_dim, self.cfg.n_kv_heads
+        if self.position_major:
+            return torch.zeros((sum(self.slot_caps), Hk, D), dtype=torch.bfloat16,
+                               device=self.device)
+        return torch.zeros((self.slots, Hk, self.kv_cap, D), dtype=torch.bfloat16,
+                           device=self.device)
+
+    def kv_strides(self) -> tuple[int, int]:
+        """(head stride, position stride) of the pools, in elements."""
+        D, Hk = self.cfg.head_dim, self.cfg.n_kv_heads
+        return (D, Hk * D) if self.position_major else (self.kv_cap * D, D)
+
+    def slot_view(self, layer: int, slot: int, which: str = "k") -> torch.Tensor:
+        """``[Hk, cap, D]`` view of one slot's keys or values."""
+        pool = self.layers[layer][f"{which}_cache"]
+        if self.position_major:
+            b0 = self._slot_base[slot]
+            return pool[b0 : b0 + self.slot_caps[slot]].permute(1, 0, 2)
+        return pool[slot]
+
     def _alloc_buffers(self):
         cfg, dev, R = self.cfg, self.device, self.max_rows
+        rows_cap = max(32, R)
         H, D, Hq, I = cfg.hidden, cfg.head_dim, cfg.n_heads, cfg.intermediate
         B = self.slots
         e = dict(device=dev)
@@ -146,8 +184,8 @@ class Target:
             "xq": torch.empty((R, Hq * D), dtype=torch.bfloat16, **e),
             "attn": torch.empty((R, Hq * D), dtype=torch.bfloat16, **e),
             "act": torch.empty((R, I), dtype=torch.bfloat16, **e),
-            "ssq_a": torch.zeros(1024 * 32, dtype=torch.float32, **e),
-            "ssq_b": torch.zeros(1024 * 32, dtype=torch.float32, **e),
+            "ssq_a": torch.zeros(1024 * rows_cap, dtype=torch.float32, **e),
+            "ssq_b": torch.zeros(1024 * rows_cap, dtype=torch.float32, **e),
             "inv_freq": torch.empty(D // 2, dtype=torch.float32, **e),
             "row_pos": torch.zeros(R, dtype=torch.int32, **e),
             "row_kv": torch.zeros(R, dtype=torch.int64, **e),
@@ -160,6 +198,7 @@ class Target:
                                                        self.kv_cap))
         self.buf["attn_ws"] = torch.empty(max(ws, 16), dtype=torch.uint8, **e)
         self.logits = torch.empty((R, cfg.vocab), dtype=torch.bfloat16, **e)
+        self.rows_cap = rows_cap
 
     def _build_structs(self):
         cfg = self.cfg
@@ -171,20 +210,23 @@ class Target:
                                 ptr(L["in_norm"]), ptr(L["post_norm"]), ptr(L["q_norm"]),
                                 ptr(L["k_norm"]), ptr(L["k_cache"]), ptr(L["v_cache"]))
         self._layers_c = arr
+        k_sh, k_ss = self.kv_strides()
         self._model_c = _lib.Model(cfg.n_layers, cfg.hidden, cfg.n_heads, Hk, D,
                                    cfg.intermediate, cfg.vocab, cfg.rms_eps, cfg.rope_theta,
                                    _qw_struct(self.embed), _qw_struct(self.lm_head),
                                    ptr(self.final_norm), arr,
-                                   self.kv_cap * D, D, self.kv_cap * D, D, self.kv_cap)
+                                   k_sh, k_ss, k_sh, k_ss, self.kv_cap)
         b = self.buf
         self._buf_c = _lib.FwdBuffers(
             ptr(b["h"]), ptr(b["xq"]), ptr(b["attn"]), ptr(b["act"]), ptr(b["ssq_a"]),
             ptr(b["ssq_b"]), ptr(b["inv_freq"]), ptr(b["row_pos"]), ptr(b["row_kv"]),
             ptr(b["kv_len"]), ptr(b["row_start"]), ptr(b["q_len"]), ptr(b["kv_off"]),
-            ptr(b["attn_ws"]), b["attn_ws"].numel())
+            ptr(b["attn_ws"]), b["attn_ws"].numel(), self.rows_cap)
 
     def slot_offset(self, slot: int) -> int:
         """Element offset of a request slot inside each layer's K/V pool."""
+        if self.position_major:
+            return self._slot_base[slot] * self.cfg.n_kv_heads * self.cfg.head_dim
         return slot * self.cfg.n_kv_heads * self.kv_cap * self.cfg.head_dim
 
     # ----------------------------------------------------------------- reference API

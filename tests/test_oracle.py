@@ -282,3 +282,18 @@ def test_rmsnorm_rope_silu_definitions():
     r = oracle.rope(np.array([[[1.0, 0, 0, 0, 0, 0, 0, 0]]], np.float32), [np.pi / 2], 1e6)
     assert abs(r[0, 0, 4] - 1.0) < 1e-2 and abs(r[0, 0, 0]) < 1e-2
     assert abs(float(oracle.silu_mul(np.float32(1.0), np.float32(2.0))) - 2 / (1 + np.exp(-1))) < 1e-2
+
+
+def test_partition_requests_balances_kv():
+    """Data-parallel placement: every request lands on exactly one rank and the ranks' summed
+    KV lengths stay within one request of each other (longest-first greedy)."""
+    import mlx_dspark_b200  # noqa: F401  (ctypes load only; no GPU call)
+    from mlx_dspark_b200.batch_engine import partition_requests
+
+    rng = np.random.default_rng(0)
+    lengths = [int(x) for x in np.exp(rng.uniform(np.log(256), np.log(16384), 256))]
+    for world in (1, 2, 4, 8):
+        parts = partition_requests(lengths, world)
+        assert sorted(i for p in parts for i in p) == list(range(256))
+        loads = [sum(lengths[i] for i in p) for p in parts]
+        assert max(loads) - min(loads) <= max(lengths)
