@@ -61,6 +61,12 @@ def parse():
     ap.add_argument("--copies", type=int, default=48)
     ap.add_argument("--lengths", type=int, nargs="+", default=[1024, 4096, 16384, 32768])
     ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--batch", action="store_true",
+                    help="BASELINE configs[4]: continuous-batching engine, requests split "
+                         "data-parallel over the ranks")
+    ap.add_argument("--batch-requests", type=int, default=64,
+                    help="requests in the whole job (256 in configs[4]; the KV of 256 "
+                         "requests is ~147 GB, so N=1 runs a sample)")
     return ap.parse_args()
 
 
@@ -492,6 +498,101 @@ def run_micro(args):
                       "device_status": _lib.device_status(0)}), flush=True)
 
 
+def run_batch(args):
+    """BASELINE configs[4] at this job's scale: ``--batch-requests`` requests (prompt lengths
+    log-uniform 256-16k, seeded) placed data-parallel over the ranks by summed KV length; each
+    step every request verifies a block of U{8..16} rows and keeps a seeded accept length
+    U{0..block-1} (random-init weights never accept a random draft). Value = committed tokens
+    per second over the whole job (sum of accepted + 1), device-timed, max over ranks."""
+    import numpy as np
+    import torch
+
+    from mlx_dspark_b200.batch_engine import SpecBatch, partition_requests
+    from mlx_dspark_b200.target import QWEN3_8B, Target
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    import mlx_dspark_b200  # noqa: F401
+    from mlx_dspark_b200 import _lib
+
+    _lib.ensure_init(local)
+    rng = np.random.default_rng(2024)
+    n_req = int(args.batch_requests)
+    lengths = [int(x) for x in np.exp(rng.uniform(np.log(256), np.log(16384), n_req))]
+    mine = partition_requests(lengths, world)[rank]
+    total = args.warmup + args.steps
+    my_len = [lengths[i] for i in mine]
+    caps = [L + 17 * (total + 1) for L in my_len]
+    B = len(mine)
+    t = Target(QWEN3_8B, seed=1 + rank, slot_caps=caps, max_rows=max(32, 16 * B))
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    for L in t.layers:  # random K/V prefixes
+        for name in ("k_cache", "v_cache"):
+            pool = L[name]
+            for r0 in range(0, pool.shape[0], 1 << 16):
+                r1 = min(pool.shape[0], r0 + (1 << 16))
+                pool[r0:r1].normal_(generator=g)
+    eng = SpecBatch(t, max_block=17)
+    for L0 in my_len:
+        eng.admit(L0, int(rng.integers(0, QWEN3_8B.vocab)))
+    blocks = rng.integers(8, 17, (total, B))
+    accs = np.array([[int(rng.integers(0, b)) for b in row] for row in blocks])
+    drafts = torch.randint(0, QWEN3_8B.vocab, (total, B, 16), device=dev, dtype=torch.int32,
+                           generator=g)
+    acc_dev = torch.from_numpy(accs.astype(np.int32)).to(dev)
+
+    def step(i):
+        eng.step(drafts[i], [int(x) for x in blocks[i]], forced_accept=acc_dev[i])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.warmup, total):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    committed = float((accs[args.warmup :] + 1).sum())
+    rows = float(blocks[args.warmup :].sum())
+    if world > 1:
+        import torch.distributed as dist
+
+        tot = torch.tensor([committed, rows], dtype=torch.float64, device=dev)
+        dist.all_reduce(tot)
+        committed, rows = float(tot[0]), float(tot[1])
+    secs = ms / 1e3
+    kv_bytes = 2 * QWEN3_8B.n_layers * QWEN3_8B.n_kv_heads * QWEN3_8B.head_dim * 2 * sum(my_len)
+    out = {"metric": "batch-engine committed tok/s (Qwen3-8B 4-bit, continuous batching)",
+           "value": round(committed / secs, 1), "unit": "tok/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (random-init weights, random K/V prefixes, seeded blocks/accepts)",
+           "config": {"workload": f"BASELINE configs[4] at {n_req} requests (prompts "
+                                  "log-uniform 256-16k, blocks U{8..16}, accepts U{0..block-1})",
+                      "requests": n_req, "requests_rank0": B,
+                      "parallelism": f"dp{world} (requests partitioned by KV length)"},
+           "verify_rows_per_s": round(rows / secs, 1),
+           "rank0_kv_gb": round(kv_bytes / 1e9, 2),
+           "device_status": _lib.device_status(local)}
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
 # ----------------------------------------------------------------------------- reference arm
 
 def run_reference(args):
@@ -568,6 +669,8 @@ def main():
     args = parse()
     if args.micro:
         run_micro(args)
+    elif args.batch:
+        run_batch(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
