@@ -64,6 +64,10 @@ def parse():
     ap.add_argument("--batch", action="store_true",
                     help="BASELINE configs[4]: continuous-batching engine, requests split "
                          "data-parallel over the ranks")
+    ap.add_argument("--tp", action="store_true",
+                    help="BASELINE configs[3]: 32B-shaped 8-bit verify at 32k context, every "
+                         "projection column-sharded over the ranks (NCCL all-gathers)")
+    ap.add_argument("--tp-context", type=int, default=32768)
     ap.add_argument("--batch-requests", type=int, default=64,
                     help="requests in the whole job (256 in configs[4]; the KV of 256 "
                          "requests is ~147 GB, so N=1 runs a sample)")
@@ -593,6 +597,120 @@ def run_batch(args):
         print(json.dumps(out), flush=True)
 
 
+def run_tp(args):
+    """Qwen3-32B-shaped 8-bit target (64 layers, hidden 5120, GQA 64/8),
+    one request verifying 16-row blocks at 32k context, projections column-sharded over the
+    ranks with NCCL all-gathers between them (mlx_dspark_b200.target_tp). A step = verify
+    forward + argmax + accept + rollback to a seeded accept length, captured in one CUDA graph
+    (collectives included). value = verified rows per second of the one request (strong
+    scaling: the same work at every N)."""
+    import numpy as np
+    import torch
+
+    from mlx_dspark_b200.target import QWEN3_32B
+    from mlx_dspark_b200.target_tp import TPTarget
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        group = dist.group.WORLD
+    import mlx_dspark_b200  # noqa: F401
+    from mlx_dspark_b200 import _lib
+
+    _lib.ensure_init(local)
+    cfg, ctx, R = QWEN3_32B, int(args.tp_context), ROWS
+    t = TPTarget(cfg, rank, world, group=group, kv_cap=ctx + R * 18, seed=1, max_rows=R,
+                 device=dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+    for L in t.layers:
+        L["k_cache"][:, :ctx].normal_(generator=g)
+        L["v_cache"][:, :ctx].normal_(generator=g)
+    total = args.warmup + args.steps
+    rng = np.random.default_rng(99)
+    acc = rng.integers(0, R, total)
+    ids_all = torch.randint(0, cfg.vocab, (total, R), device=dev, dtype=torch.int32, generator=g)
+    nrej_all = torch.from_numpy((R - 1 - acc).astype(np.int32)).to(dev)
+    ids = torch.zeros(R, dtype=torch.int32, device=dev)
+    lens = torch.tensor([ctx], dtype=torch.int32, device=dev)
+    nrej = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = {"tt": torch.empty(R, dtype=torch.int32, device=dev),
+           "next": torch.empty(1, dtype=torch.int32, device=dev),
+           "cu": torch.tensor([0, R], dtype=torch.int32, device=dev)}
+
+    def body():
+        logits = t.verify(ids, lens)
+        s = torch.cuda.current_stream(dev).cuda_stream
+        _lib.check(_lib.lib.dspark_argmax(logits.data_ptr(), logits.stride(0), R, cfg.vocab,
+                                          out["tt"].data_ptr(), s))
+        _lib.check(_lib.lib.dspark_accept(out["tt"].data_ptr(), ids.data_ptr(),
+                                          out["cu"].data_ptr(), 1, None, out["next"].data_ptr(),
+                                          None, s))
+        _lib.check(_lib.lib.dspark_kv_rollback(lens.data_ptr(), nrej.data_ptr(), 1, s))
+
+    body()  # configure every kernel once, then capture the step
+    torch.cuda.synchronize()
+    lens.fill_(ctx)
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    before = int(_lib.lib.dspark_launch_count())
+    with torch.cuda.stream(side):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            body()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    launches = int(_lib.lib.dspark_launch_count()) - before
+
+    def step(i):
+        if i % 16 == 0:
+            lens.fill_(ctx)
+        ids.copy_(ids_all[i])
+        nrej.copy_(nrej_all[i : i + 1])
+        graph.replay()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.warmup, total):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    secs = ms / 1e3
+    w_bytes = cfg.weight_bytes() / world
+    kv_bytes = 2 * cfg.n_layers * (cfg.n_kv_heads // world) * cfg.head_dim * 2 * (ctx + 8 * R)
+    res = {"metric": "verify-block tok/s at Qwen3-32B-shaped 8-bit M=16 (32k context), "
+                     "tensor-parallel", "value": round(args.steps * R / secs, 1), "unit": "tok/s",
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (random-init N(0,0.02) weights quantized MLX-affine 8-bit g64; "
+                   "random tokens; random bf16 KV prefix)",
+           "config": {"workload": "qwen3-32b-shape 8-bit verify, 16-row blocks at 32k context "
+                                  "(BASELINE configs[3])",
+                      "parallelism": f"tp{world} (column-sharded projections, heads per rank, "
+                                     "NCCL all-gathers)"},
+           "per_gpu_hbm_bytes_per_step": int(w_bytes + kv_bytes),
+           "per_gpu_hbm_gbs": round((w_bytes + kv_bytes) / (ms / args.steps / 1e3) / 1e9, 1),
+           "gpu_launches": launches * args.steps, "device_status": _lib.device_status(local)}
+    del graph
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
 # ----------------------------------------------------------------------------- reference arm
 
 def run_reference(args):
@@ -671,6 +789,8 @@ def main():
         run_micro(args)
     elif args.batch:
         run_batch(args)
+    elif args.tp:
+        run_tp(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

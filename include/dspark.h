@@ -67,6 +67,57 @@ int dspark_qmm_ex(const void* x, int64_t ldx, int M, int K, const uint32_t* wq,
                   const void* scales, const void* biases, const void* bias, int N, int bits,
                   int group, void* out, int64_t ldo, void* stream);
 
+/* Epilogues of dspark_qmm_fused. */
+#define DSPARK_EPI_PLAIN 0   /* out = bf16(x . W^T) (+ bias) */
+#define DSPARK_EPI_RESID 1   /* out = bf16(bf16(x . W^T) + resid); ssq_out[tile][m] = sum out^2 */
+#define DSPARK_EPI_SWIGLU 2  /* rows gate/up interleaved in blocks of 32: out = silu(g) * u */
+#define DSPARK_EPI_QKROPE 3  /* Qwen3 q/k RMSNorm + rotate-half RoPE; q to q_out, k/v to caches */
+
+/* One quantized matmul with the verify forward's fused prologue / epilogues: the building
+ * block of a layer, e.g. for a forward whose projections are column-sharded over GPUs (each
+ * rank runs its shard and all-gathers). An optional RMSNorm prologue scales x by
+ * rsqrt(mean of the row's squares + eps) * norm_w, the mean taken from ssq_n partial sums
+ * ssq_in[e * ssq_stride + m]. x rows may be segmented (x_seg > 0): element k of row m at
+ * x + (k / x_seg) * x_seg_stride + m * ldx + k % x_seg, the [P, M, K/P] layout an all-gather of
+ * column shards produces. M <= 32. Same numerics as dspark_verify_forward's projections. */
+typedef struct {
+  const void* x;
+  int64_t ldx, x_seg, x_seg_stride;
+  int M, K, N, bits;
+  const uint32_t* wq;
+  const void* scales;
+  const void* biases;
+  void* out;
+  int64_t ldo;
+  int epilogue;                     /* DSPARK_EPI_* */
+  const void* bias;                 /* PLAIN: optional bf16 [N] */
+  const void* norm_w;               /* optional RMSNorm prologue weight [K] */
+  const float* ssq_in;
+  int ssq_n, ssq_stride;
+  float eps;
+  const void* resid;                /* RESID */
+  int64_t ldr;
+  float* ssq_out;
+  int n_act;                        /* SWIGLU: activation columns (N / 2) */
+  int hq, hk;                       /* QKROPE: local q / kv heads (head_dim 128) */
+  const void* q_norm;
+  const void* k_norm;
+  const float* inv_freq;            /* [64] from dspark_rope_inv_freq */
+  void* q_out;
+  int64_t ldq;
+  void* k_cache;
+  void* v_cache;
+  int64_t k_sh, k_ss, v_sh, v_ss;
+  int kv_cap;
+  const int32_t* row_pos;           /* [M] absolute positions */
+  const int64_t* row_kv;            /* [M] cache slot offsets (elements), or NULL */
+} dspark_qmm_args;
+
+int dspark_qmm_fused(const dspark_qmm_args* a, void* stream);
+
+/* RoPE frequencies theta^(-2i/head_dim), i < head_dim / 2, as the fused epilogue uses them. */
+int dspark_rope_inv_freq(float* inv_freq, int head_dim, float theta, void* stream);
+
 /* Launch geometry the QMM would use for [N, K] at `bits` (depends on the weight shape only,
  * so a row's result never depends on M): tile width, split-K cluster size, k per split,
  * pipeline depth. Mirrors skinny_qmm.plan/geometry (src/mlx_dspark/skinny_qmm.py:214-236). */

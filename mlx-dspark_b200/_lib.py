@@ -63,7 +63,24 @@ class FwdBuffers(C.Structure):
                 ("attn_ws_bytes", sz), ("rows_cap", i32)]
 
 
+class QmmArgs(C.Structure):
+    _fields_ = [("x", vp), ("ldx", i64), ("x_seg", i64), ("x_seg_stride", i64),
+                ("M", i32), ("K", i32), ("N", i32), ("bits", i32),
+                ("wq", vp), ("scales", vp), ("biases", vp), ("out", vp), ("ldo", i64),
+                ("epilogue", i32), ("bias", vp), ("norm_w", vp), ("ssq_in", vp),
+                ("ssq_n", i32), ("ssq_stride", i32), ("eps", f32),
+                ("resid", vp), ("ldr", i64), ("ssq_out", vp), ("n_act", i32),
+                ("hq", i32), ("hk", i32), ("q_norm", vp), ("k_norm", vp), ("inv_freq", vp),
+                ("q_out", vp), ("ldq", i64), ("k_cache", vp), ("v_cache", vp),
+                ("k_sh", i64), ("k_ss", i64), ("v_sh", i64), ("v_ss", i64), ("kv_cap", i32),
+                ("row_pos", vp), ("row_kv", vp)]
+
+
+EPI_PLAIN, EPI_RESID, EPI_SWIGLU, EPI_QKROPE = range(4)
+
 _SIGS = {
+    "dspark_qmm_fused": (i32, [C.POINTER(QmmArgs), vp]),
+    "dspark_rope_inv_freq": (i32, [vp, i32, f32, vp]),
     "dspark_version": (i32, []),
     "dspark_last_error": (C.c_char_p, []),
     "dspark_init": (i32, [i32]),

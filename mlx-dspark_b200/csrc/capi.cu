@@ -216,6 +216,57 @@ int dspark_qmm(const void* x, int M, int K, const uint32_t* wq, const void* scal
   return dspark_qmm_ex(x, K, M, K, wq, scales, biases, nullptr, N, bits, group, out, N, stream);
 }
 
+int dspark_qmm_fused(const dspark_qmm_args* a, void* stream) {
+  if (!a || !a->x || !a->wq || !a->scales || !a->biases)
+    return fail(DSPARK_ERR_ARG, "qmm_fused: null argument");
+  if (a->epilogue < qmm::EPI_PLAIN || a->epilogue > qmm::EPI_QKROPE)
+    return fail(DSPARK_ERR_ARG, "qmm_fused: epilogue %d", a->epilogue);
+  const int epi = a->epilogue;
+  if (epi != qmm::EPI_QKROPE && !a->out) return fail(DSPARK_ERR_ARG, "qmm_fused: null out");
+  if (epi == qmm::EPI_RESID && !a->resid) return fail(DSPARK_ERR_ARG, "qmm_fused: null resid");
+  if (epi == qmm::EPI_QKROPE &&
+      (!a->q_out || !a->k_cache || !a->v_cache || !a->row_pos || !a->inv_freq || !a->q_norm ||
+       !a->k_norm))
+    return fail(DSPARK_ERR_ARG, "qmm_fused: q/k-norm + RoPE epilogue needs its buffers");
+  if (a->norm_w && !a->ssq_in) return fail(DSPARK_ERR_ARG, "qmm_fused: norm prologue needs ssq_in");
+  qmm::QmmParams p;
+  p.x = static_cast<const bf16*>(a->x); p.ldx = a->ldx;
+  p.x_seg = a->x_seg; p.x_segstride = a->x_seg_stride;
+  p.M = a->M; p.K = a->K; p.N = a->N; p.bits = a->bits;
+  p.wq = a->wq;
+  p.scales = static_cast<const bf16*>(a->scales);
+  p.biases = static_cast<const bf16*>(a->biases);
+  p.bias = static_cast<const bf16*>(a->bias);
+  p.out = static_cast<bf16*>(a->out); p.ldo = a->ldo;
+  p.norm_w = static_cast<const bf16*>(a->norm_w);
+  p.ssq_in = a->ssq_in; p.ssq_n = a->ssq_n; p.ssq_stride = a->ssq_stride > 0 ? a->ssq_stride : 32;
+  p.eps = a->eps;
+  p.resid = static_cast<const bf16*>(a->resid); p.ldr = a->ldr; p.ssq_out = a->ssq_out;
+  p.n_act = a->n_act;
+  p.hq = a->hq; p.hk = a->hk;
+  p.qnorm = static_cast<const bf16*>(a->q_norm);
+  p.knorm = static_cast<const bf16*>(a->k_norm);
+  p.inv_freq = a->inv_freq;
+  p.qout = static_cast<bf16*>(a->q_out); p.ldq = a->ldq;
+  p.kcache = static_cast<bf16*>(a->k_cache);
+  p.vcache = static_cast<bf16*>(a->v_cache);
+  p.k_sh = a->k_sh; p.k_ss = a->k_ss; p.v_sh = a->v_sh; p.v_ss = a->v_ss;
+  p.kv_cap = a->kv_cap;
+  p.row_pos = a->row_pos; p.row_kv = a->row_kv;
+  if (epi == qmm::EPI_QKROPE) {
+    p.out = p.qout;
+    p.ldo = 0;
+  }
+  if (a->M < 1 || a->M > 32) return fail(DSPARK_ERR_UNSUPPORTED, "qmm_fused: M=%d (1..32)", a->M);
+  qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, epi, a->M);
+  return qmm::run(p, epi, &pl, as_stream(stream));
+}
+
+int dspark_rope_inv_freq(float* inv_freq, int head_dim, float theta, void* stream) {
+  if (!inv_freq || head_dim <= 0 || head_dim % 2) return fail(DSPARK_ERR_ARG, "rope_inv_freq: bad args");
+  return ops::fill_inv_freq(inv_freq, head_dim, theta, as_stream(stream));
+}
+
 int dspark_qmm_plan(int N, int K, int bits, int* tile_n, int* split_k, int* k_slice, int* stages) {
   if (bits != 4 && bits != 8) return fail(DSPARK_ERR_UNSUPPORTED, "qmm_plan: bits %d", bits);
   if (K <= 0 || K % 64 || N <= 0 || N % 8) return fail(DSPARK_ERR_UNSUPPORTED, "qmm_plan: shape");

@@ -14,6 +14,9 @@ enum Epilogue { EPI_PLAIN = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKROPE = 3 };
 struct QmmParams {
   const __nv_bfloat16* x = nullptr;  // [M, K] row stride ldx (elements)
   long ldx = 0;
+  // segmented rows (an all-gather's [P, M, K/P] output): k lives in segment k / x_seg at
+  // x + (k / x_seg) * x_segstride + m * ldx + k % x_seg (x_seg == 0: contiguous rows)
+  long x_seg = 0, x_segstride = 0;
   const uint32_t* wq = nullptr;      // [N, K*bits/32]
   const __nv_bfloat16* scales = nullptr;  // [N, K/64]
   const __nv_bfloat16* biases = nullptr;  // [N, K/64]

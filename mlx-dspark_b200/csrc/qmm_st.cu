@@ -477,8 +477,19 @@ __global__ void __launch_bounds__(NTHR, 1)
       if (tid == 0) {
         const uint32_t bytes = uint32_t(kvalid) * 2;
         mbar_arrive_expect_tx(xbar, bytes * uint32_t(p.M + (nrm ? 1 : 0)));
-        for (int m = 0; m < p.M; ++m)
-          bulk_load(xs + m * XP, p.x + (size_t)m * p.ldx + kbase, bytes, xbar);
+        for (int m = 0; m < p.M; ++m) {
+          if (p.x_seg == 0) {
+            bulk_load(xs + m * XP, p.x + (size_t)m * p.ldx + kbase, bytes, xbar);
+          } else {  // one copy per segment the slice touches
+            for (int k = kbase; k < kbase + kvalid;) {
+              const long seg = k / p.x_seg, off = k - seg * p.x_seg;
+              const int len = int(min(long(kbase + kvalid - k), p.x_seg - off));
+              bulk_load(xs + m * XP + (k - kbase) * 2,
+                        p.x + seg * p.x_segstride + (size_t)m * p.ldx + off, uint32_t(len) * 2, xbar);
+              k += len;
+            }
+          }
+        }
         if (nrm) bulk_load(nws, p.norm_w + kbase, bytes, xbar);
       }
     } else {
@@ -486,7 +497,10 @@ __global__ void __launch_bounds__(NTHR, 1)
       const uint32_t xa0 = smem_u32(xs);
       for (int idx = tid; idx < p.M * vchunks; idx += NC) {
         const int m = idx / vchunks, c = idx - m * vchunks;
-        cp_async_16_zfill(xa0 + uint32_t(xoff(m, c)), p.x + (size_t)m * p.ldx + kbase + c * 8, true);
+        const long k = kbase + c * 8;
+        const long seg = p.x_seg ? k / p.x_seg : 0;
+        const bf16* src = p.x + seg * p.x_segstride + (size_t)m * p.ldx + (k - seg * p.x_seg);
+        cp_async_16_zfill(xa0 + uint32_t(xoff(m, c)), src, true);
       }
       if (nrm)
         for (int c = tid; c < vchunks; c += NC)

@@ -1,0 +1,275 @@
+"""Column-sharded (tensor-parallel) verify forward of a dense Qwen3-shaped target over P GPUs.
+
+For 27B-class targets one GPU's HBM bandwidth is the limit, so every projection's output
+columns are split over P ranks (one process per GPU, NCCL over NVLink):
+
+* q/k/v: rank r owns query heads [r*Hq/P, (r+1)*Hq/P) and KV heads [r*Hk/P, ...). The QKV
+  launch normalizes, ropes and writes its heads' K/V into the rank's own cache, and the
+  verify attention runs over those heads only — attention needs no exchange.
+* O, gate/up, down, lm_head: rank r owns 1/P of the output columns (gate/up: 1/P of the
+  intermediate units, still interleaved in blocks of 32 so SwiGLU stays in the epilogue).
+* Between projections the shards are all-gathered: the attention output before O, the
+  updated hidden state (and its per-tile RMSNorm statistics) after O and after down, the
+  SwiGLU activations before down, and the vocab-sharded logits at the end. The gathered
+  ``[P, M, K/P]`` tensors feed the next projection directly: the QMM reads x as segmented
+  rows (``dspark_qmm_fused`` with ``x_seg``), so no transpose copy runs.
+
+Every rank holds the full embedding and norm weights and computes the same argmax / accept /
+rollback, so all ranks' cache lengths stay identical. Weights are generated from one seed as
+the full matrices and sliced, so any P yields the same model (the P-independence the parity
+tests check). The reference runs 27B targets on one Apple GPU (``src/mlx_dspark/target.py``
+dense path, ``:208-221``); this layer has no counterpart there.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib, quant
+from ._torch import ptr, require_cuda, stream_of
+from .target import Qwen3Config, _interleave32, _qw_struct  # noqa: F401
+
+
+def _rows(w: quant.QWeight, a: int, b: int) -> quant.QWeight:
+    return quant.QWeight(w.wq[a:b].contiguous(), w.scales[a:b].contiguous(),
+                         w.biases[a:b].contiguous(), w.bits)
+
+
+def _cat(*ws: quant.QWeight) -> quant.QWeight:
+    return quant.QWeight(torch.cat([w.wq for w in ws]), torch.cat([w.scales for w in ws]),
+                         torch.cat([w.biases for w in ws]), ws[0].bits)
+
+
+def shard_ranges(cfg: Qwen3Config, world: int, rank: int) -> dict:
+    """Row ranges of each full weight matrix that rank ``rank`` of ``world`` owns."""
+    H, D, Hq, Hk, I, V = (cfg.hidden, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads,
+                          cfg.intermediate, cfg.vocab)
+    for what, n in (("query heads", Hq), ("kv heads", Hk), ("hidden", H // 128),
+                    ("intermediate", I // 32), ("vocab", V // 8)):
+        if n % world:
+            raise ValueError(f"{what} ({n}) do not split over {world} ranks")
+    hq, hk = Hq // world, Hk // world
+    return {"q": (rank * hq * D, (rank + 1) * hq * D),
+            "k": (Hq * D + rank * hk * D, Hq * D + (rank + 1) * hk * D),
+            "v": (Hq * D + Hk * D + rank * hk * D, Hq * D + Hk * D + (rank + 1) * hk * D),
+            "hidden": (rank * H // world, (rank + 1) * H // world),
+            "inter": (rank * I // world, (rank + 1) * I // world),
+            "vocab": (rank * V // world, (rank + 1) * V // world)}
+
+
+class TPTarget:
+    """One rank of a P-way column-sharded target (``group``: the torch.distributed NCCL group;
+    ``None`` with ``world == 1``). :meth:`verify` has :meth:`Target.verify`'s contract."""
+
+    def __init__(self, cfg: Qwen3Config, rank: int, world: int, *, group=None, kv_cap: int = 4096,
+                 seed: int = 0, std: float = 0.02, max_rows: int = 32, device="cuda"):
+        self.cfg, self.rank, self.world, self.group = cfg, int(rank), int(world), group
+        self.device = torch.device(device)
+        require_cuda(torch.empty(1, device=self.device))
+        self.kv_cap, self.max_rows = int(kv_cap), int(max_rows)
+        P, r = self.world, self.rank
+        rg = shard_ranges(cfg, P, r)
+        self.ranges = rg
+        H, D, Hq, Hk, I = cfg.hidden, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads, cfg.intermediate
+        self.hq, self.hk = Hq // P, Hk // P
+        dev = self.device
+        g = torch.Generator(device=dev).manual_seed(seed)
+
+        def full(n, k):
+            return quant.random_qweight(n, k, cfg.bits, std=std, device=dev, generator=g)
+
+        def norm_w(n):
+            return (1.0 + 0.05 * torch.randn(n, device=dev, generator=g)).to(torch.bfloat16)
+
+        self.embed = full(cfg.vocab, H)
+        self.layers = []
+        for _ in range(cfg.n_layers):
+            qkv = full((Hq + 2 * Hk) * D, H)
+            o = full(H, Hq * D)
+            gate, up = full(I, H), full(I, H)
+            down = full(H, I)
+            a, b = rg["inter"]
+            h0, h1 = rg["hidden"]
+            layer = {
+                "qkv": _cat(_rows(qkv, *rg["q"]), _rows(qkv, *rg["k"]), _rows(qkv, *rg["v"])),
+                "o": _rows(o, h0, h1),
+                "gate_up": _interleave32(_rows(gate, a, b), _rows(up, a, b)),
+                "down": _rows(down, h0, h1),
+                "in_norm": norm_w(H), "post_norm": norm_w(H),
+                "q_norm": norm_w(D), "k_norm": norm_w(D),
+                "k_cache": torch.zeros((self.hk, self.kv_cap, D), dtype=torch.bfloat16, device=dev),
+                "v_cache": torch.zeros((self.hk, self.kv_cap, D), dtype=torch.bfloat16, device=dev),
+            }
+            del qkv, o, gate, up, down
+            self.layers.append(layer)
+        self.final_norm = norm_w(H)
+        lm = full(cfg.vocab, H)
+        self.lm_head = _rows(lm, *rg["vocab"])
+        del lm
+        torch.cuda.empty_cache()
+        self._alloc()
+
+    # ------------------------------------------------------------------ buffers
+
+    def _alloc(self):
+        cfg, P, R, dev = self.cfg, self.world, self.max_rows, self.device
+        H, D, I, V = cfg.hidden, cfg.head_dim, cfg.intermediate, cfg.vocab
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.hs = H // P                       # hidden columns per rank
+        self.tiles = self.hs // 128            # RMSNorm statistics entries per rank
+        self.b = {
+            "h0": torch.empty((R, H), **bf),                    # embedding output (replicated)
+            "h_seg": [torch.empty((P, R, self.hs), **bf) for _ in range(2)],
+            "h_shard": torch.empty((R, self.hs), **bf),
+            "xq": torch.empty((R, self.hq * D), **bf),
+            "attn": torch.empty((R, self.hq * D), **bf),
+            "attn_seg": torch.empty((P, R, self.hq * D), **bf),
+            "act": torch.empty((R, I // P), **bf),
+            "act_seg": torch.empty((P, R, I // P), **bf),
+            "logits": torch.empty((R, V // P), **bf),
+            "logits_seg": torch.empty((P, R, V // P), **bf),
+            "logits_full": torch.empty((R, V), **bf),
+            "ssq0": torch.zeros(1024 * 32, dtype=torch.float32, device=dev),
+            "ssq": torch.zeros((self.tiles, 32), dtype=torch.float32, device=dev),
+            "ssq_seg": torch.zeros((P, self.tiles, 32), dtype=torch.float32, device=dev),
+            "inv_freq": torch.empty(D // 2, dtype=torch.float32, device=dev),
+            "row_pos": torch.zeros(R, dtype=torch.int32, device=dev),
+            "row_kv": torch.zeros(R, dtype=torch.int64, device=dev),
+            "kv_len": torch.zeros(1, dtype=torch.int32, device=dev),
+            "row_start": torch.zeros(1, dtype=torch.int32, device=dev),
+            "q_len": torch.zeros(1, dtype=torch.int32, device=dev),
+            "kv_off": torch.zeros(1, dtype=torch.int64, device=dev),
+        }
+        b = self.b
+        # the split plan (and its workspace) depends on the block height: size for the largest
+        ws = max(int(_lib.lib.dspark_verify_attn_workspace(1, self.hq, self.hk, qL, D, L))
+                 for qL in range(1, R + 1) for L in (self.kv_cap, max(1, self.kv_cap // 2)))
+        b["attn_ws"] = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+        # the single-request packing entry fills row_pos / kv_len through this struct
+        self._prep = _lib.FwdBuffers(None, None, None, None, None, None, None, ptr(b["row_pos"]),
+                                     ptr(b["row_kv"]), ptr(b["kv_len"]), ptr(b["row_start"]),
+                                     ptr(b["q_len"]), ptr(b["kv_off"]), None, 0, R)
+
+    def _gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        if self.world == 1:
+            out.view(-1).copy_(inp.reshape(-1))
+            return
+        import torch.distributed as dist
+
+        dist.all_gather_into_tensor(out, inp, group=self.group)
+
+    def _qmm(self, s, w: quant.QWeight, x, ldx, M, K, epi, out=None, ldo=0, *, x_seg=0,
+             x_seg_stride=0, norm_w=None, ssq_in=None, ssq_n=0, resid=None, ldr=0, ssq_out=None,
+             n_act=0, layer=None, lens_pos=None):
+        a = _lib.QmmArgs()
+        a.x, a.ldx, a.x_seg, a.x_seg_stride = ptr(x), ldx, x_seg, x_seg_stride
+        a.M, a.K, a.N, a.bits = M, K, int(w.wq.shape[0]), w.bits
+        a.wq, a.scales, a.biases = ptr(w.wq), ptr(w.scales), ptr(w.biases)
+        a.out, a.ldo, a.epilogue = ptr(out), ldo, epi
+        a.norm_w, a.ssq_in, a.ssq_n, a.ssq_stride = ptr(norm_w), ptr(ssq_in), ssq_n, 32
+        a.eps = self.cfg.rms_eps
+        a.resid, a.ldr, a.ssq_out, a.n_act = ptr(resid), ldr, ptr(ssq_out), n_act
+        if epi == _lib.EPI_QKROPE:
+            b, D = self.b, self.cfg.head_dim
+            a.hq, a.hk = self.hq, self.hk
+            a.q_norm, a.k_norm, a.inv_freq = ptr(layer["q_norm"]), ptr(layer["k_norm"]), ptr(b["inv_freq"])
+            a.q_out, a.ldq = ptr(b["xq"]), self.hq * D
+            a.k_cache, a.v_cache = ptr(layer["k_cache"]), ptr(layer["v_cache"])
+            a.k_sh, a.k_ss, a.v_sh, a.v_ss = self.kv_cap * D, D, self.kv_cap * D, D
+            a.kv_cap = self.kv_cap
+            a.row_pos, a.row_kv = ptr(b["row_pos"]), ptr(b["row_kv"])
+        _lib.check(_lib.lib.dspark_qmm_fused(C.byref(a), s))
+
+    # ------------------------------------------------------------------ forward
+
+    def verify(self, ids: torch.Tensor, lens: torch.Tensor, *, L_max: int | None = None) -> torch.Tensor:
+        """Verify forward of ``ids`` (int32 ``[R]``) at the cached length ``lens[0]`` (advanced
+        by R on the device); returns the full bf16 logits ``[R, vocab]`` on every rank."""
+        cfg, P, r, b = self.cfg, self.world, self.rank, self.b
+        R = int(ids.numel())
+        if not 1 <= R <= self.max_rows:
+            raise _lib.DSparkUnsupported(_lib.ERR_UNSUPPORTED, f"R={R} rows")
+        H, D, Hq, I, V = cfg.hidden, cfg.head_dim, cfg.n_heads, cfg.intermediate, cfg.vocab
+        hs, T = self.hs, self.tiles
+        s = stream_of(ids)
+        _lib.check(_lib.lib.dspark_verify_prepare(ptr(lens), R, C.byref(self._prep), s))
+        _lib.check(_lib.lib.dspark_rope_inv_freq(ptr(b["inv_freq"]), D, cfg.rope_theta, s))
+        _lib.check(_lib.lib.dspark_embed(ptr(ids), R, ptr(self.embed.wq), ptr(self.embed.scales),
+                                         ptr(self.embed.biases), cfg.vocab, H, cfg.bits,
+                                         ptr(b["h0"]), ptr(b["ssq0"]), s))
+        Lm = self.kv_cap if L_max is None else int(L_max)
+        # current hidden state: contiguous (embedding) or segmented [P, R, hs] (after a gather)
+        x, ldx, xseg, xss = b["h0"], H, 0, 0
+        ssq, ssq_n = b["ssq0"], 1
+        resid, ldr = b["h0"][:, r * hs:], H
+        cur = 0
+        q_st = _lib.i64_array([0, D, self.hq * D])
+        k_st = _lib.i64_array([0, self.kv_cap * D, D])
+        for L in self.layers:
+            self._qmm(s, L["qkv"], x, ldx, R, H, _lib.EPI_QKROPE, x_seg=xseg, x_seg_stride=xss,
+                      norm_w=L["in_norm"], ssq_in=ssq, ssq_n=ssq_n, layer=L)
+            _lib.check(_lib.lib.dspark_verify_attn(
+                ptr(b["xq"]), q_st, ptr(L["k_cache"]), k_st, ptr(L["v_cache"]), k_st, 1, self.hq,
+                self.hk, R, D, Lm, ptr(b["kv_len"]), float(D ** -0.5), 1, None, ptr(b["attn"]),
+                q_st, ptr(b["attn_ws"]), b["attn_ws"].numel(), s))
+            self._gather(b["attn_seg"], b["attn"])
+            # O: x = all heads' attention ([P, R, hq*D] segments), residual = own hidden shard
+            self._qmm(s, L["o"], b["attn_seg"], self.hq * D, R, Hq * D, _lib.EPI_RESID,
+                      b["h_shard"], hs, x_seg=self.hq * D, x_seg_stride=self.max_rows * self.hq * D,
+                      resid=resid, ldr=ldr, ssq_out=b["ssq"])
+            mid = b["h_seg"][cur]
+            self._gather(mid, b["h_shard"])
+            self._gather(b["ssq_seg"], b["ssq"])
+            # gate/up: post-attention norm over the gathered hidden state, SwiGLU shard
+            self._qmm(s, L["gate_up"], mid, hs, R, H, _lib.EPI_SWIGLU, b["act"], I // P,
+                      x_seg=hs, x_seg_stride=self.max_rows * hs, norm_w=L["post_norm"],
+                      ssq_in=b["ssq_seg"], ssq_n=P * T, n_act=I // P)
+            self._gather(b["act_seg"], b["act"])
+            # down: x = all activations, residual = own shard of the mid state
+            self._qmm(s, L["down"], b["act_seg"], I // P, R, I, _lib.EPI_RESID, b["h_shard"], hs,
+                      x_seg=I // P, x_seg_stride=self.max_rows * (I // P), resid=mid[r], ldr=hs,
+                      ssq_out=b["ssq"])
+            cur ^= 1
+            nxt = b["h_seg"][cur]
+            self._gather(nxt, b["h_shard"])
+            self._gather(b["ssq_seg"], b["ssq"])
+            x, ldx, xseg, xss = nxt, hs, hs, self.max_rows * hs
+            ssq, ssq_n = b["ssq_seg"], P * T
+            resid, ldr = nxt[r], hs
+        # final norm + vocab-sharded lm_head, logits gathered
+        self._qmm(s, self.lm_head, x, ldx, R, H, _lib.EPI_PLAIN, b["logits"], V // P, x_seg=xseg,
+                  x_seg_stride=xss, norm_w=self.final_norm, ssq_in=ssq, ssq_n=ssq_n)
+        self._gather(b["logits_seg"], b["logits"])
+        b["logits_full"][:R].view(R, P, V // P).copy_(b["logits_seg"][:, :R].transpose(0, 1))
+        return b["logits_full"][:R]
+
+    def accept_and_rollback(self, logits, ids, lens, out=None) -> dict:
+        """Greedy accept + rollback, identical on every rank (the ranks' caches stay in step)."""
+        R = int(ids.numel())
+        dev = ids.device
+        if out is None:
+            out = {"tt": torch.empty(R, dtype=torch.int32, device=dev),
+                   "n": torch.empty(1, dtype=torch.int32, device=dev),
+                   "next": torch.empty(1, dtype=torch.int32, device=dev),
+                   "cu": torch.tensor([0, R], dtype=torch.int32, device=dev)}
+        s = stream_of(ids)
+        _lib.check(_lib.lib.dspark_argmax(ptr(logits), logits.stride(0), R, self.cfg.vocab,
+                                          ptr(out["tt"]), s))
+        _lib.check(_lib.lib.dspark_accept(ptr(out["tt"]), ptr(ids), ptr(out["cu"]), 1,
+                                          ptr(out["n"]), ptr(out["next"]), ptr(lens), s))
+        return out
+
+    def oracle_weights(self) -> dict:
+        """Host copies of the full weights in the oracle's format (one rank, P == 1 only)."""
+        if self.world != 1:
+            raise ValueError("the full weights exist on a single rank only when P == 1")
+        from .target import Target
+
+        return Target.oracle_weights(self)
+
+    def oracle_config(self) -> dict:
+        c = self.cfg
+        return {"hidden": c.hidden, "n_heads": c.n_heads, "n_kv_heads": c.n_kv_heads,
+                "head_dim": c.head_dim, "rms_eps": c.rms_eps, "rope_theta": c.rope_theta}
