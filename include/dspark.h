@@ -73,8 +73,10 @@ int dspark_qmm_ex(const void* x, int64_t ldx, int M, int K, const uint32_t* wq,
 #define DSPARK_EPI_SWIGLU 2  /* rows gate/up interleaved in blocks of 32: out = silu(g) * u */
 #define DSPARK_EPI_QKROPE 3  /* Qwen3 q/k RMSNorm + rotate-half RoPE; q to q_out, k/v to caches */
 
-/* One quantized matmul with the verify forward's fused prologue / epilogues: the building
- * block of a layer, e.g. for a forward whose projections are column-sharded over GPUs (each
+/* One quantized matmul with the verify forward's fused prologue / epilogues (no single
+ * reference counterpart: it is one QuantizedLinear call of mlx-lm's Qwen3 layer, reached from
+ * src/mlx_dspark/target.py:208-221, with its neighbouring norm / residual / SwiGLU / RoPE
+ * fused): the building block of a layer, e.g. for a forward whose projections are column-sharded over GPUs (each
  * rank runs its shard and all-gathers). An optional RMSNorm prologue scales x by
  * rsqrt(mean of the row's squares + eps) * norm_w, the mean taken from ssq_n partial sums
  * ssq_in[e * ssq_stride + m]. x rows may be segmented (x_seg > 0): element k of row m at
