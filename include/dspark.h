@@ -113,6 +113,8 @@ typedef struct {
   int kv_cap;
   const int32_t* row_pos;           /* [M] absolute positions */
   const int64_t* row_kv;            /* [M] cache slot offsets (elements), or NULL */
+  int ssq_seg;                      /* > 0: entry e of ssq_in at (e / ssq_seg) * ssq_seg_stride */
+  int64_t ssq_seg_stride;           /*      + (e % ssq_seg) * ssq_stride (gathered statistics) */
 } dspark_qmm_args;
 
 int dspark_qmm_fused(const dspark_qmm_args* a, void* stream);

@@ -240,6 +240,7 @@ int dspark_qmm_fused(const dspark_qmm_args* a, void* stream) {
   p.out = static_cast<bf16*>(a->out); p.ldo = a->ldo;
   p.norm_w = static_cast<const bf16*>(a->norm_w);
   p.ssq_in = a->ssq_in; p.ssq_n = a->ssq_n; p.ssq_stride = a->ssq_stride > 0 ? a->ssq_stride : 32;
+  p.ssq_seg = a->ssq_seg; p.ssq_segstride = a->ssq_seg_stride;
   p.eps = a->eps;
   p.resid = static_cast<const bf16*>(a->resid); p.ldr = a->ldr; p.ssq_out = a->ssq_out;
   p.n_act = a->n_act;

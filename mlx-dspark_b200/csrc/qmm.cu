@@ -780,7 +780,7 @@ int run(const QmmParams& p_in, int epi, const QmmPlan* plan_in, cudaStream_t str
   if (pl.sct && ((reinterpret_cast<uintptr_t>(p.scales) & 15) || (reinterpret_cast<uintptr_t>(p.biases) & 15)))
     pl.sct = false;
   if (!pl.sct && pl.engine != 0) pl = plan_mma(p.N, p.K, p.bits, epi, epi == EPI_QKROPE ? 128 : 0, rt);
-  if (p.x_seg != 0) {
+  if (p.x_seg != 0 || p.ssq_seg != 0) {
     if (pl.engine != 2)
       return fail(DSPARK_ERR_UNSUPPORTED, "qmm: segmented x rows need the streaming engine (K %% 512 == 0)");
     if (p.x_seg % 8 || p.x_segstride % 8 || p.x_seg <= 0)

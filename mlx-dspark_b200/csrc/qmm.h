@@ -32,6 +32,10 @@ struct QmmParams {
   const float* ssq_in = nullptr;
   int ssq_n = 0;
   int ssq_stride = 32;
+  // segmented statistics (an all-gather of per-rank entries): entry e at
+  // (e / ssq_seg) * ssq_segstride + (e % ssq_seg) * ssq_stride (ssq_seg == 0: e * ssq_stride)
+  int ssq_seg = 0;
+  long ssq_segstride = 0;
   float eps = 1e-6f;
   // EPI_RESID: out = bf16(bf16(acc) + resid); ssq_out[ntile*ssq_stride + m] = sum(out^2)
   const __nv_bfloat16* resid = nullptr;

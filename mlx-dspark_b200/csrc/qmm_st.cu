@@ -519,7 +519,11 @@ __global__ void __launch_bounds__(NTHR, 1)
       for (int m = warp; m < RP; m += NWC) {
         float ss = 0.f;
         if (m < p.M)
-          for (int e = lane; e < p.ssq_n; e += 32) ss += __ldcg(&p.ssq_in[e * p.ssq_stride + m]);
+          for (int e = lane; e < p.ssq_n; e += 32) {
+            const long at = p.ssq_seg ? (e / p.ssq_seg) * p.ssq_segstride + long(e % p.ssq_seg) * p.ssq_stride
+                                      : long(e) * p.ssq_stride;
+            ss += __ldcg(&p.ssq_in[at + m]);
+          }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         if (lane == 0) rsm[m] = m < p.M ? rsqrtf(ss / float(p.K) + p.eps) : 0.f;

@@ -119,10 +119,15 @@ class TPTarget:
         bf = dict(dtype=torch.bfloat16, device=dev)
         self.hs = H // P                       # hidden columns per rank
         self.tiles = self.hs // 128            # RMSNorm statistics entries per rank
+        # a rank's hidden shard [R, hs] bf16 and its RMSNorm statistics [tiles, 32] fp32 travel
+        # in one buffer (one all-gather): pack = [h shard | statistics]
+        self.hbytes = R * self.hs * 2
+        self.pack = self.hbytes + self.tiles * 32 * 4
+        u8 = dict(dtype=torch.uint8, device=dev)
         self.b = {
             "h0": torch.empty((R, H), **bf),                    # embedding output (replicated)
-            "h_seg": [torch.empty((P, R, self.hs), **bf) for _ in range(2)],
-            "h_shard": torch.empty((R, self.hs), **bf),
+            "pack": torch.zeros(self.pack, **u8),
+            "pack_seg": [torch.zeros((P, self.pack), **u8) for _ in range(2)],
             "xq": torch.empty((R, self.hq * D), **bf),
             "attn": torch.empty((R, self.hq * D), **bf),
             "attn_seg": torch.empty((P, R, self.hq * D), **bf),
@@ -132,8 +137,6 @@ class TPTarget:
             "logits_seg": torch.empty((P, R, V // P), **bf),
             "logits_full": torch.empty((R, V), **bf),
             "ssq0": torch.zeros(1024 * 32, dtype=torch.float32, device=dev),
-            "ssq": torch.zeros((self.tiles, 32), dtype=torch.float32, device=dev),
-            "ssq_seg": torch.zeros((P, self.tiles, 32), dtype=torch.float32, device=dev),
             "inv_freq": torch.empty(D // 2, dtype=torch.float32, device=dev),
             "row_pos": torch.zeros(R, dtype=torch.int32, device=dev),
             "row_kv": torch.zeros(R, dtype=torch.int64, device=dev),
@@ -161,16 +164,23 @@ class TPTarget:
         dist.all_gather_into_tensor(out, inp, group=self.group)
 
     def _qmm(self, s, w: quant.QWeight, x, ldx, M, K, epi, out=None, ldo=0, *, x_seg=0,
-             x_seg_stride=0, norm_w=None, ssq_in=None, ssq_n=0, resid=None, ldr=0, ssq_out=None,
-             n_act=0, layer=None, lens_pos=None):
+             x_seg_stride=0, norm_w=None, ssq_in=None, ssq_n=0, ssq_seg=0, ssq_seg_stride=0,
+             resid=None, ldr=0, ssq_out=None, n_act=0, layer=None):
         a = _lib.QmmArgs()
-        a.x, a.ldx, a.x_seg, a.x_seg_stride = ptr(x), ldx, x_seg, x_seg_stride
+        a.x = x if isinstance(x, int) else ptr(x)
+        a.ldx, a.x_seg, a.x_seg_stride = ldx, x_seg, x_seg_stride
         a.M, a.K, a.N, a.bits = M, K, int(w.wq.shape[0]), w.bits
         a.wq, a.scales, a.biases = ptr(w.wq), ptr(w.scales), ptr(w.biases)
-        a.out, a.ldo, a.epilogue = ptr(out), ldo, epi
-        a.norm_w, a.ssq_in, a.ssq_n, a.ssq_stride = ptr(norm_w), ptr(ssq_in), ssq_n, 32
+        a.out = out if isinstance(out, int) else ptr(out)
+        a.ldo, a.epilogue = ldo, epi
+        a.norm_w, a.ssq_n, a.ssq_stride = ptr(norm_w), ssq_n, 32
+        a.ssq_in = ssq_in if isinstance(ssq_in, int) or ssq_in is None else ptr(ssq_in)
+        a.ssq_seg, a.ssq_seg_stride = ssq_seg, ssq_seg_stride
+
         a.eps = self.cfg.rms_eps
-        a.resid, a.ldr, a.ssq_out, a.n_act = ptr(resid), ldr, ptr(ssq_out), n_act
+        a.resid = resid if isinstance(resid, int) else ptr(resid)
+        a.ldr, a.n_act = ldr, n_act
+        a.ssq_out = ssq_out if isinstance(ssq_out, int) else ptr(ssq_out)
         if epi == _lib.EPI_QKROPE:
             b, D = self.b, self.cfg.head_dim
             a.hq, a.hk = self.hq, self.hk
@@ -200,47 +210,53 @@ class TPTarget:
                                          ptr(self.embed.biases), cfg.vocab, H, cfg.bits,
                                          ptr(b["h0"]), ptr(b["ssq0"]), s))
         Lm = self.kv_cap if L_max is None else int(L_max)
-        # current hidden state: contiguous (embedding) or segmented [P, R, hs] (after a gather)
-        x, ldx, xseg, xss = b["h0"], H, 0, 0
-        ssq, ssq_n = b["ssq0"], 1
-        resid, ldr = b["h0"][:, r * hs:], H
+        # current hidden state: contiguous (embedding) or the gathered packs [P, pack] (after a
+        # gather: rank q's hidden shard at q*pack, its statistics at q*pack + hbytes)
+        pk, hb = self.pack, self.hbytes
+        loc = b["pack"].data_ptr()
+        x, ldx, xseg, xss = b["h0"].data_ptr(), H, 0, 0
+        ssq, ssq_n, sseg, ssegs = b["ssq0"].data_ptr(), 1, 0, 0
+        resid, ldr = b["h0"][:, r * hs:].data_ptr(), H
         cur = 0
         q_st = _lib.i64_array([0, D, self.hq * D])
         k_st = _lib.i64_array([0, self.kv_cap * D, D])
         for L in self.layers:
             self._qmm(s, L["qkv"], x, ldx, R, H, _lib.EPI_QKROPE, x_seg=xseg, x_seg_stride=xss,
-                      norm_w=L["in_norm"], ssq_in=ssq, ssq_n=ssq_n, layer=L)
+                      norm_w=L["in_norm"], ssq_in=ssq, ssq_n=ssq_n, ssq_seg=sseg,
+                      ssq_seg_stride=ssegs, layer=L)
             _lib.check(_lib.lib.dspark_verify_attn(
                 ptr(b["xq"]), q_st, ptr(L["k_cache"]), k_st, ptr(L["v_cache"]), k_st, 1, self.hq,
                 self.hk, R, D, Lm, ptr(b["kv_len"]), float(D ** -0.5), 1, None, ptr(b["attn"]),
                 q_st, ptr(b["attn_ws"]), b["attn_ws"].numel(), s))
             self._gather(b["attn_seg"], b["attn"])
-            # O: x = all heads' attention ([P, R, hq*D] segments), residual = own hidden shard
-            self._qmm(s, L["o"], b["attn_seg"], self.hq * D, R, Hq * D, _lib.EPI_RESID,
-                      b["h_shard"], hs, x_seg=self.hq * D, x_seg_stride=self.max_rows * self.hq * D,
-                      resid=resid, ldr=ldr, ssq_out=b["ssq"])
-            mid = b["h_seg"][cur]
-            self._gather(mid, b["h_shard"])
-            self._gather(b["ssq_seg"], b["ssq"])
+            # O: x = all heads' attention ([P, R, hq*D] segments), residual = own hidden shard;
+            # the new shard and its statistics land in this rank's pack
+            self._qmm(s, L["o"], b["attn_seg"], self.hq * D, R, Hq * D, _lib.EPI_RESID, loc, hs,
+                      x_seg=self.hq * D, x_seg_stride=self.max_rows * self.hq * D,
+                      resid=resid, ldr=ldr, ssq_out=loc + hb)
+            mid = b["pack_seg"][cur]
+            self._gather(mid, b["pack"])
+            mb = mid.data_ptr()
             # gate/up: post-attention norm over the gathered hidden state, SwiGLU shard
-            self._qmm(s, L["gate_up"], mid, hs, R, H, _lib.EPI_SWIGLU, b["act"], I // P,
-                      x_seg=hs, x_seg_stride=self.max_rows * hs, norm_w=L["post_norm"],
-                      ssq_in=b["ssq_seg"], ssq_n=P * T, n_act=I // P)
+            self._qmm(s, L["gate_up"], mb, hs, R, H, _lib.EPI_SWIGLU, b["act"], I // P,
+                      x_seg=hs, x_seg_stride=pk // 2, norm_w=L["post_norm"], ssq_in=mb + hb,
+                      ssq_n=P * T, ssq_seg=T, ssq_seg_stride=pk // 4, n_act=I // P)
             self._gather(b["act_seg"], b["act"])
             # down: x = all activations, residual = own shard of the mid state
-            self._qmm(s, L["down"], b["act_seg"], I // P, R, I, _lib.EPI_RESID, b["h_shard"], hs,
-                      x_seg=I // P, x_seg_stride=self.max_rows * (I // P), resid=mid[r], ldr=hs,
-                      ssq_out=b["ssq"])
+            self._qmm(s, L["down"], b["act_seg"], I // P, R, I, _lib.EPI_RESID, loc, hs,
+                      x_seg=I // P, x_seg_stride=self.max_rows * (I // P), resid=mb + r * pk,
+                      ldr=hs, ssq_out=loc + hb)
             cur ^= 1
-            nxt = b["h_seg"][cur]
-            self._gather(nxt, b["h_shard"])
-            self._gather(b["ssq_seg"], b["ssq"])
-            x, ldx, xseg, xss = nxt, hs, hs, self.max_rows * hs
-            ssq, ssq_n = b["ssq_seg"], P * T
-            resid, ldr = nxt[r], hs
+            nxt = b["pack_seg"][cur]
+            self._gather(nxt, b["pack"])
+            nb = nxt.data_ptr()
+            x, ldx, xseg, xss = nb, hs, hs, pk // 2
+            ssq, ssq_n, sseg, ssegs = nb + hb, P * T, T, pk // 4
+            resid, ldr = nb + r * pk, hs
         # final norm + vocab-sharded lm_head, logits gathered
         self._qmm(s, self.lm_head, x, ldx, R, H, _lib.EPI_PLAIN, b["logits"], V // P, x_seg=xseg,
-                  x_seg_stride=xss, norm_w=self.final_norm, ssq_in=ssq, ssq_n=ssq_n)
+                  x_seg_stride=xss, norm_w=self.final_norm, ssq_in=ssq, ssq_n=ssq_n,
+                  ssq_seg=sseg, ssq_seg_stride=ssegs)
         self._gather(b["logits_seg"], b["logits"])
         b["logits_full"][:R].view(R, P, V // P).copy_(b["logits_seg"][:, :R].transpose(0, 1))
         return b["logits_full"][:R]
