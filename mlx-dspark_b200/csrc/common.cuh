@@ -219,6 +219,34 @@ __device__ __forceinline__ void st_dsmem_f4(uint32_t addr, float4 v) {
                : "memory");
 }
 
+// Asynchronous stores into the shared memory of a CTA of this cluster (`addr` and `mbar` are
+// shared::cluster addresses in that CTA): when the bytes land they count toward the transaction
+// count of that CTA's mbarrier, so its waiter needs no fence or arrive from the sender.
+__device__ __forceinline__ void st_async_f32(uint32_t addr, float v, uint32_t mbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(
+                   addr),
+               "f"(v), "r"(mbar)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_async_v2(uint32_t addr, float a, float b, uint32_t mbar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+          addr),
+      "f"(a), "f"(b), "r"(mbar)
+      : "memory");
+}
+
+// 16-byte global load through L2 only (data another kernel wrote)
+__device__ __forceinline__ uint4 ldcg_v4(const void* p) {
+  return __ldcg(reinterpret_cast<const uint4*>(p));
+}
+
+// 16-byte global load through the read-only path (data no kernel writes while this one runs)
+__device__ __forceinline__ uint4 ldg_v4(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
 __device__ __forceinline__ void fence_acq_rel_cluster() {
   asm volatile("fence.acq_rel.cluster;" ::: "memory");
 }

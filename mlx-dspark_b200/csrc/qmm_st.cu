@@ -14,20 +14,26 @@
 //    L2 evict-first); every 8 groups the scales and biases ride on the same mbarrier. The
 //    producer never waits on the previous kernel (griddepcontrol.wait), so under programmatic
 //    dependent launch a kernel's first weight stages stream while its predecessor finishes.
-//  * Eight consumer warps, 16 weight rows each. Per group of 64 k a thread loads its rows' words
+//  * Eight consumer warps, each owning 32 tile rows (two 16-row MMA groups sharing one set of x
+//    fragments) and one k half of every stage. Per group of 64 k a thread loads its rows' words
 //    (one 8- or 16-byte ld.shared each, conflict-free through a row permutation matched to the
 //    swizzle), dequantizes them with the bf16 magic-exponent trick (nibble | 0x4300 = 128 + q,
 //    exact; 8-bit as two exact nibble planes 128 + lo and 256 + 16 hi) straight into mma.m16n8k16
 //    A fragments (the weights are the 16-row A operand, x the 8-column B operand, so every
 //    weight is read once whatever M is), and folds the group's exact product P into fp32
 //    accumulators: acc += scale*P + (bias - MAGIC*scale) * sum_k x (packed f32x2 FMAs).
-//  * x (the CTA's K slice, <= 32 rows) is staged once per launch, k permuted inside each 8-block
-//    (4-bit) or 4-block (8-bit) exactly as the magic extraction orders the weights, so one
-//    16-byte load gives the B fragments of two k16 steps.
-//  * Four epilogue warps finish each tile while the consumers stream the next one: split-K
-//    partial tiles are exchanged through distributed shared memory (double-buffered, rows
-//    m = rank + i*cs reduced in fixed rank order: deterministic, and a row's result never
-//    depends on how many rows ride with it), then the shared epilogue runs on them.
+//  * x (the CTA's K slice, <= 32 rows) is staged once per launch by the consumer threads
+//    themselves (16-byte global loads, 8 in flight per thread, normed, k permuted inside each
+//    8-block (4-bit) or 4-block (8-bit) exactly as the magic extraction orders the weights, and
+//    summed per group in the same pass), so one 16-byte load gives the B fragments of two k16
+//    steps and the copy engine stays free for the weight stream.
+//  * Four epilogue warps finish each tile while the consumers stream the next one. At a tile's
+//    end every consumer warp pushes its k half of the partial tile to the rows' owners (row m
+//    belongs to cluster rank m % cs) and goes straight on: st.async into a peer's receive
+//    buffer (the peer's mbarrier counts the bytes; no fence, no handshake), plain stores and a
+//    per-warp arrive for its own rows. The owner sums the halves of each rank, then the ranks,
+//    in fixed order (double-buffered; deterministic, and a row's result never depends on how
+//    many rows ride with it), then the shared epilogue runs on them.
 // Every mbarrier wait is time-bounded (a failed wait records an error in the device status word
 // and the kernel drains without further waits on other agents).
 #include <algorithm>
@@ -86,13 +92,13 @@ __host__ __device__ inline int scale_slots(int bits, int nslots) {
 }
 
 struct Layout {
-  int ring, sring, xs, nw, sx, part, red, xch, rs, bars, total;
+  int ring, sring, xs, nw, sx, part, red, rs, bars, total;
 };
 
 __host__ __device__ inline int x_pitch(int kslice) { return kslice * 2 + 16; }
 
 // Rows of the split-K receive buffer: CTA c of the cluster owns rows m = c + i*cs; every CTA
-// pushes its partial rows into slot [rank][i] of the owner.
+// pushes its partial rows (one per k half of the tile) into slot [rank][half][i] of the owner.
 __host__ __device__ inline int owned_rows(int rp, int cs) { return (rp + cs - 1) / cs; }
 
 // x rows the tcgen05 MMA reads as its N dimension (zero padded): 16 or 32
@@ -109,22 +115,20 @@ __host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslot
   L.xs = off;  // row-major rows of XP bytes (mma.sync), or 8-k blocks of tc_rows rows (tcgen05)
   off += tc ? (kslice / 8) * tc_rows(mt) * 16 : rp * x_pitch(kslice);
   off = (off + 15) & ~15;
-  L.nw = off;  // the K slice of the RMSNorm weight (fused-norm prologue)
-  off += kslice * 2;
+  L.nw = off;  // the K slice of the RMSNorm weight (tcgen05 prologue)
+  if (tc) off += kslice * 2;
   L.sx = off;
   off += (kslice / 64) * rp * 4;
   off = (off + 15) & ~15;
-  L.part = off;  // two receive buffers [cs][owned_rows][PSTR]
-  off += 2 * cs * owned_rows(rp, cs) * PSTR * 4;
+  L.part = off;  // two receive buffers [cs sources][2 k halves][owned_rows][PSTR]
+  off += 2 * cs * 2 * owned_rows(rp, cs) * PSTR * 4;
   L.red = off;
   off += rp * PSTR * 4;
-  L.xch = off;  // k-half exchange: 2 row groups x mt x 4 accumulators x 128 threads
-  off += 2 * mt * 4 * 128 * 4;
   L.rs = off;
   off += 32 * 4;
   off = (off + 15) & ~15;
   L.bars = off;
-  off += (2 * nslots + 5 + kTcBars) * 8 + 16;  // + tcgen05 completion barriers, TMEM slot
+  off += (2 * nslots + 4 + kTcBars) * 8 + 16;  // + tcgen05 completion barriers, TMEM slot
   L.total = off + 1024;  // slack to align the dynamic base to 1024 bytes
   return L;
 }
@@ -145,11 +149,11 @@ __device__ __forceinline__ int row_perm(int g) {
 // (M = 128 rows, N = the staged x rows, K = 16 per instruction; x is read by the tensor core from
 // shared memory) into a D buffer and commits them to an mbarrier. With two A/D buffer pairs the
 // thread folds group q-2's product (acc += scale*P + (bias - MAGIC*scale)*sum_k x, in fp32, in
-// issue order) while the tensor core works on group q-1. The k halves of the two warpgroups are
-// summed at the tile end (warpgroup 0 + warpgroup 1) and pushed like the mma.sync partials.
+// issue order) while the tensor core works on group q-1. Each warpgroup pushes its k half of the
+// tile like the mma.sync partials; the owner sums them (warpgroup 0 + warpgroup 1).
 template <int BITS, int MT>
 __device__ __forceinline__ void consume_tc(const QmmParams& p, uint8_t* ring, uint8_t* sring,
-                                           uint8_t* xs, const float* sx, float* part, float* xch,
+                                           uint8_t* xs, const float* sx, float* part,
                                            uint64_t* full, uint64_t* empty, uint64_t* ready,
                                            uint64_t* freeb, uint64_t* tcbar, uint32_t tmem,
                                            int ntl, int nsb, int nst, int S, int SS, int cs,
@@ -316,39 +320,27 @@ __device__ __forceinline__ void consume_tc(const QmmParams& p, uint8_t* ring, ui
     for (int i = 0; i < NB; ++i)
       if (q - NB + i >= q0) fold(q - NB + i, i);
 
-    // ---- the warpgroups' k halves meet (fixed order: warpgroup 0 + warpgroup 1)
-    if (wg == 1) {
-#pragma unroll
-      for (int m = 0; m < RP; ++m) xch[m * 128 + row] = acc[m];
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(NC));
+    // ---- push this warpgroup's k half of partial tile j into receive buffer j & 1 of each
+    // row's owner (m % cs), slot [rank][wg][m / cs]
     const int pbuf = j & 1;
     const int ro = owned_rows(RP, cs);
     if (j == 0 && cs > 1) cluster_wait();  // peers' buffers and barriers exist
     // the owners' buffer pbuf last held tile j-2: every owner must be done reading it
     if (j >= 2 && ok)
       ok = mbar_wait_cluster(&freeb[pbuf], ((j - 2) >> 1) & 1, p.status, kErrWaitCluster);
-    if (wg == 0) {
-      const uint32_t pa = smem_u32(part + (pbuf * cs + rank) * ro * PSTR);
+    const uint32_t pa = smem_u32(part + ((pbuf * cs + rank) * 2 + wg) * ro * PSTR);
+    const uint32_t rb = smem_u32(&ready[pbuf]);
 #pragma unroll
-      for (int m = 0; m < RP; ++m) {
-        const float v = acc[m] + xch[m * 128 + row];
-        const int owner = m % cs, ml = m / cs;
-        if (cs > 1)
-          st_dsmem_f32(mapa_shared(pa + uint32_t((ml * PSTR + row) * 4), owner), v);
-        else
-          part[(pbuf * ro + ml) * PSTR + row] = v;
-      }
+    for (int m = 0; m < RP; ++m) {
+      const int owner = m % cs, ml = m / cs;
+      const uint32_t a = pa + uint32_t((ml * PSTR + row) * 4);
+      if (owner == rank)
+        asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(acc[m]) : "memory");
+      else
+        st_async_f32(mapa_shared(a, owner), acc[m], mapa_shared(rb, owner));
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(NC));  // pushes issued; the exchange buffer is free
-    if (warp == 0 && lane < cs) {
-      if (cs > 1) {
-        fence_acq_rel_cluster();
-        mbar_arrive_cluster(&ready[pbuf], lane);
-      } else {
-        mbar_arrive(&ready[pbuf]);
-      }
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ready[pbuf]);  // this warp's local rows are in place
     (void)nclus;
     (void)tid;
   }
@@ -378,13 +370,11 @@ __global__ void __launch_bounds__(NTHR, 1)
   float* part = reinterpret_cast<float*>(smem + Lo.part);
   float* red = reinterpret_cast<float*>(smem + Lo.red);
   float* rsm = reinterpret_cast<float*>(smem + Lo.rs);
-  float* xch = reinterpret_cast<float*>(smem + Lo.xch);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lo.bars);
   uint64_t* empty = full + S;
-  uint64_t* ready = empty + S;   // [2] every cluster CTA published its partial tile
+  uint64_t* ready = empty + S;   // [2] every local warp and every peer's bytes of a partial tile
   uint64_t* freeb = ready + 2;   // [2] every cluster CTA finished reading this CTA's partial
-  uint64_t* xbar = freeb + 2;    // the x slice (and norm weights) landed
-  uint64_t* tcbar = xbar + 1;    // [2 warpgroups][kTcBuf buffers] tcgen05 MMA completion
+  uint64_t* tcbar = freeb + 2;   // [2 warpgroups][kTcBuf buffers] tcgen05 MMA completion
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tcbar + kTcBars);
   uint8_t* nws = smem + Lo.nw;
 
@@ -401,16 +391,21 @@ __global__ void __launch_bounds__(NTHR, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
 
+  if (warp == WARP_TMA && lane == 0) {  // descriptor fetches overlap the set-up
+    prefetch_tmap(&wmap);
+    prefetch_tmap(&smap);
+    prefetch_tmap(&bmap);
+  }
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NWC);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&ready[i], cs);
+      // the owner's expect-tx arrive (peers' st.async bytes) + one arrive per local consumer warp
+      mbar_init(&ready[i], 1 + NWC);
       mbar_init(&freeb[i], cs);
     }
-    mbar_init(xbar, 1);
     for (int i = 0; i < kTcBars; ++i) mbar_init(&tcbar[i], 1);
     fence_mbar_init();
   }
@@ -429,17 +424,14 @@ __global__ void __launch_bounds__(NTHR, 1)
   if (warp == WARP_TMA) {
     // ------------------------------------------------------------- producer warp
     if (lane == 0) {
-      prefetch_tmap(&wmap);
-      prefetch_tmap(&smap);
-      prefetch_tmap(&bmap);
       const uint64_t pol = l2_policy_evict_first();
       int issued = 0;
+      int slot = 0, phase = 0, ss = 0;  // ring slot / fill count parity, scale slot
       for (int j = 0; j < ntl && ok; ++j) {
         const int n0 = (int(blockIdx.y) + j * nclus) * TN;
         for (int st = 0; st < nst; ++st) {
-          const int g = j * nst + st;
-          const int slot = g % S;
-          if (g >= S && !mbar_wait(&empty[slot], ((g / S) - 1) & 1, p.status, kErrWaitEmpty)) {
+          // slot reuse: wait until the consumers released its previous fill
+          if (issued >= S && !mbar_wait(&empty[slot], uint32_t(phase ^ 1), p.status, kErrWaitEmpty)) {
             ok = false;
             break;
           }
@@ -448,11 +440,15 @@ __global__ void __launch_bounds__(NTHR, 1)
           const int kk = kbase + st * KB;
           tma_load_2d(ring + slot * STG, &wmap, &full[slot], kk * BITS / 32, n0, pol);
           if (sblk) {
-            const int ss = (j * nsb + st / SPS) % SS;
             tma_load_2d(sring + ss * 2 * SCB, &smap, &full[slot], kk / 64, n0, pol);
             tma_load_2d(sring + ss * 2 * SCB + SCB, &bmap, &full[slot], kk / 64, n0, pol);
+            if (++ss == SS) ss = 0;
           }
           ++issued;
+          if (++slot == S) {
+            slot = 0;
+            phase ^= 1;
+          }
         }
       }
       // never leave the CTA with copies in flight: wait (bounded) for the last ones issued
@@ -471,42 +467,6 @@ __global__ void __launch_bounds__(NTHR, 1)
     // x chunk (row m, 8-k block c): row-major for the mma.sync consumers, 8-k blocks of NMX rows
     // (the UMMA K-major canonical layout) for the tcgen05 consumers
     auto xoff = [&](int m, int c) { return TC ? (c * NMX + m) * 16 : m * XP + c * 16; };
-    if constexpr (!TC) {
-      // the K slice of x lands by bulk copies, one per row (and one for the norm weights), all
-      // in flight at once; rows past M are zeroed meanwhile
-      if (tid == 0) {
-        const uint32_t bytes = uint32_t(kvalid) * 2;
-        mbar_arrive_expect_tx(xbar, bytes * uint32_t(p.M + (nrm ? 1 : 0)));
-        for (int m = 0; m < p.M; ++m) {
-          if (p.x_seg == 0) {
-            bulk_load(xs + m * XP, p.x + (size_t)m * p.ldx + kbase, bytes, xbar);
-          } else {  // one copy per segment the slice touches
-            for (int k = kbase; k < kbase + kvalid;) {
-              const long seg = k / p.x_seg, off = k - seg * p.x_seg;
-              const int len = int(min(long(kbase + kvalid - k), p.x_seg - off));
-              bulk_load(xs + m * XP + (k - kbase) * 2,
-                        p.x + seg * p.x_segstride + (size_t)m * p.ldx + off, uint32_t(len) * 2, xbar);
-              k += len;
-            }
-          }
-        }
-        if (nrm) bulk_load(nws, p.norm_w + kbase, bytes, xbar);
-      }
-    } else {
-      // 16-byte copies straight into the canonical places, all in flight at once
-      const uint32_t xa0 = smem_u32(xs);
-      for (int idx = tid; idx < p.M * vchunks; idx += NC) {
-        const int m = idx / vchunks, c = idx - m * vchunks;
-        const long k = kbase + c * 8;
-        const long seg = p.x_seg ? k / p.x_seg : 0;
-        const bf16* src = p.x + seg * p.x_segstride + (size_t)m * p.ldx + (k - seg * p.x_seg);
-        cp_async_16_zfill(xa0 + uint32_t(xoff(m, c)), src, true);
-      }
-      if (nrm)
-        for (int c = tid; c < vchunks; c += NC)
-          cp_async_16_zfill(smem_u32(nws) + uint32_t(c * 16), p.norm_w + kbase + c * 8, true);
-      asm volatile("cp.async.commit_group;" ::: "memory");
-    }
     for (int idx = tid; idx < (NMX - p.M) * chunks; idx += NC) {
       const int m = p.M + idx / chunks, c = idx % chunks;
       *reinterpret_cast<uint4*>(xs + xoff(m, c)) = make_uint4(0u, 0u, 0u, 0u);
@@ -518,69 +478,146 @@ __global__ void __launch_bounds__(NTHR, 1)
     if (nrm) {
       for (int m = warp; m < RP; m += NWC) {
         float ss = 0.f;
-        if (m < p.M)
-          for (int e = lane; e < p.ssq_n; e += 32) {
-            const long at = p.ssq_seg ? (e / p.ssq_seg) * p.ssq_segstride + long(e % p.ssq_seg) * p.ssq_stride
-                                      : long(e) * p.ssq_stride;
-            ss += __ldcg(&p.ssq_in[at + m]);
+        if (m < p.M) {
+          // entry e = lane + 32i lives in segment e / ssq_seg: advanced by subtraction, so no
+          // division sits between the loads
+          const int sg = p.ssq_seg;
+          int sseg = 0, soff = lane;
+          if (sg) {
+            sseg = lane / sg;
+            soff = lane - sseg * sg;
           }
+          for (int e = lane; e < p.ssq_n; e += 32) {
+            const long at = sg ? sseg * p.ssq_segstride + long(soff) * p.ssq_stride
+                               : long(e) * p.ssq_stride;
+            ss += __ldcg(&p.ssq_in[at + m]);
+            soff += 32;
+            if (sg)
+              while (soff >= sg) {
+                soff -= sg;
+                ++sseg;
+              }
+          }
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         if (lane == 0) rsm[m] = m < p.M ? rsqrtf(ss / float(p.K) + p.eps) : 0.f;
       }
     }
-    if constexpr (TC) asm volatile("cp.async.wait_all;" ::: "memory");
-    asm volatile("bar.sync 1, %0;" ::"n"(NC));
-    if constexpr (!TC) {
-      if (ok) ok = mbar_wait(xbar, 0, p.status, kErrWaitFull);
-    }
-    // in place: apply the norm (x * rs * w rounded to bf16), permute k inside each 8-block
-    // (4-bit: 0,4,1,5,2,6,3,7) or 4-block (8-bit: 0,2,1,3) as the magic extraction orders the
-    // weights, and sum each group of 64: the 8 chunks of a group sit on 8 consecutive lanes
-    // (chunk counts are multiples of 8) and reduce by shuffles in a fixed order
-    for (int base = 0; base < p.M * vchunks; base += NC) {
-      const int idx = base + tid;
-      const bool live = idx < p.M * vchunks;
-      const int m = live ? idx / vchunks : 0, c = live ? idx - m * vchunks : 0;
-      float part = 0.f;
-      if (live) {
-        uint4 vv = *reinterpret_cast<const uint4*>(xs + xoff(m, c));
-        if (nrm) {
-          const float r = rsm[m];
-          const uint4 w = *reinterpret_cast<const uint4*>(nws + c * 16);
-          uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
-          const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w);
+    // one 8-k chunk (row m, chunk c): apply the norm (x * rs * w rounded to bf16), permute k
+    // inside each 8-block (4-bit: 0,4,1,5,2,6,3,7) or 4-block (8-bit: 0,2,1,3) as the magic
+    // extraction orders the weights, store it, and return its sum
+    auto stage_chunk = [&](uint4 vv, uint4 w, int m, int c) -> float {
+      if (nrm) {
+        const float r = rsm[m];
+        uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
+        const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w);
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
-                                bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
-        }
-        part = (bf16_lo(vv.x) + bf16_hi(vv.x)) + (bf16_lo(vv.y) + bf16_hi(vv.y)) +
-               (bf16_lo(vv.z) + bf16_hi(vv.z)) + (bf16_lo(vv.w) + bf16_hi(vv.w));
-        uint4 o;
-        if (BITS == 4) {
-          o.x = __byte_perm(vv.x, vv.z, 0x5410);
-          o.y = __byte_perm(vv.x, vv.z, 0x7632);
-          o.z = __byte_perm(vv.y, vv.w, 0x5410);
-          o.w = __byte_perm(vv.y, vv.w, 0x7632);
-        } else {
-          o.x = __byte_perm(vv.x, vv.y, 0x5410);
-          o.y = __byte_perm(vv.x, vv.y, 0x7632);
-          o.z = __byte_perm(vv.z, vv.w, 0x5410);
-          o.w = __byte_perm(vv.z, vv.w, 0x7632);
-        }
-        *reinterpret_cast<uint4*>(xs + xoff(m, c)) = o;
+        for (int e = 0; e < 4; ++e)
+          pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
+                              bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
       }
+      const float sum = (bf16_lo(vv.x) + bf16_hi(vv.x)) + (bf16_lo(vv.y) + bf16_hi(vv.y)) +
+                        (bf16_lo(vv.z) + bf16_hi(vv.z)) + (bf16_lo(vv.w) + bf16_hi(vv.w));
+      uint4 o;
+      if (BITS == 4) {
+        o.x = __byte_perm(vv.x, vv.z, 0x5410);
+        o.y = __byte_perm(vv.x, vv.z, 0x7632);
+        o.z = __byte_perm(vv.y, vv.w, 0x5410);
+        o.w = __byte_perm(vv.y, vv.w, 0x7632);
+      } else {
+        o.x = __byte_perm(vv.x, vv.y, 0x5410);
+        o.y = __byte_perm(vv.x, vv.y, 0x7632);
+        o.z = __byte_perm(vv.z, vv.w, 0x5410);
+        o.w = __byte_perm(vv.z, vv.w, 0x7632);
+      }
+      *reinterpret_cast<uint4*>(xs + xoff(m, c)) = o;
+      return sum;
+    };
+    // the 8 chunks of a group of 64 sit on 8 consecutive lanes (chunk counts are multiples of
+    // 64) and their sums reduce by shuffles in a fixed order
+    auto group_sum = [&](float part, bool live, int m, int c) {
       part += __shfl_xor_sync(0xffffffffu, part, 1);
       part += __shfl_xor_sync(0xffffffffu, part, 2);
       part += __shfl_xor_sync(0xffffffffu, part, 4);
       if (live && (c & 7) == 0) sx[(c >> 3) * RP + m] = part;
+    };
+    if constexpr (!TC) {
+      // x straight from global memory, staged in one pass: no copy engine in the way of the
+      // weight stream, no second pass over shared memory. Thread t takes chunk column
+      // c = cb + t of U rows at a time, all U 16-byte loads in flight together. No division sits
+      // between the loads (a division's reciprocal shares the memory instruction queue and
+      // would wait behind them): the segment of k advances by subtraction, the rows by a loop.
+      if (nrm) asm volatile("bar.sync 1, %0;" ::"n"(NC));  // rs of every row
+      constexpr int U = MT == 4 ? 4 : 8;  // rows in flight per thread (register budget)
+      const int xseg = int(p.x_seg);
+      int seg = 0, off = kbase + tid * 8;  // segment and offset of k = kbase + 8c
+      if (xseg) {
+        seg = off / xseg;
+        off -= seg * xseg;
+      }
+      for (int cb = 0; cb < vchunks; cb += NC) {
+        const int c = cb + tid;
+        const bool cv = c < vchunks;
+        const bf16* col = p.x + long(seg) * p.x_segstride + off;
+        const uint4 w = (nrm && cv) ? ldg_v4(p.norm_w + kbase + c * 8) : make_uint4(0u, 0u, 0u, 0u);
+        for (int m0 = 0; m0 < p.M; m0 += U) {
+          uint4 v[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            v[u] = (cv && m0 + u < p.M) ? ldcg_v4(col + (size_t)(m0 + u) * p.ldx)
+                                        : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int m = m0 + u;
+            const bool live = cv && m < p.M;
+            const float part = live ? stage_chunk(v[u], w, m, c) : 0.f;
+            if (m < p.M) group_sum(part, live, m, c);  // warp-uniform condition
+          }
+        }
+        off += NC * 8;
+        if (xseg)
+          while (off >= xseg) {
+            off -= xseg;
+            ++seg;
+          }
+      }
+    } else {
+      // 16-byte copies straight into the canonical places, all in flight at once, then the
+      // same norm / permute / group-sum pass in place
+      const uint32_t xa0 = smem_u32(xs);
+      for (int idx = tid; idx < p.M * vchunks; idx += NC) {
+        const int m = idx / vchunks, c = idx - m * vchunks;
+        const int k = kbase + c * 8;
+        const int xseg = int(p.x_seg);
+        const int seg = xseg ? k / xseg : 0;
+        const bf16* src = p.x + seg * p.x_segstride + (size_t)m * p.ldx + (k - seg * xseg);
+        cp_async_16_zfill(xa0 + uint32_t(xoff(m, c)), src, true);
+      }
+      if (nrm)
+        for (int c = tid; c < vchunks; c += NC)
+          cp_async_16_zfill(smem_u32(nws) + uint32_t(c * 16), p.norm_w + kbase + c * 8, true);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"n"(NC));
+      for (int base = 0; base < p.M * vchunks; base += NC) {
+        const int idx = base + tid;
+        const bool live = idx < p.M * vchunks;
+        const int m = live ? idx / vchunks : 0, c = live ? idx - m * vchunks : 0;
+        float part = 0.f;
+        if (live)
+          part = stage_chunk(*reinterpret_cast<const uint4*>(xs + xoff(m, c)),
+                             nrm ? *reinterpret_cast<const uint4*>(nws + c * 16)
+                                 : make_uint4(0u, 0u, 0u, 0u),
+                             m, c);
+        group_sum(part, live, m, c);
+      }
     }
     if constexpr (TC) fence_proxy_async_smem();  // x becomes the tensor core's B operand
     asm volatile("bar.sync 1, %0;" ::"n"(NC));
 
     if constexpr (TC) {
-      consume_tc<BITS, MT>(p, ring, sring, xs, sx, part, xch, full, empty, ready, freeb, tcbar,
+      consume_tc<BITS, MT>(p, ring, sring, xs, sx, part, full, empty, ready, freeb, tcbar,
                            *tmem_slot, ntl, nsb, nst, S, SS, cs, rank, ok);
     } else {
 
@@ -602,6 +639,8 @@ __global__ void __launch_bounds__(NTHR, 1)
     // swizzled byte offset of (row, logical 16-byte chunk c) inside a stage
     auto wofs = [](int row, int c) { return uint32_t(row * 128 + ((c ^ (row & 7)) << 4)); };
 
+    // ring slot and phase of the next stage, scale slot of the next block (counted, not divided)
+    int slot = 0, phase = 0, sslot = 0;
     for (int j = 0; j < ntl; ++j) {
       float acc[2][MT][4];
 #pragma unroll
@@ -612,16 +651,16 @@ __global__ void __launch_bounds__(NTHR, 1)
           for (int i = 0; i < 4; ++i) acc[rg][mt][i] = 0.f;
 
       for (int sb = 0; sb < nsb; ++sb) {
+        const uint32_t sblk_a = sring_a + uint32_t(sslot * 2 * SCB);
+        if (++sslot == SS) sslot = 0;
 #pragma unroll
         for (int si = 0; si < SPS; ++si) {
           const int st = sb * SPS + si;
-          const int g = j * nst + st;
-          const int slot = g % S;
-          if (ok) ok = mbar_wait(&full[slot], (g / S) & 1, p.status, kErrWaitFull);
+          if (ok) ok = mbar_wait(&full[slot], uint32_t(phase), p.status, kErrWaitFull);
           // scales / biases of this stage's groups for the thread's 4 rows: one 32-bit word
           // (two consecutive groups) per row
           const int gw = (si * GPS + half * GH) & ~1;  // first group of the word
-          const uint32_t sa = sring_a + uint32_t(((j * nsb + sb) % SS) * 2 * SCB) + uint32_t(gw * 2);
+          const uint32_t sa = sblk_a + uint32_t(gw * 2);
           uint32_t sw[2][2], bw[2][2];
 #pragma unroll
           for (int rg = 0; rg < 2; ++rg)
@@ -721,69 +760,55 @@ __global__ void __launch_bounds__(NTHR, 1)
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[slot]);
+          if (++slot == S) {
+            slot = 0;
+            phase ^= 1;
+          }
         }
       }
 
-      // ---- the k halves meet: warps of half 1 hand their sums to the half-0 warp of the same
-      // rows (fixed order: half 0 + half 1)
-      constexpr int NACC = 2 * MT * 4;
-      if (half == 1) {
-#pragma unroll
-        for (int rg = 0; rg < 2; ++rg)
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              xch[((rg * MT + mt) * 4 + i) * 128 + wr * 32 + lane] = acc[rg][mt][i];
-      }
-      asm volatile("bar.sync 1, %0;" ::"n"(NC));
-      static_assert(NACC <= 32, "exchange buffer");
-
-      // ---- partial tile j: push row m into receive buffer j & 1 of its owner (m % cs), slot
-      // [rank][m / cs] (local stores when cs == 1)
+      // ---- push partial tile j (this warp's k half) into receive buffer j & 1 of each row's
+      // owner (m % cs), slot [rank][half][m / cs]. Two lanes of the same t4 hold adjacent tile
+      // rows 2r and 2r + 1 (g8 and g8 ^ 4 for 4-bit, g8 and g8 ^ 2 for 8-bit: the row
+      // permutation) for the same two columns m, m + 1: one exchange gives each lane a row pair
+      // for one column, stored with one 8-byte store (st.async to a peer, whose mbarrier counts
+      // the bytes; a plain store and a per-warp arrive for this CTA's own rows).
       const int pbuf = j & 1;
       const int ro = owned_rows(RP, cs);
       if (j == 0 && cs > 1) cluster_wait();  // peers' buffers and barriers exist
       // the owners' buffer pbuf last held tile j-2: every owner must be done reading it
       if (j >= 2 && ok)
         ok = mbar_wait_cluster(&freeb[pbuf], ((j - 2) >> 1) & 1, p.status, kErrWaitCluster);
-      if (half == 0) {
-        const uint32_t pa = smem_u32(part + (pbuf * cs + rank) * ro * PSTR);
+      constexpr int PX = BITS == 4 ? 16 : 8;                     // partner lane mask
+      const bool even = BITS == 4 ? (g8 < 4) : ((g8 & 2) == 0);  // this lane holds row 2r
+      const uint32_t pa = smem_u32(part + ((pbuf * cs + rank) * 2 + half) * ro * PSTR);
+      const uint32_t rb = smem_u32(&ready[pbuf]);
 #pragma unroll
-        for (int rg = 0; rg < 2; ++rg) {
+      for (int rg = 0; rg < 2; ++rg) {
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              acc[rg][mt][i] += xch[((rg * MT + mt) * 4 + i) * 128 + wr * 32 + lane];
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              const int m = mt * 8 + 2 * t4 + i;
-              const int owner = m % cs, ml = m / cs;
-              const int r0 = rows[rg][0], r1 = rows[rg][1];
-              const uint32_t a0 = pa + uint32_t((ml * PSTR + r0) * 4);
-              const uint32_t a1 = pa + uint32_t((ml * PSTR + r1) * 4);
-              if (cs > 1) {
-                st_dsmem_f32(mapa_shared(a0, owner), acc[rg][mt][i]);
-                st_dsmem_f32(mapa_shared(a1, owner), acc[rg][mt][2 + i]);
-              } else {
-                part[(pbuf * ro + ml) * PSTR + r0] = acc[rg][mt][i];
-                part[(pbuf * ro + ml) * PSTR + r1] = acc[rg][mt][2 + i];
-              }
-            }
+        for (int mt = 0; mt < MT; ++mt) {
+          const float* a = acc[rg][mt];  // (r0, m0) (r0, m0+1) (r1, m0) (r1, m0+1)
+          const float x0 = __shfl_xor_sync(0xffffffffu, even ? a[1] : a[0], PX);
+          const float x1 = __shfl_xor_sync(0xffffffffu, even ? a[3] : a[2], PX);
+          const int m = mt * 8 + 2 * t4 + (even ? 0 : 1);
+          const int owner = m % cs, ml = m / cs;
+          const int r0 = rows[rg][0] & ~1, r1 = rows[rg][1] & ~1;  // first row of each pair
+          const float v00 = even ? a[0] : x0, v01 = even ? x0 : a[1];
+          const float v10 = even ? a[2] : x1, v11 = even ? x1 : a[3];
+          const uint32_t a0 = pa + uint32_t((ml * PSTR + r0) * 4);
+          const uint32_t a1 = pa + uint32_t((ml * PSTR + r1) * 4);
+          if (owner == rank) {
+            asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a0), "f"(v00), "f"(v01) : "memory");
+            asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a1), "f"(v10), "f"(v11) : "memory");
+          } else {
+            const uint32_t mb = mapa_shared(rb, owner);
+            st_async_v2(mapa_shared(a0, owner), v00, v01, mb);
+            st_async_v2(mapa_shared(a1, owner), v10, v11, mb);
           }
         }
       }
-      asm volatile("bar.sync 1, %0;" ::"n"(NC));  // pushes issued; the exchange buffer is free
-      // publish to every owner of the cluster: lane c of warp 0 releases to CTA c
-      if (warp == 0 && lane < cs) {
-        if (cs > 1) {
-          fence_acq_rel_cluster();
-          mbar_arrive_cluster(&ready[pbuf], lane);
-        } else {
-          mbar_arrive(&ready[pbuf]);
-        }
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ready[pbuf]);  // this warp's local rows are in place
     }
     if (ntl == 0 && cs > 1) cluster_wait();
     }  // mma.sync consumers
@@ -794,19 +819,31 @@ __global__ void __launch_bounds__(NTHR, 1)
     if (cs > 1) cluster_wait();  // peers' barriers exist before the first remote arrive
     const int ro = owned_rows(RP, cs);
     const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
+    // bytes each peer pushes into this CTA per tile: its 2 k halves of the RP / cs rows
+    // m = rank + i*cs this CTA owns (all RP rows are pushed, padding included)
+    const int nown = RP > rank ? (RP - rank + cs - 1) / cs : 0;
+    const uint32_t peer_bytes = uint32_t((cs - 1) * nown * 2 * TN * 4);
     for (int j = 0; j < ntl; ++j) {
       const int pbuf = j & 1;
       const int t = int(blockIdx.y) + j * nclus;
-      const float* pb = part + pbuf * cs * ro * PSTR;
+      const float* pb = part + pbuf * cs * 2 * ro * PSTR;
+      if (etid == 0) mbar_arrive_expect_tx(&ready[pbuf], peer_bytes);
       if (ok) ok = mbar_wait_cluster(&ready[pbuf], (j >> 1) & 1, p.status, kErrWaitCluster);
-      // sum the cs partials of each owned row in rank order (local shared memory)
+      // sum the partials of each owned row: the two k halves of each rank, then the ranks in
+      // order (local shared memory)
       for (int idx = etid; idx < nmine * (TN / 4); idx += NE) {
         const int mi = idx / (TN / 4), n4 = idx - mi * (TN / 4);
         const int m = rank + mi * cs;
-        float4 s = *reinterpret_cast<const float4*>(&pb[mi * PSTR + n4 * 4]);
-        for (int c = 1; c < cs; ++c) {
-          const float4 v = *reinterpret_cast<const float4*>(&pb[(c * ro + mi) * PSTR + n4 * 4]);
-          s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+        float4 s;
+        for (int c = 0; c < cs; ++c) {
+          const float4 h0 = *reinterpret_cast<const float4*>(&pb[((c * 2) * ro + mi) * PSTR + n4 * 4]);
+          const float4 h1 = *reinterpret_cast<const float4*>(&pb[((c * 2 + 1) * ro + mi) * PSTR + n4 * 4]);
+          const float4 v = make_float4(h0.x + h1.x, h0.y + h1.y, h0.z + h1.z, h0.w + h1.w);
+          if (c == 0) {
+            s = v;
+          } else {
+            s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+          }
         }
         *reinterpret_cast<float4*>(&red[m * PSTR + n4 * 4]) = s;
       }
