@@ -59,10 +59,10 @@ __host__ __device__ constexpr int attn_core_bytes() {
 
 // Receive area of the cluster merge: split s of a cluster pushes row r (owned by CTA r % ns)
 // into slot [s][r / ns] of the owner, D accumulators then m and l (rows of D + 4 floats).
-// Sized for any ns <= 8: ns * ceil(RPG / ns) <= RPG + 7 rows.
+// Sized for any ns <= 16: ns * ceil(RPG / ns) <= RPG + 15 rows.
 template <int D, int NRT>
 __host__ __device__ constexpr int attn_recv_bytes() {
-  return (NRT * 16 + 8) * (D + 4) * 4;
+  return (NRT * 16 + 16) * (D + 4) * 4;
 }
 
 template <int D, int NRT, int KS>
@@ -240,19 +240,36 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
             mma_bf16_16816(s[2 * jp + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
           }
         }
-        // mask + online softmax (exp2 domain)
+        // mask + online softmax (exp2 domain). Steps whose every key is visible to every row of
+        // the warp (all but the split's last and the causal / tree boundary) skip the mask.
         float mx0 = -INFINITY, mx1 = -INFINITY;
+        const int klast = kt + kl + KB - 1;
+        const bool interior = __all_sync(
+            0xffffffffu, klast < kend && klast <= min(kmax0, kmax1) &&
+                             (p.tree_anc == nullptr || klast < tree_lo));
+        if (interior) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < 4; ++j) {
+            s[j][0] *= sc;
+            s[j][1] *= sc;
+            s[j][2] *= sc;
+            s[j][3] *= sc;
+            mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+            mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+          }
+        } else {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int key = kt + kl + j * 8 + 2 * tig + (e & 1);
-            const bool row1 = e >= 2;
-            bool ok = key < kend && key <= (row1 ? kmax1 : kmax0);
-            if (p.tree_anc != nullptr && key >= tree_lo)
-              ok = ok && (((row1 ? anc1 : anc0) >> (key - tree_lo)) & 1u);
-            s[j][e] = ok ? s[j][e] * sc : -INFINITY;
-            if (row1) mx1 = fmaxf(mx1, s[j][e]); else mx0 = fmaxf(mx0, s[j][e]);
+          for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int key = kt + kl + j * 8 + 2 * tig + (e & 1);
+              const bool row1 = e >= 2;
+              bool ok = key < kend && key <= (row1 ? kmax1 : kmax0);
+              if (p.tree_anc != nullptr && key >= tree_lo)
+                ok = ok && (((row1 ? anc1 : anc0) >> (key - tree_lo)) & 1u);
+              s[j][e] = ok ? s[j][e] * sc : -INFINITY;
+              if (row1) mx1 = fmaxf(mx1, s[j][e]); else mx0 = fmaxf(mx0, s[j][e]);
+            }
           }
         }
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
@@ -275,10 +292,13 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
         }
         l0 = l0 * f0 + ps0;
         l1 = l1 * f1 + ps1;
+        // once the running maxima settle, every factor is exactly 1: skip the rescale
+        if (!__all_sync(0xffffffffu, f0 == 1.f && f1 == 1.f)) {
 #pragma unroll
-        for (int i = 0; i < NDT; ++i) {
-          o[i][0] *= f0; o[i][1] *= f0;
-          o[i][2] *= f1; o[i][3] *= f1;
+          for (int i = 0; i < NDT; ++i) {
+            o[i][0] *= f0; o[i][1] *= f0;
+            o[i][2] *= f1; o[i][3] *= f1;
+          }
         }
         // O += P . V over two k16 steps of keys
 #pragma unroll
@@ -309,37 +329,67 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
 
     // every warp is past the ring once all consumers reach this barrier
     asm volatile("bar.sync 1, %0;" ::"n"(NC * 32));
-    float* myO = bufO + kslot * RPG * D;
+    // the key slots k >= 1 hand their partials to the slot-0 warp of the same rows, which
+    // merges them in registers (weights once per row, fixed slot order)
+    if (kslot > 0) {
+      float* myO = bufO + kslot * RPG * D;
 #pragma unroll
-    for (int dt = 0; dt < NDT; ++dt) {
-      const int d = dt * 8 + 2 * tig;
-      *reinterpret_cast<float2*>(&myO[r0 * D + d]) = make_float2(o[dt][0], o[dt][1]);
-      *reinterpret_cast<float2*>(&myO[r1 * D + d]) = make_float2(o[dt][2], o[dt][3]);
-    }
-    if (tig == 0) {
-      bufM[kslot * RPG + r0] = m0;
-      bufM[kslot * RPG + r1] = m1;
-      bufL[kslot * RPG + r0] = l0;
-      bufL[kslot * RPG + r1] = l1;
+      for (int dt = 0; dt < NDT; ++dt) {
+        const int d = dt * 8 + 2 * tig;
+        *reinterpret_cast<float2*>(&myO[r0 * D + d]) = make_float2(o[dt][0], o[dt][1]);
+        *reinterpret_cast<float2*>(&myO[r1 * D + d]) = make_float2(o[dt][2], o[dt][3]);
+      }
+      if (tig == 0) {
+        bufM[kslot * RPG + r0] = m0;
+        bufM[kslot * RPG + r1] = m1;
+        bufL[kslot * RPG + r0] = l0;
+        bufL[kslot * RPG + r1] = l1;
+      }
     }
     asm volatile("bar.sync 1, %0;" ::"n"(NC * 32));
-    // merge the KS key slots of each row into slot 0
-    for (int idx = threadIdx.x; idx < RPG * D; idx += NC * 32) {
-      const int r = idx / D;
-      float M = bufM[r];
+    if (kslot == 0) {
+      float M0 = m0, M1 = m1;
 #pragma unroll
-      for (int k = 1; k < KS; ++k) M = fmaxf(M, bufM[k * RPG + r]);
-      float acc = 0.f, L = 0.f;
-#pragma unroll
-      for (int k = 0; k < KS; ++k) {
-        const float w = fast_exp2(bufM[k * RPG + r] - M);
-        acc += w * bufO[k * RPG * D + idx];
-        L += w * bufL[k * RPG + r];
+      for (int k = 1; k < KS; ++k) {
+        M0 = fmaxf(M0, bufM[k * RPG + r0]);
+        M1 = fmaxf(M1, bufM[k * RPG + r1]);
       }
-      bufO[idx] = acc;
-      if ((idx % D) == 0) {
-        finM[r] = M;
-        finL[r] = L;
+      float w0[KS], w1[KS];
+      w0[0] = fast_exp2(m0 - M0);
+      w1[0] = fast_exp2(m1 - M1);
+#pragma unroll
+      for (int k = 1; k < KS; ++k) {
+        w0[k] = fast_exp2(bufM[k * RPG + r0] - M0);
+        w1[k] = fast_exp2(bufM[k * RPG + r1] - M1);
+      }
+#pragma unroll
+      for (int dt = 0; dt < NDT; ++dt) {
+        const int d = dt * 8 + 2 * tig;
+        float a0 = fmaf(w0[0], o[dt][0], 0.f), a1 = fmaf(w0[0], o[dt][1], 0.f);
+        float a2 = fmaf(w1[0], o[dt][2], 0.f), a3 = fmaf(w1[0], o[dt][3], 0.f);
+#pragma unroll
+        for (int k = 1; k < KS; ++k) {
+          const float2 u = *reinterpret_cast<const float2*>(&bufO[(k * RPG + r0) * D + d]);
+          const float2 v = *reinterpret_cast<const float2*>(&bufO[(k * RPG + r1) * D + d]);
+          a0 = fmaf(w0[k], u.x, a0);
+          a1 = fmaf(w0[k], u.y, a1);
+          a2 = fmaf(w1[k], v.x, a2);
+          a3 = fmaf(w1[k], v.y, a3);
+        }
+        *reinterpret_cast<float2*>(&bufO[r0 * D + d]) = make_float2(a0, a1);
+        *reinterpret_cast<float2*>(&bufO[r1 * D + d]) = make_float2(a2, a3);
+      }
+      if (tig == 0) {
+        float L0 = fmaf(w0[0], l0, 0.f), L1 = fmaf(w1[0], l1, 0.f);
+#pragma unroll
+        for (int k = 1; k < KS; ++k) {
+          L0 = fmaf(w0[k], bufL[k * RPG + r0], L0);
+          L1 = fmaf(w1[k], bufL[k * RPG + r1], L1);
+        }
+        finM[r0] = M0;
+        finM[r1] = M1;
+        finL[r0] = L0;
+        finL[r1] = L1;
       }
     }
   }
@@ -478,10 +528,12 @@ template <int D, int NRT, int KS>
 static int max_clusters_t(int cs) {
   auto kern = attn_kernel<D, NRT, KS>;
   constexpr int smem = attn_smem_bytes<D, NRT, KS>();
+  // a refused query: portable sizes fall back to one CTA per SM, larger ones are not used
+  const int fallback = cs <= 8 ? sm_count(current_device()) / cs : 0;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
       cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
     cudaGetLastError();
-    return sm_count(current_device()) / cs;
+    return fallback;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cs, 1, 1);
@@ -497,7 +549,7 @@ static int max_clusters_t(int cs) {
   int c = 0;
   if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) != cudaSuccess || c <= 0) {
     cudaGetLastError();
-    c = sm_count(current_device()) / cs;
+    c = fallback;
   }
   return c;
 }
@@ -538,9 +590,10 @@ AttnPlan plan(int B, int Hq, int Hk, int qL, int D, int L) {
   pl.nrg = (tiles + nrt - 1) / nrt;
   const int heads = B * Hk * pl.nrg;
   // key splits per head: as many CTAs as run at once in a single wave (clusters of ns CTAs
-  // merge their splits through distributed shared memory; ns <= 8 portable sizes, chosen by
-  // how many such clusters the device co-schedules), each streaming >= 128 keys; cluster
-  // groups merge through the workspace
+  // merge their splits through distributed shared memory; ns <= 16, 16 being a non-portable
+  // size the device may refuse, chosen by how many such clusters the device co-schedules),
+  // each streaming >= 128 keys; cluster groups merge through the workspace. At equal split
+  // counts the larger cluster wins: fewer groups, and with one group no merge kernel at all.
   const int max_splits = std::max(1, L / 128);
   const int force = env_int("DSPARK_ATTN_SPLITS", 0);
   int ns = 1, ng = 1;
@@ -548,14 +601,26 @@ AttnPlan plan(int B, int Hq, int Hk, int qL, int D, int L) {
     ns = std::min(force, 8);
     ng = (force + ns - 1) / ns;
   } else {
-    for (int c : {8, 6, 4, 3, 2}) {
+    // Modelled as: every CTA streams ceil(L / splits / 64) key tiles at ~1.3 us each (64 packed
+    // rows, measured on B200), and a second cluster group adds the workspace merge pass
+    // (~7 us: the merge launch and its round trip); the fixed per-launch costs are common to
+    // every plan. Cluster groups are limited to what the device co-schedules in one wave.
+    const double t_tile = 1.3, t_merge = 7.0;
+    double best = 1e30;
+    for (int c : {16, 8, 6, 4, 3, 2, 1}) {
       if (c > max_splits) continue;
-      const int fit = max_clusters(D, nrt, pl.ks, c) / std::max(1, heads);  // clusters per head
-      if (fit < 1) continue;
-      const int g = std::max(1, std::min(fit, max_splits / c));
-      if (c * g > ns * ng) {
-        ns = c;
-        ng = g;
+      const int fit = c == 1 ? sm_count(current_device()) / std::max(1, heads)
+                             : max_clusters(D, nrt, pl.ks, c) / std::max(1, heads);
+      const int gmax = std::min({fit, max_splits / c, 32});
+      for (int g = 1; g <= gmax; ++g) {
+        const int keys = (L + c * g - 1) / (c * g);
+        const int tiles = (keys + KT - 1) / KT;
+        const double t = tiles * t_tile + (g > 1 ? t_merge : 0.0);
+        if (t < best - 1e-9) {  // ties keep the larger cluster (tried first)
+          best = t;
+          ns = c;
+          ng = g;
+        }
       }
     }
   }
@@ -631,6 +696,8 @@ int run(AttnParams p, const AttnPlan* plan_in, cudaStream_t stream) {
   p.ng = pl.ng;
   p.chunk = pl.chunk;
   if (pl.ng > 32) return fail(DSPARK_ERR_UNSUPPORTED, "attn: at most 32 cluster groups (got %d)", pl.ng);
+  if (pl.ns < 1 || pl.ns > 16)
+    return fail(DSPARK_ERR_UNSUPPORTED, "attn: cluster of %d key splits (1..16)", pl.ns);
   if (pl.ng > 1 && p.ws == nullptr)
     return fail(DSPARK_ERR_ARG, "attn: this launch needs a workspace of %zu bytes",
                 workspace_bytes(pl, p.B, p.Hk, p.D));
