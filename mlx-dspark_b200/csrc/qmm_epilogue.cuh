@@ -11,10 +11,39 @@ namespace qmm {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
 
-// Run by `nwarps` warps starting at warp `warp0` of the CTA.
+// Rows per warp of the prefetched residual epilogue (the streaming engine: 4 epilogue warps,
+// at most 32 owned rows, so nwarps * kResidRows covers every row).
+constexpr int kResidRows = 8;
+
+// The residual words the EPI_RESID epilogue of tile n0 reads, loaded by the same threads ahead
+// of the split-K reduction so that their latency overlaps the wait for the partial tiles (the
+// residual comes from an earlier kernel).
+template <int TN>
+__device__ __forceinline__ void resid_prefetch(const QmmParams& p, int rank, int cs, int n0,
+                                               int nwarps, int warp0, uint32_t (&pre)[2 * kResidRows]) {
+  const int tidx = int(threadIdx.x) - warp0 * 32;
+  const int warp = tidx >> 5, lane = tidx & 31;
+  const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
+#pragma unroll
+  for (int i = 0; i < kResidRows; ++i) {
+    const int mi = warp + i * nwarps;
+    const int m = rank + mi * cs;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int n = n0 + (lane + 32 * h) * 2;
+      pre[i * 2 + h] = (mi < nmine && n < p.N)
+                           ? __ldcg(reinterpret_cast<const unsigned int*>(p.resid + (size_t)m * p.ldr + n))
+                           : 0u;
+    }
+  }
+}
+
+// Run by `nwarps` warps starting at warp `warp0` of the CTA. `pre`: the residual words from
+// resid_prefetch for this tile (EPI_RESID, 128-column tiles), or null to load them here.
 template <int EPI, int TN, int PSTR>
 __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, int rank, int cs,
-                                         int ntile, int n0, int nwarps, int warp0 = 0) {
+                                         int ntile, int n0, int nwarps, int warp0 = 0,
+                                         const uint32_t* pre = nullptr) {
   const int nthr = nwarps * 32;
   const int tidx = int(threadIdx.x) - warp0 * 32;
   const int warp = tidx >> 5, lane = tidx & 31;
@@ -35,6 +64,32 @@ __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, i
     }
   } else if constexpr (EPI == EPI_RESID) {
     // out = bf16(bf16(acc) + resid); ssq_out[ntile][m] = sum over the tile of out^2
+    if (pre != nullptr && TN == 128) {
+      // the resid_prefetch map: warp w takes rows mi = w, w + nwarps, ... (at most kResidRows
+      // per warp), lane l columns 2l and 2l + 64 of the tile
+#pragma unroll
+      for (int i = 0; i < kResidRows; ++i) {
+        const int mi = warp + i * nwarps;
+        if (mi >= nmine) break;
+        const int m = rank + mi * cs;
+        float ss = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int n2 = lane + 32 * h;
+          const int n = n0 + n2 * 2;
+          if (n >= p.N) continue;
+          const uint32_t rr = pre[i * 2 + h];
+          const float h0 = round_bf16(round_bf16(red[m * PSTR + n2 * 2]) + bf16_lo(rr));
+          const float h1 = round_bf16(round_bf16(red[m * PSTR + n2 * 2 + 1]) + bf16_hi(rr));
+          *reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n) = pack_bf16x2(h0, h1);
+          ss += h0 * h0 + h1 * h1;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0 && p.ssq_out != nullptr) p.ssq_out[ntile * p.ssq_stride + m] = ss;
+      }
+      return;
+    }
     for (int mi = warp; mi < nmine; mi += nwarps) {
       const int m = rank + mi * cs;
       float ss = 0.f;

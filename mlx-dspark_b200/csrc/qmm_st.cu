@@ -827,6 +827,9 @@ __global__ void __launch_bounds__(NTHR, 1)
       const int pbuf = j & 1;
       const int t = int(blockIdx.y) + j * nclus;
       const float* pb = part + pbuf * cs * 2 * ro * PSTR;
+      // the residual of this tile comes from an earlier kernel: load it before the wait
+      uint32_t pre[2 * kResidRows];
+      if constexpr (EPI == EPI_RESID) resid_prefetch<TN>(p, rank, cs, t * TN, NWE, WARP_EPI, pre);
       if (etid == 0) mbar_arrive_expect_tx(&ready[pbuf], peer_bytes);
       if (ok) ok = mbar_wait_cluster(&ready[pbuf], (j >> 1) & 1, p.status, kErrWaitCluster);
       // sum the partials of each owned row: the two k halves of each rank, then the ranks in
@@ -855,7 +858,8 @@ __global__ void __launch_bounds__(NTHR, 1)
         else
           mbar_arrive(&freeb[pbuf]);
       }
-      epilogue<EPI, TN, PSTR>(p, red, rank, cs, t, t * TN, NWE, WARP_EPI);
+      epilogue<EPI, TN, PSTR>(p, red, rank, cs, t, t * TN, NWE, WARP_EPI,
+                              EPI == EPI_RESID ? pre : nullptr);
       asm volatile("bar.sync 2, %0;" ::"n"(NE));  // red reads done
     }
   }
