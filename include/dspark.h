@@ -332,6 +332,38 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf,
  * block's K/V; dspark_accept then trims the rejected tail). */
 int dspark_verify_prepare(int32_t* len, int R, const dspark_fwd_buffers* buf, void* stream);
 
+/* ---- all-gather over peer memory (tensor-parallel verify) ------------------------------
+ * Replaces the NCCL all-gathers between the column-sharded projections (the collective the
+ * reference's verify path does not have: it runs 27B targets on one Apple GPU, target.py:208-221;
+ * the fused peer-store variant is the survey's multi-GPU plan). Set-up, once per rank:
+ * dspark_ipc_alloc an arena (zero-filled device memory and its IPC handle), share the handles
+ * between the ranks' processes, dspark_ipc_open every peer's handle. The arena layout is the
+ * caller's, identical on every rank: a flag area (uint32 [8 buffers][8 ranks]), a counter area
+ * (uint32 [8][2]) and the gather buffers ([world][seg_bytes] each). */
+#define DSPARK_IPC_HANDLE_BYTES 64
+
+int dspark_ipc_alloc(size_t bytes, void** ptr, void* handle /* DSPARK_IPC_HANDLE_BYTES */);
+int dspark_ipc_open(const void* handle, void** ptr);
+int dspark_ipc_close(void* ptr);
+int dspark_ipc_free(void* ptr);
+
+typedef struct dspark_p2p_gather_args {
+  void* const* arenas;   /* [world] every rank's arena as mapped in this process (own: local) */
+  const void* src;       /* this rank's segment, seg_bytes (16-byte aligned) */
+  size_t seg_bytes;      /* multiple of 16 */
+  size_t flags_off;      /* byte offsets inside every arena (multiples of 16) */
+  size_t count_off;
+  size_t dst_off;        /* destination [world][seg_bytes]; segment `rank` receives src */
+  int rank, world;       /* world <= 8 */
+  int buf;               /* flag / counter slot of the destination buffer, 0..7 */
+} dspark_p2p_gather_args;
+
+/* One all-gather: this rank's segment lands in segment `rank` of the destination buffer of every
+ * arena; the launch returns (on the stream) once every rank's segment has landed here. All ranks
+ * must issue the same gathers in the same order. Waits on peers are bounded (~2 s): a timeout
+ * sets the device status word. */
+int dspark_p2p_allgather(const dspark_p2p_gather_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -63,6 +63,15 @@ class FwdBuffers(C.Structure):
                 ("attn_ws_bytes", sz), ("rows_cap", i32)]
 
 
+IPC_HANDLE_BYTES = 64
+
+
+class P2PGatherArgs(C.Structure):
+    """``dspark_p2p_gather_args`` (include/dspark.h)."""
+    _fields_ = [("arenas", C.POINTER(vp)), ("src", vp), ("seg_bytes", sz), ("flags_off", sz),
+                ("count_off", sz), ("dst_off", sz), ("rank", i32), ("world", i32), ("buf", i32)]
+
+
 class QmmArgs(C.Structure):
     _fields_ = [("x", vp), ("ldx", i64), ("x_seg", i64), ("x_seg_stride", i64),
                 ("M", i32), ("K", i32), ("N", i32), ("bits", i32),
@@ -80,6 +89,11 @@ EPI_PLAIN, EPI_RESID, EPI_SWIGLU, EPI_QKROPE = range(4)
 
 _SIGS = {
     "dspark_qmm_fused": (i32, [C.POINTER(QmmArgs), vp]),
+    "dspark_ipc_alloc": (i32, [sz, C.POINTER(vp), vp]),
+    "dspark_ipc_open": (i32, [vp, C.POINTER(vp)]),
+    "dspark_ipc_close": (i32, [vp]),
+    "dspark_ipc_free": (i32, [vp]),
+    "dspark_p2p_allgather": (i32, [C.POINTER(P2PGatherArgs), vp]),
     "dspark_rope_inv_freq": (i32, [vp, i32, f32, vp]),
     "dspark_version": (i32, []),
     "dspark_last_error": (C.c_char_p, []),

@@ -13,6 +13,10 @@ columns are split over P ranks (one process per GPU, NCCL over NVLink):
   SwiGLU activations before down, and the vocab-sharded logits at the end. The gathered
   ``[P, M, K/P]`` tensors feed the next projection directly: the QMM reads x as segmented
   rows (``dspark_qmm_fused`` with ``x_seg``), so no transpose copy runs.
+* The gathers run over peer memory by default (``comm="p2p"``): every rank maps every peer's
+  arena through CUDA IPC and one ``dspark_p2p_allgather`` launch stores its segment into all
+  of them and waits, bounded, on the peers' completion counters. ``comm="nccl"`` uses NCCL's
+  all-gather instead (the baseline).
 
 Every rank holds the full embedding and norm weights and computes the same argmax / accept /
 rollback, so all ranks' cache lengths stay identical. Weights are generated from one seed as
@@ -30,6 +34,18 @@ import torch
 from . import _lib, quant
 from ._torch import ptr, require_cuda, stream_of
 from .target import Qwen3Config, _interleave32, _qw_struct  # noqa: F401
+
+
+class _CudaBytes:
+    """A device byte range exposed through ``__cuda_array_interface__`` (zero-copy view)."""
+
+    def __init__(self, addr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (addr, False),
+                                         "version": 3, "strides": None}
+
+
+def _device_bytes(addr: int, n: int, device) -> torch.Tensor:
+    return torch.as_tensor(_CudaBytes(addr, n), device=device)
 
 
 def _rows(w: quant.QWeight, a: int, b: int) -> quant.QWeight:
@@ -64,8 +80,13 @@ class TPTarget:
     ``None`` with ``world == 1``). :meth:`verify` has :meth:`Target.verify`'s contract."""
 
     def __init__(self, cfg: Qwen3Config, rank: int, world: int, *, group=None, kv_cap: int = 4096,
-                 seed: int = 0, std: float = 0.02, max_rows: int = 32, device="cuda"):
+                 seed: int = 0, std: float = 0.02, max_rows: int = 32, device="cuda",
+                 comm: str = "p2p"):
         self.cfg, self.rank, self.world, self.group = cfg, int(rank), int(world), group
+        if comm not in ("p2p", "nccl"):
+            raise ValueError(f"comm must be 'p2p' or 'nccl', not {comm!r}")
+        self.comm = comm if self.world > 1 else "local"
+        self._arena, self._peers = None, []
         self.device = torch.device(device)
         require_cuda(torch.empty(1, device=self.device))
         self.kv_cap, self.max_rows = int(kv_cap), int(max_rows)
@@ -124,17 +145,23 @@ class TPTarget:
         self.hbytes = R * self.hs * 2
         self.pack = self.hbytes + self.tiles * 32 * 4
         u8 = dict(dtype=torch.uint8, device=dev)
+        # gather destinations: two per kind (alternating: a buffer is rewritten only after the
+        # kernels that read it have run on every rank), one for the logits
+        self._segs = {"attn": (R * self.hq * D * 2, 2), "pack": (self.pack, 2),
+                      "act": (R * (I // P) * 2, 2), "logits": (R * (V // P) * 2, 1)}
+        seg = self._alloc_gather_buffers() if self.comm == "p2p" else {
+            k: [torch.zeros(P * n, **u8) for _ in range(c)] for k, (n, c) in self._segs.items()}
         self.b = {
             "h0": torch.empty((R, H), **bf),                    # embedding output (replicated)
             "pack": torch.zeros(self.pack, **u8),
-            "pack_seg": [torch.zeros((P, self.pack), **u8) for _ in range(2)],
+            "pack_seg": [t.view(P, self.pack) for t in seg["pack"]],
             "xq": torch.empty((R, self.hq * D), **bf),
             "attn": torch.empty((R, self.hq * D), **bf),
-            "attn_seg": torch.empty((P, R, self.hq * D), **bf),
+            "attn_seg": [t.view(torch.bfloat16).view(P, R, self.hq * D) for t in seg["attn"]],
             "act": torch.empty((R, I // P), **bf),
-            "act_seg": torch.empty((P, R, I // P), **bf),
+            "act_seg": [t.view(torch.bfloat16).view(P, R, I // P) for t in seg["act"]],
             "logits": torch.empty((R, V // P), **bf),
-            "logits_seg": torch.empty((P, R, V // P), **bf),
+            "logits_seg": seg["logits"][0].view(torch.bfloat16).view(P, R, V // P),
             "logits_full": torch.empty((R, V), **bf),
             "ssq0": torch.zeros(1024 * 32, dtype=torch.float32, device=dev),
             "inv_freq": torch.empty(D // 2, dtype=torch.float32, device=dev),
@@ -155,13 +182,70 @@ class TPTarget:
                                      ptr(b["row_kv"]), ptr(b["kv_len"]), ptr(b["row_start"]),
                                      ptr(b["q_len"]), ptr(b["kv_off"]), None, 0, R)
 
-    def _gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
-        if self.world == 1:
-            out.view(-1).copy_(inp.reshape(-1))
-            return
+    # arena layout (identical on every rank): flags uint32 [8][8] at 0, counters uint32 [8][2]
+    # at 256, then the gather buffers, 256-byte aligned, [P][segment bytes] each
+    _FLAGS_OFF, _COUNT_OFF, _DATA_OFF = 0, 256, 512
+
+    def _alloc_gather_buffers(self) -> dict:
+        """One IPC arena per rank holding every gather destination; peers' arenas are mapped
+        so that ``dspark_p2p_allgather`` stores straight into them."""
         import torch.distributed as dist
 
-        dist.all_gather_into_tensor(out, inp, group=self.group)
+        P = self.world
+        self._slots, off = {}, self._DATA_OFF
+        for k, (n, c) in self._segs.items():
+            for i in range(c):
+                self._slots[(k, i)] = (len(self._slots), off, n)
+                off += (P * n + 255) // 256 * 256
+        base, handle = C.c_void_p(), (C.c_char * _lib.IPC_HANDLE_BYTES)()
+        _lib.check(_lib.lib.dspark_ipc_alloc(off, C.byref(base), handle))
+        self._arena = base.value
+        handles = [None] * P
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        ptrs = []
+        for q in range(P):
+            if q == self.rank:
+                ptrs.append(self._arena)
+                continue
+            h = (C.c_char * _lib.IPC_HANDLE_BYTES).from_buffer_copy(handles[q])
+            peer = C.c_void_p()
+            _lib.check(_lib.lib.dspark_ipc_open(h, C.byref(peer)))
+            self._peers.append(peer.value)
+            ptrs.append(peer.value)
+        self._arena_ptrs = (C.c_void_p * P)(*ptrs)
+        views = {}
+        for (k, i), (_, o, n) in self._slots.items():
+            views.setdefault(k, []).append(_device_bytes(self._arena + o, P * n, self.device))
+        return views
+
+    def close(self) -> None:
+        """Unmap the peers' arenas and free this rank's (after the device is idle)."""
+        if self._arena is None:
+            return
+        torch.cuda.synchronize(self.device)
+        for q in self._peers:
+            _lib.lib.dspark_ipc_close(C.c_void_p(q))
+        self._peers = []
+        _lib.lib.dspark_ipc_free(C.c_void_p(self._arena))
+        self._arena = None
+
+    def _gather(self, kind: str, i: int, inp: torch.Tensor) -> None:
+        """All-gather this rank's ``inp`` into segment ``rank`` of destination ``(kind, i)``."""
+        out = {"attn": self.b["attn_seg"], "pack": self.b["pack_seg"],
+               "act": self.b["act_seg"]}.get(kind)
+        out = self.b["logits_seg"] if kind == "logits" else out[i]
+        if self.comm == "local":
+            out.view(-1).copy_(inp.view(-1).view(out.dtype))
+        elif self.comm == "nccl":
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(out.view(-1), inp.view(-1).view(out.dtype), group=self.group)
+        else:
+            slot, off, n = self._slots[(kind, i)]
+            a = _lib.P2PGatherArgs(C.cast(self._arena_ptrs, C.POINTER(C.c_void_p)), inp.data_ptr(), n,
+                                   self._FLAGS_OFF,
+                                   self._COUNT_OFF, off, self.rank, self.world, slot)
+            _lib.check(_lib.lib.dspark_p2p_allgather(C.byref(a), stream_of(inp)))
 
     def _qmm(self, s, w: quant.QWeight, x, ldx, M, K, epi, out=None, ldo=0, *, x_seg=0,
              x_seg_stride=0, norm_w=None, ssq_in=None, ssq_n=0, ssq_seg=0, ssq_seg_stride=0,
@@ -220,7 +304,8 @@ class TPTarget:
         cur = 0
         q_st = _lib.i64_array([0, D, self.hq * D])
         k_st = _lib.i64_array([0, self.kv_cap * D, D])
-        for L in self.layers:
+        for li, L in enumerate(self.layers):
+            j = li & 1  # alternating gather destinations
             self._qmm(s, L["qkv"], x, ldx, R, H, _lib.EPI_QKROPE, x_seg=xseg, x_seg_stride=xss,
                       norm_w=L["in_norm"], ssq_in=ssq, ssq_n=ssq_n, ssq_seg=sseg,
                       ssq_seg_stride=ssegs, layer=L)
@@ -228,27 +313,27 @@ class TPTarget:
                 ptr(b["xq"]), q_st, ptr(L["k_cache"]), k_st, ptr(L["v_cache"]), k_st, 1, self.hq,
                 self.hk, R, D, Lm, ptr(b["kv_len"]), float(D ** -0.5), 1, None, ptr(b["attn"]),
                 q_st, ptr(b["attn_ws"]), b["attn_ws"].numel(), s))
-            self._gather(b["attn_seg"], b["attn"])
+            self._gather("attn", j, b["attn"])
             # O: x = all heads' attention ([P, R, hq*D] segments), residual = own hidden shard;
             # the new shard and its statistics land in this rank's pack
-            self._qmm(s, L["o"], b["attn_seg"], self.hq * D, R, Hq * D, _lib.EPI_RESID, loc, hs,
+            self._qmm(s, L["o"], b["attn_seg"][j], self.hq * D, R, Hq * D, _lib.EPI_RESID, loc, hs,
                       x_seg=self.hq * D, x_seg_stride=self.max_rows * self.hq * D,
                       resid=resid, ldr=ldr, ssq_out=loc + hb)
             mid = b["pack_seg"][cur]
-            self._gather(mid, b["pack"])
+            self._gather("pack", cur, b["pack"])
             mb = mid.data_ptr()
             # gate/up: post-attention norm over the gathered hidden state, SwiGLU shard
             self._qmm(s, L["gate_up"], mb, hs, R, H, _lib.EPI_SWIGLU, b["act"], I // P,
                       x_seg=hs, x_seg_stride=pk // 2, norm_w=L["post_norm"], ssq_in=mb + hb,
                       ssq_n=P * T, ssq_seg=T, ssq_seg_stride=pk // 4, n_act=I // P)
-            self._gather(b["act_seg"], b["act"])
+            self._gather("act", j, b["act"])
             # down: x = all activations, residual = own shard of the mid state
-            self._qmm(s, L["down"], b["act_seg"], I // P, R, I, _lib.EPI_RESID, loc, hs,
+            self._qmm(s, L["down"], b["act_seg"][j], I // P, R, I, _lib.EPI_RESID, loc, hs,
                       x_seg=I // P, x_seg_stride=self.max_rows * (I // P), resid=mb + r * pk,
                       ldr=hs, ssq_out=loc + hb)
             cur ^= 1
             nxt = b["pack_seg"][cur]
-            self._gather(nxt, b["pack"])
+            self._gather("pack", cur, b["pack"])
             nb = nxt.data_ptr()
             x, ldx, xseg, xss = nb, hs, hs, pk // 2
             ssq, ssq_n, sseg, ssegs = nb + hb, P * T, T, pk // 4
@@ -257,7 +342,7 @@ class TPTarget:
         self._qmm(s, self.lm_head, x, ldx, R, H, _lib.EPI_PLAIN, b["logits"], V // P, x_seg=xseg,
                   x_seg_stride=xss, norm_w=self.final_norm, ssq_in=ssq, ssq_n=ssq_n,
                   ssq_seg=sseg, ssq_seg_stride=ssegs)
-        self._gather(b["logits_seg"], b["logits"])
+        self._gather("logits", 0, b["logits"])
         b["logits_full"][:R].view(R, P, V // P).copy_(b["logits_seg"][:, :R].transpose(0, 1))
         return b["logits_full"][:R]
 

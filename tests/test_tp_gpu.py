@@ -2,8 +2,9 @@
 
 * P = 1 against the oracle's Qwen3 forward (bars as in test_forward_gpu.py): exercises the fused
   QMM entry point, segmented x rows and the gather-based layer sequence on one GPU;
-* P = 2 against P = 1 on the same seeded model and cache (two GPUs, NCCL; skipped with fewer):
-  logits within the bf16 noise of the single-rank forward, identical cache lengths.
+* P = 2 against P = 1 on the same seeded model and cache (two GPUs, skipped with fewer), with
+  the gathers over peer memory and over NCCL: logits within the bf16 noise of the single-rank
+  forward for two blocks in a row, identical on both ranks, identical cache lengths.
 """
 
 from __future__ import annotations
@@ -69,7 +70,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _tp_worker(rank, world, port, q):
+def _tp_worker(rank, world, port, q, comm):
     import datetime
 
     import torch.distributed as dist
@@ -88,7 +89,7 @@ def _tp_worker(rank, world, port, q):
         _lib.ensure_init(rank)
         cfg = tiny_config(bits=8)
         t = TPTarget(cfg, rank, world, group=dist.group.WORLD, kv_cap=1024, seed=8,
-                     max_rows=16, device=dev)
+                     max_rows=16, device=dev, comm=comm)
         _fill_cache(t, 300, seed=5)
         g = torch.Generator().manual_seed(9)
         ids = torch.randint(0, cfg.vocab, (16,), generator=g, dtype=torch.int32).to(dev)
@@ -96,13 +97,23 @@ def _tp_worker(rank, world, port, q):
         logits = t.verify(ids, lens).float().cpu().numpy()
         out = t.accept_and_rollback(t.b["logits_full"][:16], ids, lens)
         torch.cuda.synchronize()
-        q.put((rank, logits, int(lens[0]), int(out["n"][0]), _lib.device_status(rank)))
+        ln = int(lens[0])
+        # a second block at the same position (its K/V rows overwrite the first's) through the
+        # same gather buffers: the peers' completion counters must advance in step
+        ids2 = torch.randint(0, cfg.vocab, (16,), generator=g, dtype=torch.int32).to(dev)
+        lens.fill_(300)
+        logits2 = t.verify(ids2, lens).float().cpu().numpy()
+        torch.cuda.synchronize()
+        st = _lib.device_status(rank)
+        t.close()
+        q.put((rank, logits, logits2, ln, int(out["n"][0]), st))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tp2_matches_tp1(cuda):
+@pytest.mark.parametrize("comm", ["p2p", "nccl"])
+def test_tp2_matches_tp1(cuda, comm):
     import torch.multiprocessing as mp
 
     from mlx_dspark_b200.target import tiny_config
@@ -111,13 +122,13 @@ def test_tp2_matches_tp1(cuda):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q, comm)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
     for _ in procs:
-        rank, logits, ln, n, st = q.get(timeout=600)
-        res[rank] = (logits, ln, n, st)
+        rank, logits, logits2, ln, n, st = q.get(timeout=600)
+        res[rank] = (logits, logits2, ln, n, st)
     for p in procs:
         p.join(timeout=120)
     cfg = tiny_config(bits=8)
@@ -127,9 +138,14 @@ def test_tp2_matches_tp1(cuda):
     ids = torch.randint(0, cfg.vocab, (16,), generator=g, dtype=torch.int32).to(cuda)
     lens = torch.tensor([300], dtype=torch.int32, device=cuda)
     ref = t.verify(ids, lens).float().cpu().numpy()
+    ids2 = torch.randint(0, cfg.vocab, (16,), generator=g, dtype=torch.int32).to(cuda)
+    lens.fill_(300)
+    ref2 = t.verify(ids2, lens).float().cpu().numpy()
     for rank in (0, 1):
-        logits, ln, n, st = res[rank]
+        logits, logits2, ln, n, st = res[rank]
         assert st == 0
         assert _rel(logits, ref) <= 1e-2, (rank, _rel(logits, ref))
+        assert _rel(logits2, ref2) <= 1e-2, (rank, _rel(logits2, ref2))
         assert ln == 300 + n + 1
     assert np.array_equal(res[0][0], res[1][0])  # every rank holds the same logits
+    assert np.array_equal(res[0][1], res[1][1])
