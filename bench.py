@@ -68,8 +68,9 @@ def parse():
                     help="BASELINE configs[3]: 32B-shaped 8-bit verify at 32k context, every "
                          "projection column-sharded over the ranks (NCCL all-gathers)")
     ap.add_argument("--tp-context", type=int, default=32768)
-    ap.add_argument("--tp-comm", choices=["p2p", "nccl"], default="p2p",
-                    help="--tp gathers: over peer memory (dspark_p2p_allgather) or NCCL")
+    ap.add_argument("--tp-comm", choices=["fused", "p2p", "nccl"], default="nccl",
+                    help="--tp gathers: fused into the projections' peer stores, separate "
+                         "peer-memory launches (dspark_p2p_allgather), or NCCL")
     ap.add_argument("--batch-requests", type=int, default=64,
                     help="requests in the whole job (256 in configs[4]; the KV of 256 "
                          "requests is ~147 GB, so N=1 runs a sample)")
@@ -602,8 +603,8 @@ def run_batch(args):
 def run_tp(args):
     """Qwen3-32B-shaped 8-bit target (64 layers, hidden 5120, GQA 64/8),
     one request verifying 16-row blocks at 32k context, projections column-sharded over the
-    ranks with all-gathers between them (mlx_dspark_b200.target_tp; over peer memory by
-    default, NCCL with --tp-comm nccl). A step = verify
+    ranks with all-gathers between them (mlx_dspark_b200.target_tp; NCCL by default, the
+    fastest measured; --tp-comm fused / p2p for the peer-memory transports). A step = verify
     forward + argmax + accept + rollback to a seeded accept length, captured in one CUDA graph
     (collectives included). value = verified rows per second of the one request (strong
     scaling: the same work at every N)."""
@@ -703,7 +704,8 @@ def run_tp(args):
                       "parallelism": f"tp{world} (column-sharded projections, heads per rank, "
                                      + ("NCCL all-gathers)" if t.comm == "nccl" else
                                         "peer-memory all-gathers)" if t.comm == "p2p" else
-                                        "no collectives)")},
+                                        "gathers fused into the projections' peer stores)"
+                                        if t.comm == "fused" else "no collectives)")},
            "per_gpu_hbm_bytes_per_step": int(w_bytes + kv_bytes),
            "per_gpu_hbm_gbs": round((w_bytes + kv_bytes) / (ms / args.steps / 1e3) / 1e9, 1),
            "gpu_launches": launches * args.steps, "device_status": _lib.device_status(local)}

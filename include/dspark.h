@@ -115,6 +115,22 @@ typedef struct {
   const int64_t* row_kv;            /* [M] cache slot offsets (elements), or NULL */
   int ssq_seg;                      /* > 0: entry e of ssq_in at (e / ssq_seg) * ssq_seg_stride */
   int64_t ssq_seg_stride;           /*      + (e % ssq_seg) * ssq_stride (gathered statistics) */
+  /* Tensor-parallel gathers fused into the projections (K % 512 == 0, not with
+   * DSPARK_QMM_ST_TC). Peer stores (RESID / SWIGLU): every output element, and every RESID
+   * statistic, is also stored at its address + peer_delta[s] for each rank s < peer_world
+   * (peer_delta[own rank] = 0: the buffers sit at one offset in every rank's IPC arena, see
+   * dspark_ipc_alloc). After each output tile the writing CTA adds the number of elements it
+   * stored to the uint32 at peer_flag + peer_delta[s] (system-scope release). peer_world = 0: off. */
+  int peer_world;
+  int64_t peer_delta[8];
+  uint32_t* peer_flag;
+  /* Wait (before x is read) until wait_flag[s] >= wait_state[0] + wait_elems for every source
+   * s < wait_world (bounded, ~2 s); the launch's last CTA then advances wait_state[0] by
+   * wait_elems (wait_state[1] counts the launch's finished CTAs). wait_flag = NULL: no wait. */
+  const uint32_t* wait_flag;
+  int wait_world;
+  uint32_t wait_elems;
+  uint32_t* wait_state;
 } dspark_qmm_args;
 
 int dspark_qmm_fused(const dspark_qmm_args* a, void* stream);

@@ -82,7 +82,10 @@ class QmmArgs(C.Structure):
                 ("hq", i32), ("hk", i32), ("q_norm", vp), ("k_norm", vp), ("inv_freq", vp),
                 ("q_out", vp), ("ldq", i64), ("k_cache", vp), ("v_cache", vp),
                 ("k_sh", i64), ("k_ss", i64), ("v_sh", i64), ("v_ss", i64), ("kv_cap", i32),
-                ("row_pos", vp), ("row_kv", vp), ("ssq_seg", i32), ("ssq_seg_stride", i64)]
+                ("row_pos", vp), ("row_kv", vp), ("ssq_seg", i32), ("ssq_seg_stride", i64),
+                ("peer_world", i32), ("peer_delta", i64 * 8), ("peer_flag", vp),
+                ("wait_flag", vp), ("wait_world", i32), ("wait_elems", C.c_uint32),
+                ("wait_state", vp)]
 
 
 EPI_PLAIN, EPI_RESID, EPI_SWIGLU, EPI_QKROPE = range(4)

@@ -254,6 +254,19 @@ int dspark_qmm_fused(const dspark_qmm_args* a, void* stream) {
   p.k_sh = a->k_sh; p.k_ss = a->k_ss; p.v_sh = a->v_sh; p.v_ss = a->v_ss;
   p.kv_cap = a->kv_cap;
   p.row_pos = a->row_pos; p.row_kv = a->row_kv;
+  if (a->peer_world < 0 || a->peer_world > 8 || (a->peer_world > 0 && !a->peer_flag))
+    return fail(DSPARK_ERR_ARG, "qmm_fused: peer stores need 1..8 ranks and a flag");
+  if (a->peer_world > 0 && epi != qmm::EPI_RESID && epi != qmm::EPI_SWIGLU)
+    return fail(DSPARK_ERR_UNSUPPORTED, "qmm_fused: peer stores serve the RESID / SWIGLU epilogues");
+  if (a->wait_flag && (a->wait_world < 1 || a->wait_world > 8 || !a->wait_state))
+    return fail(DSPARK_ERR_ARG, "qmm_fused: a wait needs 1..8 sources and its state words");
+  p.peer_world = a->peer_world;
+  for (int s = 0; s < 8; ++s) p.peer_delta[s] = a->peer_delta[s];
+  p.peer_flag = a->peer_flag;
+  p.wait_flag = a->wait_flag;
+  p.wait_world = a->wait_world;
+  p.wait_elems = a->wait_elems;
+  p.wait_state = a->wait_state;
   if (epi == qmm::EPI_QKROPE) {
     p.out = p.qout;
     p.ldo = 0;

@@ -237,6 +237,35 @@ __device__ __forceinline__ void st_async_v2(uint32_t addr, float a, float b, uin
       : "memory");
 }
 
+// Release (system scope) add to a counter in this or another GPU's memory: the writes this thread
+// (and, cumulatively, the threads it synchronised with) made before are visible to whoever
+// acquires the new value.
+__device__ __forceinline__ void red_add_release_sys(uint32_t* addr, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// Wait until the monotonic counter *f reaches `target` (wrap-safe); false (and `code` recorded)
+// if it has not within kWaitLimitNs.
+__device__ __forceinline__ bool wait_counter_sys(const uint32_t* f, uint32_t target, int* status,
+                                                 int code) {
+  if (int32_t(ld_acquire_sys(f) - target) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (int32_t(ld_acquire_sys(f) - target) < 0) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      report_error(status, code);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
 // 16-byte global load through L2 only (data another kernel wrote)
 __device__ __forceinline__ uint4 ldcg_v4(const void* p) {
   return __ldcg(reinterpret_cast<const uint4*>(p));

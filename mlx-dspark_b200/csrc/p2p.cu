@@ -49,16 +49,6 @@ struct Params {
   int* status;
 };
 
-__device__ __forceinline__ void red_add_release_sys(uint32_t* addr, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
-  return v;
-}
-
 __global__ void __launch_bounds__(kThreads) allgather_kernel(const __grid_constant__ Params p) {
   uint32_t* counts = reinterpret_cast<uint32_t*>(p.arena[p.rank] + p.count_off) + p.buf * 2;
   __shared__ uint32_t round;
@@ -85,18 +75,7 @@ __global__ void __launch_bounds__(kThreads) allgather_kernel(const __grid_consta
   if (blockIdx.x == 0 && threadIdx.x < p.world) {
     const uint32_t* f = reinterpret_cast<const uint32_t*>(p.arena[p.rank] + p.flags_off) +
                         p.buf * kMaxRanks + threadIdx.x;
-    const uint32_t target = (round + 1u) * uint32_t(p.nblk);
-    // wrap-safe comparison of monotonic counters
-    if (int32_t(ld_acquire_sys(f) - target) < 0) {
-      const uint64_t t0 = globaltimer_ns();
-      while (int32_t(ld_acquire_sys(f) - target) < 0) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          report_error(p.status, kErrWaitPeer);
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
+    wait_counter_sys(f, (round + 1u) * uint32_t(p.nblk), p.status, kErrWaitPeer);
   }
   __syncthreads();
   // the last block of this launch advances the round (every block has read it by now)

@@ -786,6 +786,9 @@ int run(const QmmParams& p_in, int epi, const QmmPlan* plan_in, cudaStream_t str
     if (p.x_seg % 8 || p.x_segstride % 8 || p.x_seg <= 0)
       return fail(DSPARK_ERR_UNSUPPORTED, "qmm: x segments must be multiples of 8 elements");
   }
+  if ((p.peer_world > 0 || p.wait_flag != nullptr) && (pl.engine != 2 || pl.tcmma))
+    return fail(DSPARK_ERR_UNSUPPORTED,
+                "qmm: peer stores / gather waits need the streaming engine with mma.sync consumers");
   p.kslice = pl.kslice;
   p.cs = pl.cs;
   p.nslots = pl.nslots;

@@ -56,6 +56,19 @@ struct QmmParams {
   int kv_cap = 0;                    // positions per cache slot (writes at pos >= kv_cap are dropped)
   const int32_t* row_pos = nullptr;  // [M] absolute position of each row
   const int64_t* row_kv = nullptr;   // [M] element offset of the row's cache slot (or null)
+  // peer-store epilogue (RESID / SWIGLU, streaming engine): every output element (and RESID
+  // statistic) also lands at address + peer_delta[s] for each rank s (peer_delta[own] = 0),
+  // and after each tile the writing CTA adds the elements it wrote to *(peer_flag +
+  // peer_delta[s]) (release, system scope). peer_world == 0: off.
+  int peer_world = 0;
+  long peer_delta[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  uint32_t* peer_flag = nullptr;
+  // wait before reading x: until wait_flag[s] (s < wait_world) reaches wait_state[0] +
+  // wait_elems; the launch's last CTA then advances wait_state[0] (wait_state[1]: CTAs done)
+  const uint32_t* wait_flag = nullptr;
+  int wait_world = 0;
+  uint32_t wait_elems = 0;
+  uint32_t* wait_state = nullptr;
 };
 
 struct QmmPlan {

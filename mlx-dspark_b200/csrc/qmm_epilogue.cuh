@@ -11,6 +11,18 @@ namespace qmm {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
 
+// Store v at addr and, in the peer-store instance (PEER), at the same offset in every rank's
+// arena (p.peer_delta[s]; the own rank's delta is 0).
+template <bool PEER, typename T>
+__device__ __forceinline__ void put(const QmmParams& p, T* addr, T v) {
+  if (!PEER || p.peer_world == 0) {
+    *addr = v;
+    return;
+  }
+  for (int s = 0; s < p.peer_world; ++s)
+    *reinterpret_cast<T*>(reinterpret_cast<char*>(addr) + p.peer_delta[s]) = v;
+}
+
 // Rows per warp of the prefetched residual epilogue (the streaming engine: 4 epilogue warps,
 // at most 32 owned rows, so nwarps * kResidRows covers every row).
 constexpr int kResidRows = 8;
@@ -40,7 +52,7 @@ __device__ __forceinline__ void resid_prefetch(const QmmParams& p, int rank, int
 
 // Run by `nwarps` warps starting at warp `warp0` of the CTA. `pre`: the residual words from
 // resid_prefetch for this tile (EPI_RESID, 128-column tiles), or null to load them here.
-template <int EPI, int TN, int PSTR>
+template <int EPI, int TN, int PSTR, bool PEER = false>
 __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, int rank, int cs,
                                          int ntile, int n0, int nwarps, int warp0 = 0,
                                          const uint32_t* pre = nullptr) {
@@ -81,12 +93,12 @@ __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, i
           const uint32_t rr = pre[i * 2 + h];
           const float h0 = round_bf16(round_bf16(red[m * PSTR + n2 * 2]) + bf16_lo(rr));
           const float h1 = round_bf16(round_bf16(red[m * PSTR + n2 * 2 + 1]) + bf16_hi(rr));
-          *reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n) = pack_bf16x2(h0, h1);
+          put<PEER>(p, reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n), pack_bf16x2(h0, h1));
           ss += h0 * h0 + h1 * h1;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0 && p.ssq_out != nullptr) p.ssq_out[ntile * p.ssq_stride + m] = ss;
+        if (lane == 0 && p.ssq_out != nullptr) put<PEER>(p, &p.ssq_out[ntile * p.ssq_stride + m], ss);
       }
       return;
     }
@@ -100,12 +112,12 @@ __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, i
             __ldcg(reinterpret_cast<const unsigned int*>(p.resid + (size_t)m * p.ldr + n));
         const float h0 = round_bf16(round_bf16(red[m * PSTR + n2 * 2]) + bf16_lo(rr));
         const float h1 = round_bf16(round_bf16(red[m * PSTR + n2 * 2 + 1]) + bf16_hi(rr));
-        *reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n) = pack_bf16x2(h0, h1);
+        put<PEER>(p, reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n), pack_bf16x2(h0, h1));
         ss += h0 * h0 + h1 * h1;
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0 && p.ssq_out != nullptr) p.ssq_out[ntile * p.ssq_stride + m] = ss;
+      if (lane == 0 && p.ssq_out != nullptr) put<PEER>(p, &p.ssq_out[ntile * p.ssq_stride + m], ss);
     }
   } else if constexpr (EPI == EPI_SWIGLU) {
     // tile rows: pairs of (32 gate rows, 32 up rows); act column = pair*32 + j
@@ -118,7 +130,7 @@ __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, i
       if (a >= p.n_act) continue;
       const float g = round_bf16(red[m * PSTR + pr * 64 + j]);
       const float u = round_bf16(red[m * PSTR + pr * 64 + 32 + j]);
-      p.out[(size_t)m * p.ldo + a] = __float2bfloat16_rn(silu_mul(g, u));
+      put<PEER>(p, &p.out[(size_t)m * p.ldo + a], __float2bfloat16_rn(silu_mul(g, u)));
     }
   } else if constexpr (EPI == EPI_QKROPE) {
     // tile = TN/128 heads of 128; columns [q heads | k heads | v heads]

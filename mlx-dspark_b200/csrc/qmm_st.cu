@@ -347,7 +347,7 @@ __device__ __forceinline__ void consume_tc(const QmmParams& p, uint8_t* ring, ui
   if (ntl == 0 && cs > 1) cluster_wait();
 }
 
-template <int BITS, int MT, int EPI, bool TC>
+template <int BITS, int MT, int EPI, bool TC, bool PEER = false>
 __global__ void __launch_bounds__(NTHR, 1)
     qmm_st_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                   const __grid_constant__ CUtensorMap bmap, const QmmParams p) {
@@ -460,6 +460,16 @@ __global__ void __launch_bounds__(NTHR, 1)
   } else if (warp < NWC) {
     // ------------------------------------------------------------- consumer warps
     pdl_wait();  // x (and the RMSNorm statistics) come from the previous kernel
+    if constexpr (!TC) {
+      // x gathered by the producing projections' peer stores: wait until every rank's rows
+      // (and statistics) of this round have landed
+      if (PEER && p.wait_flag != nullptr) {
+        if (tid < p.wait_world && ok)
+          ok = wait_counter_sys(&p.wait_flag[tid], __ldcg(&p.wait_state[0]) + p.wait_elems,
+                                p.status, kErrWaitPeer);
+        asm volatile("bar.sync 1, %0;" ::"n"(NC));
+      }
+    }
     const bool nrm = p.norm_w != nullptr;
     const int chunks = p.kslice / 8;
     const int vchunks = kvalid / 8;
@@ -858,14 +868,37 @@ __global__ void __launch_bounds__(NTHR, 1)
         else
           mbar_arrive(&freeb[pbuf]);
       }
-      epilogue<EPI, TN, PSTR>(p, red, rank, cs, t, t * TN, NWE, WARP_EPI,
+      epilogue<EPI, TN, PSTR, PEER>(p, red, rank, cs, t, t * TN, NWE, WARP_EPI,
                               EPI == EPI_RESID ? pre : nullptr);
       asm volatile("bar.sync 2, %0;" ::"n"(NE));  // red reads done
+      if (PEER && p.peer_world > 0 && etid == 0 && nmine > 0) {
+        // this tile's rows sit in every rank's arena: publish how many elements (the
+        // consumers wait for M x columns per source)
+        const int cols = EPI == EPI_SWIGLU ? min(TN / 2, p.n_act - t * (TN / 2)) : min(TN, p.N - t * TN);
+        if (cols > 0) {
+          __threadfence_system();
+          for (int q = 0; q < p.peer_world; ++q)
+            red_add_release_sys(reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(p.peer_flag) +
+                                                            p.peer_delta[q]),
+                                uint32_t(nmine * cols));
+        }
+      }
     }
   }
 
   // no CTA leaves while a peer may still read its partial tiles or arrive on its barriers
   if (cs > 1) cluster_sync_all(); else __syncthreads();
+  // a gather wait: the launch's last CTA advances this rank's cumulative target (every CTA read
+  // it before counting itself here)
+  if (PEER && p.wait_flag != nullptr && tid == 0) {
+    __threadfence();
+    const uint32_t nctas = gridDim.x * gridDim.y;
+    if (atomicAdd(&p.wait_state[1], 1u) == nctas - 1) {
+      p.wait_state[1] = 0;
+      p.wait_state[0] += p.wait_elems;
+      __threadfence();
+    }
+  }
   if constexpr (TC) {
     if (warp == 0) {
       tcg::tc_fence_after();
@@ -929,9 +962,9 @@ int st_max_clusters(int cs, int smem) {
   return n;
 }
 
-template <int BITS, int MT, int EPI, bool TC>
+template <int BITS, int MT, int EPI, bool TC, bool PEER = false>
 static int launch_st(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream) {
-  auto kern = st::qmm_st_kernel<BITS, MT, EPI, TC>;
+  auto kern = st::qmm_st_kernel<BITS, MT, EPI, TC, PEER>;
   const int smem = st_smem_bytes(BITS, MT, pl.kslice, pl.nslots, pl.cs, TC);
   static bool configured = false;
   if (!configured) {
@@ -955,6 +988,11 @@ static int st_dispatch(const QmmParams& p, const QmmPlan& pl, cudaStream_t s) {
     if (p.M <= 8) return launch_st<BITS, 1, EPI, true>(p, pl, s);
     if (p.M <= 16) return launch_st<BITS, 2, EPI, true>(p, pl, s);
     return launch_st<BITS, 4, EPI, true>(p, pl, s);
+  }
+  if (p.peer_world > 0 || p.wait_flag != nullptr) {  // the tensor-parallel instances
+    if (p.M <= 8) return launch_st<BITS, 1, EPI, false, true>(p, pl, s);
+    if (p.M <= 16) return launch_st<BITS, 2, EPI, false, true>(p, pl, s);
+    return launch_st<BITS, 4, EPI, false, true>(p, pl, s);
   }
   if (p.M <= 8) return launch_st<BITS, 1, EPI, false>(p, pl, s);
   if (p.M <= 16) return launch_st<BITS, 2, EPI, false>(p, pl, s);

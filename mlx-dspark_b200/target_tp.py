@@ -13,10 +13,15 @@ columns are split over P ranks (one process per GPU, NCCL over NVLink):
   SwiGLU activations before down, and the vocab-sharded logits at the end. The gathered
   ``[P, M, K/P]`` tensors feed the next projection directly: the QMM reads x as segmented
   rows (``dspark_qmm_fused`` with ``x_seg``), so no transpose copy runs.
-* The gathers run over peer memory by default (``comm="p2p"``): every rank maps every peer's
-  arena through CUDA IPC and one ``dspark_p2p_allgather`` launch stores its segment into all
-  of them and waits, bounded, on the peers' completion counters. ``comm="nccl"`` uses NCCL's
-  all-gather instead (the baseline).
+* ``comm="nccl"`` (the default, the fastest measured at P = 2) all-gathers with NCCL. The two
+  peer-memory transports map every peer's arena through CUDA IPC. ``comm="fused"`` folds three
+  of a layer's four gathers into the projections:
+  O and down store their hidden shard and its statistics, gate/up its activations, straight
+  into segment ``rank`` of every rank's buffer from the epilogue, and count the elements on
+  the peers' completion counters; the next projection waits, bounded, on those counters before
+  it reads x. The attention output and the logits go through ``dspark_p2p_allgather``, one
+  launch that stores a segment into every arena and waits for the peers'. ``comm="p2p"`` uses
+  that launch for every gather.
 
 Every rank holds the full embedding and norm weights and computes the same argmax / accept /
 rollback, so all ranks' cache lengths stay identical. Weights are generated from one seed as
@@ -81,10 +86,10 @@ class TPTarget:
 
     def __init__(self, cfg: Qwen3Config, rank: int, world: int, *, group=None, kv_cap: int = 4096,
                  seed: int = 0, std: float = 0.02, max_rows: int = 32, device="cuda",
-                 comm: str = "p2p"):
+                 comm: str = "nccl"):
         self.cfg, self.rank, self.world, self.group = cfg, int(rank), int(world), group
-        if comm not in ("p2p", "nccl"):
-            raise ValueError(f"comm must be 'p2p' or 'nccl', not {comm!r}")
+        if comm not in ("fused", "p2p", "nccl"):
+            raise ValueError(f"comm must be 'fused', 'p2p' or 'nccl', not {comm!r}")
         self.comm = comm if self.world > 1 else "local"
         self._arena, self._peers = None, []
         self.device = torch.device(device)
@@ -149,7 +154,7 @@ class TPTarget:
         # kernels that read it have run on every rank), one for the logits
         self._segs = {"attn": (R * self.hq * D * 2, 2), "pack": (self.pack, 2),
                       "act": (R * (I // P) * 2, 2), "logits": (R * (V // P) * 2, 1)}
-        seg = self._alloc_gather_buffers() if self.comm == "p2p" else {
+        seg = self._alloc_gather_buffers() if self.comm in ("p2p", "fused") else {
             k: [torch.zeros(P * n, **u8) for _ in range(c)] for k, (n, c) in self._segs.items()}
         self.b = {
             "h0": torch.empty((R, H), **bf),                    # embedding output (replicated)
@@ -229,6 +234,26 @@ class TPTarget:
         _lib.lib.dspark_ipc_free(C.c_void_p(self._arena))
         self._arena = None
 
+    def _own(self, kind: str, i: int) -> int:
+        """Address of this rank's segment of gather destination (kind, i) in its own arena."""
+        _, off, n = self._slots[(kind, i)]
+        return self._arena + off + self.rank * n
+
+    def _peer_args(self, a, kind: str, i: int) -> None:
+        """Peer stores of a projection's output into destination (kind, i) of every arena."""
+        slot = self._slots[(kind, i)][0]
+        a.peer_world = self.world
+        for q in range(self.world):
+            a.peer_delta[q] = self._arena_ptrs[q] - self._arena
+        a.peer_flag = self._arena + self._FLAGS_OFF + (slot * 8 + self.rank) * 4
+
+    def _wait_args(self, a, kind: str, i: int, elems: int) -> None:
+        """Wait, before x is read, for every rank's ``elems`` elements of destination (kind, i)."""
+        slot = self._slots[(kind, i)][0]
+        a.wait_flag = self._arena + self._FLAGS_OFF + slot * 8 * 4
+        a.wait_world, a.wait_elems = self.world, elems
+        a.wait_state = self._arena + self._COUNT_OFF + slot * 2 * 4
+
     def _gather(self, kind: str, i: int, inp: torch.Tensor) -> None:
         """All-gather this rank's ``inp`` into segment ``rank`` of destination ``(kind, i)``."""
         out = {"attn": self.b["attn_seg"], "pack": self.b["pack_seg"],
@@ -236,6 +261,8 @@ class TPTarget:
         out = self.b["logits_seg"] if kind == "logits" else out[i]
         if self.comm == "local":
             out.view(-1).copy_(inp.view(-1).view(out.dtype))
+        elif self.comm == "fused" and kind in ("pack", "act"):
+            return  # the producing projection stored into every rank's buffer itself
         elif self.comm == "nccl":
             import torch.distributed as dist
 
@@ -249,8 +276,12 @@ class TPTarget:
 
     def _qmm(self, s, w: quant.QWeight, x, ldx, M, K, epi, out=None, ldo=0, *, x_seg=0,
              x_seg_stride=0, norm_w=None, ssq_in=None, ssq_n=0, ssq_seg=0, ssq_seg_stride=0,
-             resid=None, ldr=0, ssq_out=None, n_act=0, layer=None):
+             resid=None, ldr=0, ssq_out=None, n_act=0, layer=None, peer=None, wait=None):
         a = _lib.QmmArgs()
+        if peer is not None:
+            self._peer_args(a, *peer)
+        if wait is not None:
+            self._wait_args(a, *wait)
         a.x = x if isinstance(x, int) else ptr(x)
         a.ldx, a.x_seg, a.x_seg_stride = ldx, x_seg, x_seg_stride
         a.M, a.K, a.N, a.bits = M, K, int(w.wq.shape[0]), w.bits
@@ -302,13 +333,15 @@ class TPTarget:
         ssq, ssq_n, sseg, ssegs = b["ssq0"].data_ptr(), 1, 0, 0
         resid, ldr = b["h0"][:, r * hs:].data_ptr(), H
         cur = 0
+        fz = self.comm == "fused"
+        xwait = None  # the gathered hidden state x is waited on (fused gathers, after layer 0)
         q_st = _lib.i64_array([0, D, self.hq * D])
         k_st = _lib.i64_array([0, self.kv_cap * D, D])
         for li, L in enumerate(self.layers):
             j = li & 1  # alternating gather destinations
             self._qmm(s, L["qkv"], x, ldx, R, H, _lib.EPI_QKROPE, x_seg=xseg, x_seg_stride=xss,
                       norm_w=L["in_norm"], ssq_in=ssq, ssq_n=ssq_n, ssq_seg=sseg,
-                      ssq_seg_stride=ssegs, layer=L)
+                      ssq_seg_stride=ssegs, layer=L, wait=xwait)
             _lib.check(_lib.lib.dspark_verify_attn(
                 ptr(b["xq"]), q_st, ptr(L["k_cache"]), k_st, ptr(L["v_cache"]), k_st, 1, self.hq,
                 self.hk, R, D, Lm, ptr(b["kv_len"]), float(D ** -0.5), 1, None, ptr(b["attn"]),
@@ -316,21 +349,28 @@ class TPTarget:
             self._gather("attn", j, b["attn"])
             # O: x = all heads' attention ([P, R, hq*D] segments), residual = own hidden shard;
             # the new shard and its statistics land in this rank's pack
-            self._qmm(s, L["o"], b["attn_seg"][j], self.hq * D, R, Hq * D, _lib.EPI_RESID, loc, hs,
-                      x_seg=self.hq * D, x_seg_stride=self.max_rows * self.hq * D,
-                      resid=resid, ldr=ldr, ssq_out=loc + hb)
+            o_out = self._own("pack", cur) if fz else loc
+            self._qmm(s, L["o"], b["attn_seg"][j], self.hq * D, R, Hq * D, _lib.EPI_RESID, o_out,
+                      hs, x_seg=self.hq * D, x_seg_stride=self.max_rows * self.hq * D,
+                      resid=resid, ldr=ldr, ssq_out=o_out + hb,
+                      peer=("pack", cur) if fz else None)
             mid = b["pack_seg"][cur]
             self._gather("pack", cur, b["pack"])
             mb = mid.data_ptr()
             # gate/up: post-attention norm over the gathered hidden state, SwiGLU shard
-            self._qmm(s, L["gate_up"], mb, hs, R, H, _lib.EPI_SWIGLU, b["act"], I // P,
+            self._qmm(s, L["gate_up"], mb, hs, R, H, _lib.EPI_SWIGLU,
+                      self._own("act", j) if fz else b["act"], I // P,
                       x_seg=hs, x_seg_stride=pk // 2, norm_w=L["post_norm"], ssq_in=mb + hb,
-                      ssq_n=P * T, ssq_seg=T, ssq_seg_stride=pk // 4, n_act=I // P)
+                      ssq_n=P * T, ssq_seg=T, ssq_seg_stride=pk // 4, n_act=I // P,
+                      peer=("act", j) if fz else None,
+                      wait=("pack", cur, R * hs) if fz else None)
             self._gather("act", j, b["act"])
             # down: x = all activations, residual = own shard of the mid state
-            self._qmm(s, L["down"], b["act_seg"][j], I // P, R, I, _lib.EPI_RESID, loc, hs,
+            d_out = self._own("pack", cur ^ 1) if fz else loc
+            self._qmm(s, L["down"], b["act_seg"][j], I // P, R, I, _lib.EPI_RESID, d_out, hs,
                       x_seg=I // P, x_seg_stride=self.max_rows * (I // P), resid=mb + r * pk,
-                      ldr=hs, ssq_out=loc + hb)
+                      ldr=hs, ssq_out=d_out + hb, peer=("pack", cur ^ 1) if fz else None,
+                      wait=("act", j, R * (I // P)) if fz else None)
             cur ^= 1
             nxt = b["pack_seg"][cur]
             self._gather("pack", cur, b["pack"])
@@ -338,10 +378,11 @@ class TPTarget:
             x, ldx, xseg, xss = nb, hs, hs, pk // 2
             ssq, ssq_n, sseg, ssegs = nb + hb, P * T, T, pk // 4
             resid, ldr = nb + r * pk, hs
+            xwait = ("pack", cur, R * hs) if fz else None
         # final norm + vocab-sharded lm_head, logits gathered
         self._qmm(s, self.lm_head, x, ldx, R, H, _lib.EPI_PLAIN, b["logits"], V // P, x_seg=xseg,
                   x_seg_stride=xss, norm_w=self.final_norm, ssq_in=ssq, ssq_n=ssq_n,
-                  ssq_seg=sseg, ssq_seg_stride=ssegs)
+                  ssq_seg=sseg, ssq_seg_stride=ssegs, wait=xwait)
         self._gather("logits", 0, b["logits"])
         b["logits_full"][:R].view(R, P, V // P).copy_(b["logits_seg"][:, :R].transpose(0, 1))
         return b["logits_full"][:R]

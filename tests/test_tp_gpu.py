@@ -3,7 +3,8 @@
 * P = 1 against the oracle's Qwen3 forward (bars as in test_forward_gpu.py): exercises the fused
   QMM entry point, segmented x rows and the gather-based layer sequence on one GPU;
 * P = 2 against P = 1 on the same seeded model and cache (two GPUs, skipped with fewer), with
-  the gathers over peer memory and over NCCL: logits within the bf16 noise of the single-rank
+  the gathers fused into the projections' peer stores, over peer memory by separate launches,
+  and over NCCL: logits within the bf16 noise of the single-rank
   forward for two blocks in a row, identical on both ranks, identical cache lengths.
 """
 
@@ -112,7 +113,7 @@ def _tp_worker(rank, world, port, q, comm):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("comm", ["p2p", "nccl"])
+@pytest.mark.parametrize("comm", ["fused", "p2p", "nccl"])
 def test_tp2_matches_tp1(cuda, comm):
     import torch.multiprocessing as mp
 
