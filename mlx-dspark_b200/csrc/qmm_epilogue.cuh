@@ -12,7 +12,8 @@ namespace qmm {
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
 
 // Store v at addr and, in the peer-store instance (PEER), at the same offset in every rank's
-// arena (p.peer_delta[s]; the own rank's delta is 0).
+// arena (p.peer_delta[s]; the own rank's delta is 0). Used for the scattered statistics words;
+// the output rows reach the peers as 16-byte copies after the tile (qmm_st.cu).
 template <bool PEER, typename T>
 __device__ __forceinline__ void put(const QmmParams& p, T* addr, T v) {
   if (!PEER || p.peer_world == 0) {
@@ -93,7 +94,7 @@ __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, i
           const uint32_t rr = pre[i * 2 + h];
           const float h0 = round_bf16(round_bf16(red[m * PSTR + n2 * 2]) + bf16_lo(rr));
           const float h1 = round_bf16(round_bf16(red[m * PSTR + n2 * 2 + 1]) + bf16_hi(rr));
-          put<PEER>(p, reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n), pack_bf16x2(h0, h1));
+          *reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n) = pack_bf16x2(h0, h1);
           ss += h0 * h0 + h1 * h1;
         }
 #pragma unroll
@@ -112,7 +113,7 @@ __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, i
             __ldcg(reinterpret_cast<const unsigned int*>(p.resid + (size_t)m * p.ldr + n));
         const float h0 = round_bf16(round_bf16(red[m * PSTR + n2 * 2]) + bf16_lo(rr));
         const float h1 = round_bf16(round_bf16(red[m * PSTR + n2 * 2 + 1]) + bf16_hi(rr));
-        put<PEER>(p, reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n), pack_bf16x2(h0, h1));
+        *reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + n) = pack_bf16x2(h0, h1);
         ss += h0 * h0 + h1 * h1;
       }
 #pragma unroll
@@ -130,7 +131,7 @@ __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, i
       if (a >= p.n_act) continue;
       const float g = round_bf16(red[m * PSTR + pr * 64 + j]);
       const float u = round_bf16(red[m * PSTR + pr * 64 + 32 + j]);
-      put<PEER>(p, &p.out[(size_t)m * p.ldo + a], __float2bfloat16_rn(silu_mul(g, u)));
+      p.out[(size_t)m * p.ldo + a] = __float2bfloat16_rn(silu_mul(g, u));
     }
   } else if constexpr (EPI == EPI_QKROPE) {
     // tile = TN/128 heads of 128; columns [q heads | k heads | v heads]

@@ -871,16 +871,30 @@ __global__ void __launch_bounds__(NTHR, 1)
       epilogue<EPI, TN, PSTR, PEER>(p, red, rank, cs, t, t * TN, NWE, WARP_EPI,
                               EPI == EPI_RESID ? pre : nullptr);
       asm volatile("bar.sync 2, %0;" ::"n"(NE));  // red reads done
-      if (PEER && p.peer_world > 0 && etid == 0 && nmine > 0) {
-        // this tile's rows sit in every rank's arena: publish how many elements (the
-        // consumers wait for M x columns per source)
-        const int cols = EPI == EPI_SWIGLU ? min(TN / 2, p.n_act - t * (TN / 2)) : min(TN, p.N - t * TN);
+      if (PEER && p.peer_world > 0 && nmine > 0) {
+        // this tile's rows, written locally by the epilogue, go to every peer's arena as
+        // 16-byte copies (rows of 64-128 bf16, 16-byte aligned), then the elements are counted
+        // on the peers' counters (the consumers wait for M x columns per source)
+        const int col0 = EPI == EPI_SWIGLU ? t * (TN / 2) : t * TN;
+        const int cols = EPI == EPI_SWIGLU ? min(TN / 2, p.n_act - col0) : min(TN, p.N - col0);
         if (cols > 0) {
-          __threadfence_system();
-          for (int q = 0; q < p.peer_world; ++q)
-            red_add_release_sys(reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(p.peer_flag) +
-                                                            p.peer_delta[q]),
-                                uint32_t(nmine * cols));
+          const int c16 = cols / 8;  // 16-byte chunks per row
+          for (int idx = etid; idx < nmine * c16; idx += NE) {
+            const int mi = idx / c16, c = idx - mi * c16;
+            const char* src = reinterpret_cast<const char*>(p.out + (size_t)(rank + mi * cs) * p.ldo + col0) + c * 16;
+            const uint4 v = *reinterpret_cast<const uint4*>(src);
+            for (int q = 0; q < p.peer_world; ++q)
+              if (p.peer_delta[q] != 0)
+                *reinterpret_cast<uint4*>(const_cast<char*>(src) + p.peer_delta[q]) = v;
+          }
+          asm volatile("bar.sync 2, %0;" ::"n"(NE));  // every copy precedes the release
+          if (etid == 0) {
+            __threadfence_system();
+            for (int q = 0; q < p.peer_world; ++q)
+              red_add_release_sys(reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(p.peer_flag) +
+                                                              p.peer_delta[q]),
+                                  uint32_t(nmine * cols));
+          }
         }
       }
     }
