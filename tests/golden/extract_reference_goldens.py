@@ -7,7 +7,7 @@ operation sequences are transcribed below; every expected value is taken from th
 source's own literals, in the order they appear, so a change in the reference's goldens
 changes the fixture.
 
-Usage: python tests/golden/extract_reference_goldens.py [path/to/reference/tests]
+Usage: python tests/golden/extract_reference_goldens.py path/to/mlx-dspark/tests
 """
 
 from __future__ import annotations
@@ -105,7 +105,9 @@ def main(ref_tests: Path) -> dict:
 
 
 if __name__ == "__main__":
-    ref = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference/tests")
+    if len(sys.argv) != 2:
+        sys.exit("usage: extract_reference_goldens.py path/to/mlx-dspark/tests")
+    ref = Path(sys.argv[1])
     data = main(ref)
     (HERE / "reference_goldens.json").write_text(json.dumps(data, indent=1) + "\n")
     print(f"wrote {HERE / 'reference_goldens.json'}")
