@@ -633,6 +633,7 @@ QmmPlan plan_st(int N, int K, int bits, int rt) {
     if (force_cs && cs != force_cs) continue;
     const int kslice = ((K + cs - 1) / cs + 511) / 512 * 512;
     if ((cs - 1) * kslice >= K) continue;
+    if (kslice > 8192) continue;  // x is staged in at most 16 blocks of 512 k
     int slots = max_slots;
     while (slots >= 3 && st_smem_bytes(bits, mt, kslice, slots, cs, pl.tcmma) > 227 * 1024) --slots;
     if (slots < 3) continue;

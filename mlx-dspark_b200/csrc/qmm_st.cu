@@ -22,11 +22,12 @@
 //    A fragments (the weights are the 16-row A operand, x the 8-column B operand, so every
 //    weight is read once whatever M is), and folds the group's exact product P into fp32
 //    accumulators: acc += scale*P + (bias - MAGIC*scale) * sum_k x (packed f32x2 FMAs).
-//  * x (the CTA's K slice, <= 32 rows) is staged once per launch by the consumer threads
-//    themselves (16-byte global loads, 8 in flight per thread, normed, k permuted inside each
-//    8-block (4-bit) or 4-block (8-bit) exactly as the magic extraction orders the weights, and
-//    summed per group in the same pass), so one 16-byte load gives the B fragments of two k16
-//    steps and the copy engine stays free for the weight stream.
+//  * x (the CTA's K slice, <= 32 rows) is staged once per launch by the epilogue warps, which
+//    are idle until the first tile ends: 512 k at a time (16-byte global loads, 8 in flight per
+//    thread), normed, k permuted inside each 8-block (4-bit) or 4-block (8-bit) exactly as the
+//    magic extraction orders the weights, and summed per group, each block released on its own
+//    mbarrier. The first tile's consumers wait per block, so staging overlaps their compute;
+//    one 16-byte load gives the B fragments of two k16 steps.
 //  * Four epilogue warps finish each tile while the consumers stream the next one. At a tile's
 //    end every consumer warp pushes its k half of the partial tile to the rows' owners (row m
 //    belongs to cluster rank m % cs) and goes straight on: st.async into a peer's receive
@@ -65,6 +66,7 @@ constexpr int SCB = TN * 16;            // 8 groups of bf16 scales (or biases) f
 constexpr int KBLK = 512;               // k per scale block (8 groups)
 constexpr int kTcBuf = 4;               // tcgen05 A/D buffer pairs per warpgroup, at most
 constexpr int kTcBars = 2 * kTcBuf;     // their completion barriers, two warpgroups
+constexpr int kXBlocks = 16;            // x staging blocks of 512 k per K slice (kslice <= 8192)
 
 template <int BITS>
 struct Tr;
@@ -128,7 +130,7 @@ __host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslot
   off += 32 * 4;
   off = (off + 15) & ~15;
   L.bars = off;
-  off += (2 * nslots + 4 + kTcBars) * 8 + 16;  // + tcgen05 completion barriers, TMEM slot
+  off += (2 * nslots + 4 + kXBlocks + kTcBars) * 8 + 16;  // + x blocks, tcgen05, TMEM slot
   L.total = off + 1024;  // slack to align the dynamic base to 1024 bytes
   return L;
 }
@@ -347,6 +349,102 @@ __device__ __forceinline__ void consume_tc(const QmmParams& p, uint8_t* ring, ui
   if (ntl == 0 && cs > 1) cluster_wait();
 }
 
+// rs[m] = rsqrt(mean of x_m^2 + eps) for rows m = m0, m0 + mstep, ... from the sums of squares
+// the previous projection's epilogue left per tile (segmented when gathered from several ranks).
+// Entry e = lane + 32i lives in segment e / ssq_seg: advanced by subtraction, so no division
+// sits between the loads. One warp per row.
+__device__ __forceinline__ void norm_stats(const QmmParams& p, float* rsm, int rp, int m0,
+                                           int mstep, int lane) {
+  for (int m = m0; m < rp; m += mstep) {
+    float ss = 0.f;
+    if (m < p.M) {
+      const int sg = p.ssq_seg;
+      int sseg = 0, soff = lane;
+      if (sg) {
+        sseg = lane / sg;
+        soff = lane - sseg * sg;
+      }
+      for (int e = lane; e < p.ssq_n; e += 32) {
+        const long at = sg ? sseg * p.ssq_segstride + long(soff) * p.ssq_stride
+                           : long(e) * p.ssq_stride;
+        ss += __ldcg(&p.ssq_in[at + m]);
+        soff += 32;
+        if (sg)
+          while (soff >= sg) {
+            soff -= sg;
+            ++sseg;
+          }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) rsm[m] = m < p.M ? rsqrtf(ss / float(p.K) + p.eps) : 0.f;
+  }
+}
+
+// Stage k block kb (512 k: chunks c = 64kb .. 64kb + 63 of the K slice) of every row of x into
+// shared memory (rows of XP bytes), by 128 threads: thread t takes chunk column 64kb + t % 64 and
+// rows t / 64, t / 64 + 2, ..., U loads in flight at once (16-byte global loads). Each chunk is
+// normed (x * rs * w rounded to bf16), permuted inside each 8-block (4-bit: 0,4,1,5,2,6,3,7) or
+// 4-block (8-bit: 0,2,1,3) as the magic extraction orders the weights, and summed per group of
+// 64 into sx: a group's 8 chunks sit on 8 consecutive lanes and reduce by shuffles in a fixed
+// order. The block's one division (the segment of k) comes before its loads are issued.
+template <int BITS, int RP, int U>
+__device__ __forceinline__ void stage_block(const QmmParams& p, uint8_t* xs, int XP, float* sx,
+                                            const float* rsm, bool nrm, int kbase, int kb, int t) {
+  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+  const int c = kb * 64 + (t & 63);
+  const int k = kbase + c * 8;
+  const int xseg = int(p.x_seg);
+  int seg = 0, off = k;
+  if (xseg) {
+    seg = off / xseg;
+    off -= seg * xseg;
+  }
+  const bf16* col = p.x + long(seg) * p.x_segstride + off;
+  const uint4 w = nrm ? ldg_v4(p.norm_w + k) : z4;
+  const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w);
+  for (int m0 = t >> 6; m0 < p.M; m0 += 2 * U) {  // the row parity is uniform in a warp
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      v[u] = m0 + 2 * u < p.M ? ldcg_v4(col + (size_t)(m0 + 2 * u) * p.ldx) : z4;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int m = m0 + 2 * u;
+      if (m >= p.M) break;  // uniform in a warp
+      uint4 vv = v[u];
+      uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
+      if (nrm) {
+        const float r = rsm[m];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
+                              bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
+      }
+      float part = (bf16_lo(vv.x) + bf16_hi(vv.x)) + (bf16_lo(vv.y) + bf16_hi(vv.y)) +
+                   (bf16_lo(vv.z) + bf16_hi(vv.z)) + (bf16_lo(vv.w) + bf16_hi(vv.w));
+      uint4 o;
+      if (BITS == 4) {
+        o.x = __byte_perm(vv.x, vv.z, 0x5410);
+        o.y = __byte_perm(vv.x, vv.z, 0x7632);
+        o.z = __byte_perm(vv.y, vv.w, 0x5410);
+        o.w = __byte_perm(vv.y, vv.w, 0x7632);
+      } else {
+        o.x = __byte_perm(vv.x, vv.y, 0x5410);
+        o.y = __byte_perm(vv.x, vv.y, 0x7632);
+        o.z = __byte_perm(vv.z, vv.w, 0x5410);
+        o.w = __byte_perm(vv.z, vv.w, 0x7632);
+      }
+      *reinterpret_cast<uint4*>(xs + m * XP + c * 16) = o;
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      part += __shfl_xor_sync(0xffffffffu, part, 4);
+      if ((c & 7) == 0) sx[(c >> 3) * RP + m] = part;
+    }
+  }
+}
+
 template <int BITS, int MT, int EPI, bool TC, bool PEER = false>
 __global__ void __launch_bounds__(NTHR, 1)
     qmm_st_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
@@ -374,7 +472,8 @@ __global__ void __launch_bounds__(NTHR, 1)
   uint64_t* empty = full + S;
   uint64_t* ready = empty + S;   // [2] every local warp and every peer's bytes of a partial tile
   uint64_t* freeb = ready + 2;   // [2] every cluster CTA finished reading this CTA's partial
-  uint64_t* tcbar = freeb + 2;   // [2 warpgroups][kTcBuf buffers] tcgen05 MMA completion
+  uint64_t* xrdy = freeb + 2;    // [kXBlocks] k block b of the x slice is staged
+  uint64_t* tcbar = xrdy + kXBlocks;  // [2 warpgroups][kTcBuf buffers] tcgen05 MMA completion
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tcbar + kTcBars);
   uint8_t* nws = smem + Lo.nw;
 
@@ -406,6 +505,7 @@ __global__ void __launch_bounds__(NTHR, 1)
       mbar_init(&ready[i], 1 + NWC);
       mbar_init(&freeb[i], cs);
     }
+    for (int i = 0; i < kXBlocks; ++i) mbar_init(&xrdy[i], 1);
     for (int i = 0; i < kTcBars; ++i) mbar_init(&tcbar[i], 1);
     fence_mbar_init();
   }
@@ -459,17 +559,6 @@ __global__ void __launch_bounds__(NTHR, 1)
     if (cs > 1) cluster_wait();
   } else if (warp < NWC) {
     // ------------------------------------------------------------- consumer warps
-    pdl_wait();  // x (and the RMSNorm statistics) come from the previous kernel
-    if constexpr (!TC) {
-      // x gathered by the producing projections' peer stores: wait until every rank's rows
-      // (and statistics) of this round have landed
-      if (PEER && p.wait_flag != nullptr) {
-        if (tid < p.wait_world && ok)
-          ok = wait_counter_sys(&p.wait_flag[tid], __ldcg(&p.wait_state[0]) + p.wait_elems,
-                                p.status, kErrWaitPeer);
-        asm volatile("bar.sync 1, %0;" ::"n"(NC));
-      }
-    }
     const bool nrm = p.norm_w != nullptr;
     const int chunks = p.kslice / 8;
     const int vchunks = kvalid / 8;
@@ -484,35 +573,6 @@ __global__ void __launch_bounds__(NTHR, 1)
     for (int idx = tid; idx < (RP - p.M) * (kvalid / 64); idx += NC) {
       const int g = idx / (RP - p.M), m = p.M + idx % (RP - p.M);
       sx[g * RP + m] = 0.f;
-    }
-    if (nrm) {
-      for (int m = warp; m < RP; m += NWC) {
-        float ss = 0.f;
-        if (m < p.M) {
-          // entry e = lane + 32i lives in segment e / ssq_seg: advanced by subtraction, so no
-          // division sits between the loads
-          const int sg = p.ssq_seg;
-          int sseg = 0, soff = lane;
-          if (sg) {
-            sseg = lane / sg;
-            soff = lane - sseg * sg;
-          }
-          for (int e = lane; e < p.ssq_n; e += 32) {
-            const long at = sg ? sseg * p.ssq_segstride + long(soff) * p.ssq_stride
-                               : long(e) * p.ssq_stride;
-            ss += __ldcg(&p.ssq_in[at + m]);
-            soff += 32;
-            if (sg)
-              while (soff >= sg) {
-                soff -= sg;
-                ++sseg;
-              }
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) rsm[m] = m < p.M ? rsqrtf(ss / float(p.K) + p.eps) : 0.f;
-      }
     }
     // one 8-k chunk (row m, chunk c): apply the norm (x * rs * w rounded to bf16), permute k
     // inside each 8-block (4-bit: 0,4,1,5,2,6,3,7) or 4-block (8-bit: 0,2,1,3) as the magic
@@ -553,46 +613,10 @@ __global__ void __launch_bounds__(NTHR, 1)
       if (live && (c & 7) == 0) sx[(c >> 3) * RP + m] = part;
     };
     if constexpr (!TC) {
-      // x straight from global memory, staged in one pass: no copy engine in the way of the
-      // weight stream, no second pass over shared memory. Thread t takes chunk column
-      // c = cb + t of U rows at a time, all U 16-byte loads in flight together. No division sits
-      // between the loads (a division's reciprocal shares the memory instruction queue and
-      // would wait behind them): the segment of k advances by subtraction, the rows by a loop.
-      if (nrm) asm volatile("bar.sync 1, %0;" ::"n"(NC));  // rs of every row
-      constexpr int U = MT == 4 ? 4 : 8;  // rows in flight per thread (register budget)
-      const int xseg = int(p.x_seg);
-      int seg = 0, off = kbase + tid * 8;  // segment and offset of k = kbase + 8c
-      if (xseg) {
-        seg = off / xseg;
-        off -= seg * xseg;
-      }
-      for (int cb = 0; cb < vchunks; cb += NC) {
-        const int c = cb + tid;
-        const bool cv = c < vchunks;
-        const bf16* col = p.x + long(seg) * p.x_segstride + off;
-        const uint4 w = (nrm && cv) ? ldg_v4(p.norm_w + kbase + c * 8) : make_uint4(0u, 0u, 0u, 0u);
-        for (int m0 = 0; m0 < p.M; m0 += U) {
-          uint4 v[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u)
-            v[u] = (cv && m0 + u < p.M) ? ldcg_v4(col + (size_t)(m0 + u) * p.ldx)
-                                        : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int m = m0 + u;
-            const bool live = cv && m < p.M;
-            const float part = live ? stage_chunk(v[u], w, m, c) : 0.f;
-            if (m < p.M) group_sum(part, live, m, c);  // warp-uniform condition
-          }
-        }
-        off += NC * 8;
-        if (xseg)
-          while (off >= xseg) {
-            off -= xseg;
-            ++seg;
-          }
-      }
+      // the epilogue warps stage x block by block (xrdy); the first tile waits for each block
     } else {
+      pdl_wait();  // x (and the RMSNorm statistics) come from the previous kernel
+      if (nrm) norm_stats(p, rsm, RP, warp, NWC, lane);
       // 16-byte copies straight into the canonical places, all in flight at once, then the
       // same norm / permute / group-sum pass in place
       const uint32_t xa0 = smem_u32(xs);
@@ -661,6 +685,8 @@ __global__ void __launch_bounds__(NTHR, 1)
           for (int i = 0; i < 4; ++i) acc[rg][mt][i] = 0.f;
 
       for (int sb = 0; sb < nsb; ++sb) {
+        // the first tile waits until the epilogue warps staged this k block of x
+        if (j == 0 && ok) ok = mbar_wait(&xrdy[sb], 0, p.status, kErrWaitFull);
         const uint32_t sblk_a = sring_a + uint32_t(sslot * 2 * SCB);
         if (++sslot == SS) sslot = 0;
 #pragma unroll
@@ -824,8 +850,28 @@ __global__ void __launch_bounds__(NTHR, 1)
     }  // mma.sync consumers
   } else {
     // ------------------------------------------------------------- epilogue warps
-    pdl_wait();  // the epilogues read / write buffers of earlier kernels (residual, caches)
+    pdl_wait();  // x, the statistics and the epilogues' buffers come from earlier kernels
     const int etid = tid - WARP_EPI * 32;
+    if constexpr (!TC) {
+      // idle until the first tile ends: stage x for the consumers, 512 k at a time, releasing
+      // each block as it lands so that the first tile's compute overlaps the rest
+      if (PEER && p.wait_flag != nullptr) {  // x gathered by the producers' peer stores
+        if (etid < p.wait_world && ok)
+          ok = wait_counter_sys(&p.wait_flag[etid], __ldcg(&p.wait_state[0]) + p.wait_elems,
+                                p.status, kErrWaitPeer);
+        asm volatile("bar.sync 2, %0;" ::"n"(NE));
+      }
+      const bool nrm = p.norm_w != nullptr;
+      if (nrm) {
+        norm_stats(p, rsm, RP, warp - WARP_EPI, NWE, lane);
+        asm volatile("bar.sync 2, %0;" ::"n"(NE));  // rs of every row
+      }
+      for (int kb = 0; kb < kvalid / KBLK; ++kb) {
+        stage_block<BITS, RP, MT == 4 ? 4 : 8>(p, xs, XP, sx, rsm, nrm, kbase, kb, etid);
+        asm volatile("bar.sync 2, %0;" ::"n"(NE));  // the block's chunks and sums are stored
+        if (etid == 0) mbar_arrive(&xrdy[kb]);
+      }
+    }
     if (cs > 1) cluster_wait();  // peers' barriers exist before the first remote arrive
     const int ro = owned_rows(RP, cs);
     const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
@@ -1017,6 +1063,9 @@ int run_st(const QmmParams& p, int epi, const QmmPlan& pl, cudaStream_t s) {
   if (!pl.sct || p.K % st::KBLK)
     return fail(DSPARK_ERR_UNSUPPORTED, "qmm_st: needs K %% 512 == 0 and 16-byte aligned scales");
   if (pl.kslice % st::KBLK) return fail(DSPARK_ERR_ARG, "qmm_st: k slice %d", pl.kslice);
+  if (pl.kslice / st::KBLK > st::kXBlocks)
+    return fail(DSPARK_ERR_UNSUPPORTED, "qmm_st: k slice %d (at most %d)", pl.kslice,
+                st::kXBlocks * st::KBLK);
   if (p.bits == 4) {
     switch (epi) {
       case EPI_PLAIN: return st_dispatch<4, EPI_PLAIN>(p, pl, s);
