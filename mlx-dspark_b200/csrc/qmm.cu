@@ -29,6 +29,7 @@
 //    for the next RMSNorm), SwiGLU on interleaved gate/up rows, and Qwen3 q/k RMSNorm + RoPE
 //    + KV-cache write. The prologue can apply RMSNorm to x while staging it.
 #include <algorithm>
+#include <cstdio>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -609,9 +610,13 @@ QmmPlan plan(int N, int K, int bits, int epi, int min_tn, int rt) {
 
 // Streaming engine: choose the split-K factor cs (= cluster size), the ring depth and the
 // number of persistent clusters. Modelled as: every cluster walks ceil(tiles / clusters) tiles,
-// each CTA streaming 128 rows x K/cs of weights (+ scales/biases) at the smaller of a per-SM
-// streaming cap and its share of HBM bandwidth, plus a per-tile cost and a once-per-launch
-// start (x staging, first TMA bytes).
+// each CTA streaming 128 rows x K/cs of weights (+ scales/biases) at the smaller of a per-CTA
+// consumer rate and its share of HBM bandwidth, plus a per-tile cost (split-K exchange,
+// epilogue) and the x staging of its K slice, which grows with the rows staged.
+// The terms are a least-squares fit to B200 sweeps of every split over the Qwen3-8B
+// projections (4-bit, 1 and 16 rows): per streamed KB 0.015 + 0.013 * mt us (mt = 8-row
+// column tiles), 0.5 us per tile, 0.29 * mt us per 1024 k staged. The fit picks the fastest
+// measured split for all four shapes at 16 rows. DSPARK_QMM_PLAN_LOG=1 prints every candidate.
 QmmPlan plan_st(int N, int K, int bits, int rt) {
   QmmPlan pl;
   pl.engine = 2;
@@ -624,9 +629,13 @@ QmmPlan plan_st(int N, int K, int bits, int rt) {
   const int force_clusters = env_int("DSPARK_QMM_CLUSTERS", 0);
   pl.tcmma = env_int("DSPARK_QMM_ST_TC", 0) != 0;  // tcgen05 consumers measured slower
   const double hbm = env_int("DSPARK_QMM_HBM_GBS", 6500) * 1e9;
-  const double sm_cap = env_int("DSPARK_QMM_SM_MBS", bits == 8 ? 60000 : 40000) * 1e6;
-  const double t_tile = env_int("DSPARK_QMM_TILE_NS", 300) * 1e-9;
   const int mt = rt <= 1 ? 1 : rt <= 2 ? 2 : 4;
+  // bytes/s one CTA's consumers take in; 8-bit weights carry half the MACs per byte
+  const double cta_rate = 1e3 / ((0.015 + 0.013 * mt) * 1e-6) * (bits == 8 ? 1.5 : 1.0);
+  const int sm_mbs = env_int("DSPARK_QMM_SM_MBS", 0);
+  const double sm_cap = sm_mbs > 0 ? sm_mbs * 1e6 : cta_rate;
+  const double t_tile = env_int("DSPARK_QMM_TILE_NS", 500) * 1e-9;
+  const bool log = env_int("DSPARK_QMM_PLAN_LOG", 0) != 0;
   const int ntiles = (N + 127) / 128;
   double best = 1e30;
   for (int cs : {1, 2, 3, 4, 5, 6, 8, 10, 12, 16}) {
@@ -644,8 +653,13 @@ QmmPlan plan_st(int N, int K, int bits, int rt) {
     const int waves = (ntiles + clusters - 1) / clusters;
     const double tile_bytes = 128.0 * kslice * (bits / 8.0 + 4.0 / 64.0);
     const double rate = std::min(sm_cap, hbm / (clusters * cs));
-    double t = waves * (tile_bytes / rate + t_tile) + 1.5e-6 + kslice * 2.0 * 8 * mt / 2e11;
+    double t = waves * (tile_bytes / rate + t_tile) + 1.5e-6 + 0.29e-6 * mt * kslice / 1024.0;
     if (cs & (cs - 1)) t *= 1.03;  // odd cluster shapes pack less evenly into GPCs
+    if (log)
+      std::fprintf(stderr,
+                   "plan_st N=%d K=%d bits=%d rt=%d cs=%d kslice=%d slots=%d clusters=%d waves=%d "
+                   "model_us=%.3f\n",
+                   N, K, bits, rt, cs, kslice, slots, clusters, waves, t * 1e6);
     if (t < best) {
       best = t;
       pl.nw = 8;  // 128-row tile
