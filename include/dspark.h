@@ -351,7 +351,8 @@ int dspark_verify_prepare(int32_t* len, int R, const dspark_fwd_buffers* buf, vo
 /* ---- all-gather over peer memory (tensor-parallel verify) ------------------------------
  * Replaces the NCCL all-gathers between the column-sharded projections (the collective the
  * reference's verify path does not have: it runs 27B targets on one Apple GPU, target.py:208-221;
- * the fused peer-store variant is the survey's multi-GPU plan). Set-up, once per rank:
+ * the fused peer-store variant stores a projection's finished rows straight into the peers'
+ * arenas from its epilogue). Set-up, once per rank:
  * dspark_ipc_alloc an arena (zero-filled device memory and its IPC handle), share the handles
  * between the ranks' processes, dspark_ipc_open every peer's handle. The arena layout is the
  * caller's, identical on every rank: a flag area (uint32 [8 buffers][8 ranks]), a counter area
