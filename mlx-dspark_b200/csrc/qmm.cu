@@ -599,6 +599,11 @@ QmmPlan plan(int N, int K, int bits, int epi, int min_tn, int rt) {
   QmmPlan pl;
   pl.nw = 0;
   if (impl == 2) pl = plan_st(N, K, bits, rt);
+  if (impl == 2 && rt == 4 && pl.nw != 0 && !pl.tcmma) {
+    // the 16-row plan twice, when the model prefers it (rows 0-15 and the rest)
+    const QmmPlan h = plan_st(N, K, bits, 2);
+    if (h.nw != 0 && !h.tcmma && 2.0 * h.model_s < pl.model_s) pl.halves = true;
+  }
   if (pl.nw == 0 && impl >= 1) pl = plan_tc(N, K, bits, rt);
   // shapes whose x slice and ring fit neither persistent engine run on per-tile CTAs (the same
   // contract, all hand-written CUDA)
@@ -667,6 +672,7 @@ QmmPlan plan_st(int N, int K, int bits, int rt) {
       pl.kslice = kslice;
       pl.nslots = slots;
       pl.clusters = clusters;
+      pl.model_s = t;
     }
   }
   return pl;
@@ -804,6 +810,28 @@ int run(const QmmParams& p_in, int epi, const QmmPlan* plan_in, cudaStream_t str
   if ((p.peer_world > 0 || p.wait_flag != nullptr) && (pl.engine != 2 || pl.tcmma))
     return fail(DSPARK_ERR_UNSUPPORTED,
                 "qmm: peer stores / gather waits need the streaming engine with mma.sync consumers");
+  if (pl.halves && p.M > 16 && p.peer_world == 0 && p.wait_flag == nullptr) {
+    // two launches of the 16-row plan: every per-row pointer of the second one moves 16 rows
+    // (x, out, residual, statistics in / out, q output, positions, cache offsets)
+    const QmmPlan h = plan(p.N, p.K, p.bits, epi, epi == EPI_QKROPE ? 128 : 0, 2);
+    if (h.nw != 0 && !h.halves) {
+      QmmParams a = p_in;
+      a.M = 16;
+      const int rc = run(a, epi, &h, stream);
+      if (rc != DSPARK_OK) return rc;
+      QmmParams b = p_in;
+      b.M = p_in.M - 16;
+      b.x = p_in.x + 16 * p_in.ldx;
+      if (b.out) b.out = p_in.out + 16 * p_in.ldo;
+      if (b.resid) b.resid = p_in.resid + 16 * p_in.ldr;
+      if (b.ssq_in) b.ssq_in = p_in.ssq_in + 16;
+      if (b.ssq_out) b.ssq_out = p_in.ssq_out + 16;
+      if (b.qout) b.qout = p_in.qout + 16 * p_in.ldq;
+      if (b.row_pos) b.row_pos = p_in.row_pos + 16;
+      if (b.row_kv) b.row_kv = p_in.row_kv + 16;
+      return run(b, epi, &h, stream);
+    }
+  }
   p.kslice = pl.kslice;
   p.cs = pl.cs;
   p.nslots = pl.nslots;

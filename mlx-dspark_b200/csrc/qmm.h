@@ -82,6 +82,11 @@ struct QmmPlan {
                     // 0: mma.sync per-tile CTAs (qmm.cu)
   int clusters = 0; // tcgen05: persistent clusters walking the tiles (0: one per cs SMs)
   bool tcmma = false; // streaming engine: tcgen05 MMA consumers (else mma.sync consumers)
+  double model_s = 0; // streaming engine: the planner's modelled launch time (seconds)
+  // 17-32 rows: run as two launches of the 16-row plan (rows 0-15, then the rest). Chosen for
+  // deep-K shapes, where 32 staged rows of x leave shared memory for a high split-K factor only
+  // and two 16-row launches are modelled faster. Never set with peer stores or gather waits.
+  bool halves = false;
 };
 
 // TMA descriptors of the packed weights (128-byte swizzle, boxes of 32 words x tn rows) and,

@@ -144,3 +144,56 @@ def test_rejects_unsupported(cuda):
         skinny_qmm.qmm(torch.zeros((33, 512), dtype=torch.bfloat16, device=cuda), w, s, s, 4)
     with pytest.raises(DSparkUnsupported):
         skinny_qmm.qmm(torch.zeros((2, 512), dtype=torch.bfloat16, device=cuda), w, s, s, 3)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_deep_k_32_rows(cuda, oracle, bits):
+    """17-32 rows on the down-projection shape (K = 12288). There, 32 staged rows of x leave
+    shared memory for a high split-K factor only, and the planner may run the rows as two
+    16-row launches. Parity with the oracle, and a row's result is the same bits whichever
+    count of 17-32 rows rides with it."""
+    N, K = 4096, 12288
+    wq, sc, bi = _weights(oracle, N, K, bits, seed=21)
+    x = _x(oracle, 32, K, seed=9, scale=0.1)
+    _, full = _run(cuda, oracle, x, wq, sc, bi, bits)
+    ref = oracle.qmm(x, wq, sc, bi, bits)
+    _check(full.float().cpu().numpy(), ref)
+    for m in (17, 24):
+        got, part = _run(cuda, oracle, x[:m], wq, sc, bi, bits)
+        _check(got, ref[:m])
+        assert torch.equal(full[:m], part), m
+
+
+def test_deep_k_32_rows_residual_epilogue(cuda, oracle):
+    """The residual epilogue (down projection + residual add + the next RMSNorm's per-tile
+    sums of squares) at 24 rows on the deep-K shape, through dspark_qmm_fused: rows 16-23
+    land at their own output, residual and statistics slots."""
+    import ctypes as C
+
+    from mlx_dspark_b200 import _lib
+    from mlx_dspark_b200._torch import ptr
+
+    N, K, M, bits = 4096, 12288, 24, 4
+    wq, sc, bi = _weights(oracle, N, K, bits, seed=23)
+    x = _x(oracle, M, K, seed=4, scale=0.1)
+    w_d, s_d, b_d = _to_dev(oracle, wq, sc, bi, cuda)
+    xd = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(cuda)
+    g = torch.Generator(device=cuda).manual_seed(5)
+    resid = (torch.randn((M, N), device=cuda, generator=g) * 0.5).to(torch.bfloat16)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=cuda)
+    ntiles = N // 128
+    ssq = torch.full((ntiles * 32,), float("nan"), dtype=torch.float32, device=cuda)
+    a = _lib.QmmArgs()
+    a.x, a.ldx, a.M, a.K, a.N, a.bits = ptr(xd), K, M, K, N, bits
+    a.wq, a.scales, a.biases = ptr(w_d), ptr(s_d), ptr(b_d)
+    a.out, a.ldo, a.epilogue = ptr(out), N, _lib.EPI_RESID
+    a.resid, a.ldr, a.ssq_out, a.ssq_stride, a.eps = ptr(resid), N, ptr(ssq), 32, 1e-6
+    _lib.check(_lib.lib.dspark_qmm_fused(C.byref(a), torch.cuda.current_stream(cuda).cuda_stream))
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    ref = oracle.round_bf16(oracle.round_bf16(oracle.qmm(x, wq, sc, bi, bits)) +
+                            resid.float().cpu().numpy())
+    _check(got, ref)
+    sums = (got.reshape(M, ntiles, 128) ** 2).sum(axis=2)  # [M, tiles]
+    s = ssq.cpu().numpy().reshape(ntiles, 32)
+    np.testing.assert_allclose(s[:, :M].T, sums, rtol=5e-3, atol=1e-3)
