@@ -206,3 +206,36 @@ def test_tree_bits():
     from mlx_dspark_b200.multirow_attn import tree_bits
 
     assert tree_bits([-1, 0, 0, 1]) == [0b1, 0b11, 0b101, 0b1011]
+
+
+_MIRRORS = {"QWeight": "dspark_qweight", "Layer": "dspark_layer", "Model": "dspark_model",
+            "FwdBuffers": "dspark_fwd_buffers", "P2PGatherArgs": "dspark_p2p_gather_args",
+            "QmmArgs": "dspark_qmm_args"}
+
+
+def test_ctypes_mirrors_match_the_header_layout(tmp_path):
+    """Every struct the shim passes by pointer has, field by field, the offsets and the size the
+    C compiler gives include/dspark.h (a drifted mirror would hand the kernels shifted fields)."""
+    import shutil
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "dspark.h"', "int main(void) {"]
+    want = {}
+    for py, c in _MIRRORS.items():
+        cls = getattr(_lib, py)
+        lines.append(f'  printf("{py} %zu\\n", sizeof({c}));')
+        want[py] = C.sizeof(cls)
+        for name, _ in cls._fields_:
+            lines.append(f'  printf("{py}.{name} %zu\\n", offsetof({c}, {name}));')
+            want[f"{py}.{name}"] = getattr(cls, name).offset
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([gcc, "-std=c11", "-I", str(ROOT / "include"), str(src), "-o", str(exe)],
+                   check=True, capture_output=True)
+    got = dict(line.split() for line in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                       text=True).stdout.splitlines())
+    assert {k: int(v) for k, v in got.items()} == want
