@@ -42,6 +42,12 @@ int dspark_init(int device);
  * wait that ran out on that device. Synchronizes the device. */
 int dspark_device_status(int device, int* code, int clear);
 
+/* Bound of every kernel wait on `device` (a stage, a cluster peer, a peer GPU's flag), in
+ * nanoseconds; 0 restores the built-in 2 s. A wait that runs out records its code in the status
+ * word and the kernel drains without further waits. Library extension for failure detection (the
+ * reference has no device waits: MLX raises on the host). Synchronizes the device. */
+int dspark_set_wait_limit_ns(int device, uint64_t ns);
+
 /* Number of streaming multiprocessors of `device` (launch planning). */
 int dspark_sm_count(int device);
 
@@ -138,11 +144,19 @@ int dspark_qmm_fused(const dspark_qmm_args* a, void* stream);
 /* RoPE frequencies theta^(-2i/head_dim), i < head_dim / 2, as the fused epilogue uses them. */
 int dspark_rope_inv_freq(float* inv_freq, int head_dim, float theta, void* stream);
 
-/* Launch geometry the QMM would use for [N, K] at `bits` (depends on the weight shape only,
- * so a row's result never depends on M): tile width, split-K cluster size, k per split,
- * pipeline depth. Mirrors skinny_qmm.plan/geometry (src/mlx_dspark/skinny_qmm.py:214-236). */
+/* Launch geometry the QMM uses for [N, K] at `bits` for 1-16 rows: tile width, split-K
+ * cluster size, k per split, pipeline depth. The plan is fixed within each row class (1-16 rows
+ * and 17-32 rows), so inside a class a row's result never depends on how many rows ride with it.
+ * Mirrors skinny_qmm.plan/geometry (src/mlx_dspark/skinny_qmm.py:214-236). */
 int dspark_qmm_plan(int N, int K, int bits, int* tile_n, int* split_k, int* k_slice,
                     int* stages);
+
+/* The plan dspark_qmm runs for `rows` (1..32) rows: out[0] tile width, out[1] split-K cluster
+ * size, out[2] k per split, out[3] pipeline depth, out[4] persistent clusters (0: one per tile),
+ * out[5] launches (2 when a 17-32-row call runs as two 16-row launches), out[6] engine (2:
+ * streaming, 1: tcgen05 / tensor memory, 0: per-tile CTAs). Same plan source as
+ * dspark_qmm_plan. */
+int dspark_qmm_plan_rows(int N, int K, int bits, int rows, int out[7]);
 
 /* ------------------------------------------------------------------------------------ K2 */
 
@@ -171,7 +185,8 @@ int dspark_verify_attn(const void* q, const int64_t q_strides[3], const void* k,
  * let an allocation or a cudaFree stall the device. Its scratch is a static 4 MiB device array
  * per GPU (held until exit); shapes whose workspace (dspark_verify_attn_workspace) exceeds it
  * fail with DSPARK_ERR_UNSUPPORTED. The first call on a device looks up that array's device
- * address, so make it before any stream capture. Calls share the array: calls that overlap on
+ * address, so make it before any stream capture. The stream must belong to the current device
+ * (a stream of another device is DSPARK_ERR_ARG). Calls share the array: calls that overlap on
  * the GPU race. Nothing is allocated and nothing needs clearing between calls. */
 int dspark_verify_attn_noalloc(const void* q, const int64_t q_strides[3], const void* k,
                                const int64_t k_strides[3], const void* v,

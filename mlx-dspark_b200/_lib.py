@@ -102,11 +102,13 @@ _SIGS = {
     "dspark_last_error": (C.c_char_p, []),
     "dspark_init": (i32, [i32]),
     "dspark_device_status": (i32, [i32, P_int, i32]),
+    "dspark_set_wait_limit_ns": (i32, [i32, C.c_uint64]),
     "dspark_sm_count": (i32, [i32]),
     "dspark_launch_count": (C.c_longlong, []),
     "dspark_qmm": (i32, [vp, i32, i32, vp, vp, vp, i32, i32, i32, vp, vp]),
     "dspark_qmm_ex": (i32, [vp, i64, i32, i32, vp, vp, vp, vp, i32, i32, i32, vp, i64, vp]),
     "dspark_qmm_plan": (i32, [i32, i32, i32, P_int, P_int, P_int, P_int]),
+    "dspark_qmm_plan_rows": (i32, [i32, i32, i32, i32, P_int]),
     "dspark_verify_attn": (i32, [vp, P_i64, vp, P_i64, vp, P_i64, i32, i32, i32, i32, i32, i32,
                                  vp, f32, i32, vp, vp, P_i64, vp, sz, vp]),
     "dspark_verify_attn_noalloc": (i32, [vp, P_i64, vp, P_i64, vp, P_i64, i32, i32, i32, i32, i32,
@@ -174,6 +176,11 @@ def ensure_init(device: int) -> None:
     if device not in _inited:
         check(lib.dspark_init(device))
         _inited.add(device)
+
+
+def set_wait_limit_ns(device: int, ns: int) -> None:
+    """Bound of every kernel wait on ``device`` (0 restores the built-in 2 s)."""
+    check(lib.dspark_set_wait_limit_ns(device, int(ns)))
 
 
 def device_status(device: int = 0, clear: bool = True) -> int:

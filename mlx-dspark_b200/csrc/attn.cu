@@ -646,14 +646,14 @@ template <int D, int NRT, int KS>
 static int launch_attn(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) {
   auto kern = attn_kernel<D, NRT, KS>;
   constexpr int smem = attn_smem_bytes<D, NRT, KS>();
-  static bool configured = false;
-  if (!configured) {
-    DSPARK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                    "attn: set smem");
-    DSPARK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
-                    "attn: allow cluster 16");
-    configured = true;
-  }
+  DSPARK_CUDA_TRY(configure_once(reinterpret_cast<const void*>(kern), 1, [&] {
+                    cudaError_t e = cudaFuncSetAttribute(
+                        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                    if (e != cudaSuccess) return e;
+                    return cudaFuncSetAttribute(
+                        kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+                  }),
+                  "attn: set smem / cluster attributes");
   dim3 grid(pl.ns, p.B * p.Hk * pl.nrg, pl.ng);
   dim3 block((NRT * KS + 1) * 32);
   DSPARK_CUDA_TRY(launch_ex(kern, grid, block, smem, s, pl.ns, true, p), "attn: launch");

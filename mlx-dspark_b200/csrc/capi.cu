@@ -6,9 +6,11 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <utility>
 
 #include "attn.h"
 #include "host_common.h"
@@ -74,6 +76,22 @@ bool pdl_enabled() {
 static std::atomic<long long> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+// Function attributes (dynamic shared memory, cluster size) belong to one device's context, so
+// the value a kernel was configured with is kept per (kernel, device).
+static std::mutex g_cfg_mu;
+static std::map<std::pair<const void*, int>, int> g_cfg;
+
+int configured_value(const void* fn, int device) {
+  std::lock_guard<std::mutex> lk(g_cfg_mu);
+  auto it = g_cfg.find(std::make_pair(fn, device));
+  return it == g_cfg.end() ? 0 : it->second;
+}
+
+void set_configured_value(const void* fn, int device, int value) {
+  std::lock_guard<std::mutex> lk(g_cfg_mu);
+  g_cfg[std::make_pair(fn, device)] = value;
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -115,14 +133,15 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, 
 // ------------------------------------------------------------------------ forward plans
 
 struct PlanKey {
-  int N, K, bits, epi;
+  int dev, N, K, bits, epi;
   bool operator==(const PlanKey& o) const {
-    return N == o.N && K == o.K && bits == o.bits && epi == o.epi;
+    return dev == o.dev && N == o.N && K == o.K && bits == o.bits && epi == o.epi;
   }
 };
 struct PlanKeyHash {
   size_t operator()(const PlanKey& k) const {
-    return (size_t(k.N) * 1000003u) ^ (size_t(k.K) * 7919u) ^ (size_t(k.bits) << 3) ^ size_t(k.epi);
+    return (size_t(k.N) * 1000003u) ^ (size_t(k.K) * 7919u) ^ (size_t(k.bits) << 3) ^
+           size_t(k.epi) ^ (size_t(k.dev) << 40);
   }
 };
 static std::unordered_map<PlanKey, qmm::QmmPlan, PlanKeyHash> g_plans;
@@ -130,7 +149,7 @@ static std::unordered_map<PlanKey, qmm::QmmPlan, PlanKeyHash> g_plans;
 static qmm::QmmPlan cached_plan(int N, int K, int bits, int epi, int rows) {
   std::lock_guard<std::mutex> lk(g_mu);
   const int rt = rows <= 16 ? 2 : 4;
-  PlanKey key{N, K, bits, epi * 8 + rt};
+  PlanKey key{current_device(), N, K, bits, epi * 8 + rt};
   auto it = g_plans.find(key);
   if (it != g_plans.end()) return it->second;
   qmm::QmmPlan pl = qmm::plan(N, K, bits, epi, epi == qmm::EPI_QKROPE ? 128 : 0, rt);
@@ -166,6 +185,20 @@ int dspark_init(int device) {
   if (e != cudaSuccess) return cuda_fail(e, "init: status word");
   g_status[device] = p;
   sm_count(device);
+  return DSPARK_OK;
+}
+
+int dspark_set_wait_limit_ns(int device, uint64_t ns) {
+  int* w = status_word(device);
+  if (w == nullptr) return fail(DSPARK_ERR_NOT_INIT, "set_wait_limit_ns: dspark_init(%d) not called", device);
+  int prev = 0;
+  DSPARK_CUDA_TRY(cudaGetDevice(&prev), "set_wait_limit_ns");
+  DSPARK_CUDA_TRY(cudaSetDevice(device), "set_wait_limit_ns");
+  // bytes 8..15 of the status block; 0 restores the built-in bound
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(w + 2, &ns, sizeof(ns), cudaMemcpyHostToDevice);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "set_wait_limit_ns");
   return DSPARK_OK;
 }
 
@@ -290,6 +323,21 @@ int dspark_qmm_plan(int N, int K, int bits, int* tile_n, int* split_k, int* k_sl
   if (split_k) *split_k = pl.cs;
   if (k_slice) *k_slice = pl.kslice;
   if (stages) *stages = pl.nslots;
+  return DSPARK_OK;
+}
+
+int dspark_qmm_plan_rows(int N, int K, int bits, int rows, int out[7]) {
+  if (!out) return fail(DSPARK_ERR_ARG, "qmm_plan_rows: null");
+  if (bits != 4 && bits != 8) return fail(DSPARK_ERR_UNSUPPORTED, "qmm_plan_rows: bits %d", bits);
+  if (K <= 0 || K % 64 || N <= 0 || N % 8) return fail(DSPARK_ERR_UNSUPPORTED, "qmm_plan_rows: shape");
+  if (rows < 1 || rows > 32) return fail(DSPARK_ERR_UNSUPPORTED, "qmm_plan_rows: rows %d", rows);
+  const int rt = rows <= 16 ? 2 : 4;
+  qmm::QmmPlan pl = qmm::plan(N, K, bits, qmm::EPI_PLAIN, 0, rt);
+  if (pl.nw == 0) return fail(DSPARK_ERR_UNSUPPORTED, "qmm_plan_rows: no geometry");
+  const bool two = pl.halves && rows > 16;
+  if (two) pl = qmm::plan(N, K, bits, qmm::EPI_PLAIN, 0, 2);
+  out[0] = 16 * pl.nw; out[1] = pl.cs; out[2] = pl.kslice; out[3] = pl.nslots;
+  out[4] = pl.clusters; out[5] = two ? 2 : 1; out[6] = pl.engine;
   return DSPARK_OK;
 }
 

@@ -31,7 +31,9 @@ enum DeviceError : int {
   kErrWaitMma = 0x107,       // a tensor-core completion wait ran out of time
 };
 
-// ~2 s: far beyond any legitimate wait inside one kernel launch.
+// ~2 s: far beyond any legitimate wait inside one kernel launch. The default bound; a process
+// can change it per device (dspark_set_wait_limit_ns), which stores the bound in the second
+// 8-byte word of the device status block.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -46,6 +48,14 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 __device__ __forceinline__ void report_error(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
+}
+
+// The bound of a wait: the per-device value stored after the status word (bytes 8..15 of the
+// status block), or kWaitLimitNs when unset. Read only on a wait's slow path.
+__device__ __forceinline__ uint64_t wait_limit_ns(const int* status) {
+  if (status == nullptr) return kWaitLimitNs;
+  const uint64_t v = *reinterpret_cast<const volatile uint64_t*>(status + 2);
+  return v ? v : kWaitLimitNs;
 }
 
 // ------------------------------------------------------------------ mbarrier
@@ -88,16 +98,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete. Returns false (and records `code`)
-// if it has not completed within kWaitLimitNs.
+// if it has not completed within the wait bound (wait_limit_ns).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(status);
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(a, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit) {
       report_error(status, code);
       return false;
     }
@@ -251,13 +262,14 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
 }
 
 // Wait until the monotonic counter *f reaches `target` (wrap-safe); false (and `code` recorded)
-// if it has not within kWaitLimitNs.
+// if it has not within the wait bound (wait_limit_ns).
 __device__ __forceinline__ bool wait_counter_sys(const uint32_t* f, uint32_t target, int* status,
                                                  int code) {
   if (int32_t(ld_acquire_sys(f) - target) >= 0) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(status);
   while (int32_t(ld_acquire_sys(f) - target) < 0) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit) {
       report_error(status, code);
       return false;
     }
@@ -307,11 +319,12 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait_cluster(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(status);
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait_cluster(a, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit) {
       report_error(status, code);
       return false;
     }

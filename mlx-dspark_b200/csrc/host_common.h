@@ -48,6 +48,23 @@ int env_int(const char* name, int dflt);
 // Kernel launches issued through launch_ex since the library was loaded.
 void count_launch();
 
+// The value a kernel's function attributes were last configured with on `device` (0: never).
+// cudaFuncSetAttribute acts on the current device's context only, so a kernel launched on a
+// second device of the same process must be configured there again.
+int configured_value(const void* fn, int device);
+void set_configured_value(const void* fn, int device, int value);
+
+// Run `setup()` (returning cudaError_t) unless `fn` was configured with at least `value` on the
+// current device; record `value` when it succeeds.
+template <typename F>
+cudaError_t configure_once(const void* fn, int value, F&& setup) {
+  const int dev = current_device();
+  if (configured_value(fn, dev) >= value) return cudaSuccess;
+  const cudaError_t e = setup();
+  if (e == cudaSuccess) set_configured_value(fn, dev, value);
+  return e;
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
                       cudaStream_t stream, int cluster_x, bool pdl, Args&&... args) {

@@ -11,7 +11,9 @@
 // The array is kNoAllocScratchBytes (4 MiB) on every GPU that loads this library, held until the
 // process exits. Its host-side name is only a stand-in for the device copy, so the device
 // address is looked up once per device (cudaGetSymbolAddress, with that device current) on the
-// first call there; that first call should therefore happen before any stream capture. All calls
+// first call there; that first call should therefore happen before any stream capture. The
+// stream must belong to the current device (checked: another device's stream is an argument
+// error, since the array's address differs per device). All calls
 // on a device share the array: calls that overlap on the GPU (different streams with no ordering
 // between them) race on it. Nothing in it needs clearing: every value a launch reads from the
 // workspace is written earlier in the same launch sequence.
@@ -83,6 +85,14 @@ extern "C" int dspark_verify_attn_noalloc(const void* q, const int64_t q_strides
                 "%zu-byte static maximum (use dspark_verify_attn with a workspace)",
                 need, kNoAllocScratchBytes);
   if (need > 0) {
+    // the array is looked up for the current device, so the stream must belong to it
+    int sdev = -1;
+    const cudaError_t se = cudaStreamGetDevice(reinterpret_cast<cudaStream_t>(stream), &sdev);
+    if (se != cudaSuccess) return cuda_fail(se, "verify_attn_noalloc: stream device");
+    if (sdev != current_device())
+      return fail(DSPARK_ERR_ARG,
+                  "verify_attn_noalloc: the stream belongs to device %d, the current device is %d",
+                  sdev, current_device());
     void* ws = nullptr;
     const int rc = scratch_address(&ws);
     if (rc != DSPARK_OK) return rc;

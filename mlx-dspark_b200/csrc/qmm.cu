@@ -525,18 +525,20 @@ static int launch_one(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream
   auto kern = qmm_kernel<BITS, RT, NW, EPI, SCT>;
   constexpr int TN = 16 * NW;
   const SmemLayout L = smem_layout<BITS, NW, RT>(pl.kslice, pl.nslots);
-  static int configured_smem = 0;  // per instantiation
-  if (L.total > configured_smem) {
-    DSPARK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total),
-                    "qmm: set smem");
-    DSPARK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
-                    "qmm: allow cluster 16");
-    const int carve = env_int("DSPARK_QMM_CARVEOUT", -1);
-    if (carve >= 0)
-      DSPARK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, carve),
-                      "qmm: carveout");
-    configured_smem = L.total;
-  }
+  // configured per device with the largest dynamic shared memory asked for so far
+  DSPARK_CUDA_TRY(configure_once(reinterpret_cast<const void*>(kern), L.total, [&] {
+                    cudaError_t e = cudaFuncSetAttribute(
+                        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
+                    if (e == cudaSuccess)
+                      e = cudaFuncSetAttribute(
+                          kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+                    const int carve = env_int("DSPARK_QMM_CARVEOUT", -1);
+                    if (e == cudaSuccess && carve >= 0)
+                      e = cudaFuncSetAttribute(
+                          kern, cudaFuncAttributePreferredSharedMemoryCarveout, carve);
+                    return e;
+                  }),
+                  "qmm: set smem / cluster attributes");
   CUtensorMap wmap, smap, bmap;
   if (!tma_maps(p, TN, SCT, &wmap, &smap, &bmap)) return DSPARK_ERR_CUDA;
   dim3 grid(pl.cs, (p.N + TN - 1) / TN);

@@ -1026,11 +1026,9 @@ template <int BITS, int MT, int EPI, bool TC, bool PEER = false>
 static int launch_st(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream) {
   auto kern = st::qmm_st_kernel<BITS, MT, EPI, TC, PEER>;
   const int smem = st_smem_bytes(BITS, MT, pl.kslice, pl.nslots, pl.cs, TC);
-  static bool configured = false;
-  if (!configured) {
-    DSPARK_CUDA_TRY(configure_st(kern), "qmm_st: set smem / cluster attributes");
-    configured = true;
-  }
+  DSPARK_CUDA_TRY(configure_once(reinterpret_cast<const void*>(kern), 1,
+                                 [&] { return configure_st(kern); }),
+                  "qmm_st: set smem / cluster attributes");
   CUtensorMap wmap, smap, bmap;
   if (!tma_maps(p, st::TN, true, &wmap, &smap, &bmap)) return DSPARK_ERR_CUDA;
   const int ntiles = (p.N + st::TN - 1) / st::TN;

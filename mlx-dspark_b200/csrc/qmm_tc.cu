@@ -660,11 +660,9 @@ template <int BITS, int RT, int EPI, bool SCT>
 static int launch_tc(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream) {
   auto kern = tc::qmm_tc_kernel<BITS, RT, EPI, SCT>;
   const int smem = tc_launch_smem(BITS, RT, pl.kslice, pl.nslots);
-  static bool configured = false;
-  if (!configured) {
-    DSPARK_CUDA_TRY(configure_tc(kern), "qmm_tc: set smem / cluster attributes");
-    configured = true;
-  }
+  DSPARK_CUDA_TRY(configure_once(reinterpret_cast<const void*>(kern), 1,
+                                 [&] { return configure_tc(kern); }),
+                  "qmm_tc: set smem / cluster attributes");
   CUtensorMap wmap, smap, bmap;
   if (!tma_maps(p, tc::TN, SCT, &wmap, &smap, &bmap)) return DSPARK_ERR_CUDA;
   const int ntiles = (p.N + tc::TN - 1) / tc::TN;

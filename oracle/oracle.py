@@ -77,8 +77,11 @@ def set_threads(n: int) -> None:
 def to_bf16(a) -> np.ndarray:
     """fp32 -> bf16 bit patterns (uint16), round to nearest even (NaN kept quiet)."""
     a = np.ascontiguousarray(np.asarray(a, dtype=np.float32))
-    u = a.view(np.uint32).astype(np.uint64)
-    rounded = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    u = a.view(np.uint32)
+    # finite values and infinities stay below 2^32 after the rounding bias; NaN patterns may
+    # wrap and are replaced below
+    rounded = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1)))
+               >> np.uint32(16)).astype(np.uint16)
     nan = np.isnan(a)
     if nan.any():
         rounded = np.where(nan, np.uint16(0x7FC0), rounded)
@@ -375,8 +378,9 @@ def verify_forward(weights: dict, cfg: dict, ids, kcache: list, vcache: list, L0
     dataflows, and the spread between them is the noise floor a GPU forward is judged by.
 
     weights: numpy arrays from the device model (separate q/k/v/gate/up matrices);
-    kcache / vcache: per-layer float32 arrays [Hk, cap, D] (modified in place).
-    Returns fp32 logits [M, vocab]."""
+    kcache / vcache: per-layer arrays [Hk, cap, D] (modified in place), either float32 values
+    or uint16 bf16 bit patterns (read by the attention without a per-layer conversion; the
+    timed CPU baseline keeps its cache that way). Returns fp32 logits [M, vocab]."""
     H, Hq, Hk, D = cfg["hidden"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"]
     eps, theta = cfg["rms_eps"], cfg["rope_theta"]
     M = len(ids)
@@ -393,10 +397,15 @@ def verify_forward(weights: dict, cfg: dict, ids, kcache: list, vcache: list, L0
         v = qlinear(x, lw["v"]).reshape(M, Hk, D)
         q = rope(rmsnorm(q, lw["q_norm"], eps).transpose(1, 0, 2), pos, theta)  # [Hq, M, D]
         k = rope(rmsnorm(k, lw["k_norm"], eps).transpose(1, 0, 2), pos, theta)
-        kcache[li][:, L0:L] = k
-        vcache[li][:, L0:L] = v.transpose(1, 0, 2)
-        o = sdpa(to_bf16(q)[None], to_bf16(kcache[li][:, :L])[None],
-                 to_bf16(vcache[li][:, :L])[None], D ** -0.5, True, round_p=round_p)[0]
+        if kcache[li].dtype == np.uint16:  # bf16 bit-pattern cache
+            kcache[li][:, L0:L] = to_bf16(k)
+            vcache[li][:, L0:L] = to_bf16(v.transpose(1, 0, 2))
+            kb, vb = kcache[li][None, :, :L], vcache[li][None, :, :L]
+        else:
+            kcache[li][:, L0:L] = k
+            vcache[li][:, L0:L] = v.transpose(1, 0, 2)
+            kb, vb = to_bf16(kcache[li][:, :L])[None], to_bf16(vcache[li][:, :L])[None]
+        o = sdpa(to_bf16(q)[None], kb, vb, D ** -0.5, True, round_p=round_p)[0]
         o = round_bf16(o).transpose(1, 0, 2).reshape(M, Hq * D)
         h = round_bf16(h + qlinear(o, lw["o"]))
         if trace is not None:

@@ -140,3 +140,101 @@ def test_qwen3_8b_shape_runs(cuda):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(t.logits[:16], a)
+
+
+def _accept_check(oracle, t, logits_t, ids, lens, L0):
+    """Accept + rollback on the device vs the host restatement of the greedy rule
+    (src/mlx_dspark/generate.py:1548-1555) applied to the same logits: bit-exact."""
+    out = t.accept_and_rollback(logits_t, ids, lens)
+    torch.cuda.synchronize()
+    tt = oracle.argmax_first(logits_t.float().cpu().numpy())
+    assert np.array_equal(out["tt"].cpu().numpy(), tt)
+    n, committed, trim = oracle.accept(ids[1:].cpu().numpy(), tt)
+    assert int(out["n"][0]) == n and int(out["next"][0]) == committed[-1]
+    assert int(lens[0]) == L0 + n + 1
+    return n
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_qwen3_8b_dims_match_oracle(cuda, oracle, bits):
+    """The projections, attention and head at the benchmarked Qwen3-8B dims (hidden 4096,
+    intermediate 12288, GQA 32/8, head_dim 128, vocab 151936), 2 layers, one 16-row block at
+    2k context: the planner's split-K / cluster / epilogue choices at these shapes are the
+    ones the bench times. Logits within the forward's bar, greedy argmax identical on every
+    decided row, then a block whose first drafts follow the target's own argmax is accepted
+    and rolled back bit-exactly."""
+    from dataclasses import replace
+
+    from mlx_dspark_b200.target import QWEN3_8B, Target
+
+    cfg = replace(QWEN3_8B, n_layers=2, bits=bits)
+    L0, R = 2048, 16
+    t = Target(cfg, kv_cap=L0 + 64, seed=20 + bits)
+    kc, vc = _prefill(t, L0, seed=bits)
+    ids = torch.randint(0, cfg.vocab, (R,), device=cuda, dtype=torch.int32)
+    lens = torch.tensor([L0], dtype=torch.int32, device=cuda)
+    logits = t.verify(ids, lens).float().cpu().numpy()
+    assert int(lens[0]) == L0 + R
+    ow, oc = t.oracle_weights(), t.oracle_config()
+    ref_p = oracle.verify_forward(ow, oc, ids.cpu().numpy(), [c.copy() for c in kc],
+                                  [c.copy() for c in vc], L0, round_p=True)
+    ref = oracle.verify_forward(ow, oc, ids.cpu().numpy(), kc, vc, L0)
+    err, ties = _compare(oracle, logits, ref, ref_p)
+    # random-init logits at vocab 151936 have top-2 gaps of ~0.2 on average, so a few rows fall
+    # inside twice the max logit error (near-ties, reported); most rows must be decided
+    print(f"max logit err {err:.4f}, near-tie rows {ties} of {R}")
+    assert ties <= R - 4, f"only {R - ties} decided rows"
+    # drafts 1..6 follow the target's argmax (fixed point), the rest do not
+    ids2 = ids.clone()
+    for _ in range(8):
+        lens.fill_(L0)
+        tt = t.verify(ids2, lens).float().argmax(dim=1).to(torch.int32)
+        ids2[1:7] = tt[0:6]
+    lens.fill_(L0)
+    n = _accept_check(oracle, t, t.verify(ids2, lens), ids2, lens, L0)
+    assert n >= 6
+
+
+def test_qwen3_32b_dims_tp1_match_oracle(cuda, oracle):
+    """The 27B-class configuration's dims (hidden 5120, intermediate 25600, GQA 64/8, 8-bit,
+    vocab 151936) through the column-sharded target at P = 1, 2 layers, one 16-row block at
+    32k context (the attention runs its split-and-merge plan there): logits, greedy argmax and
+    accept / rollback as above."""
+    from dataclasses import replace
+
+    from mlx_dspark_b200.target import QWEN3_32B
+    from mlx_dspark_b200.target_tp import TPTarget
+    from test_tp_gpu import _fill_cache
+
+    cfg = replace(QWEN3_32B, n_layers=2)
+    L0, R = 32768, 16
+    cap = L0 + 64
+    t = TPTarget(cfg, 0, 1, kv_cap=cap, seed=32, max_rows=R)
+    full = _fill_cache(t, L0, seed=6)
+    ids = torch.randint(0, cfg.vocab, (R,), device=cuda, dtype=torch.int32)
+    lens = torch.tensor([L0], dtype=torch.int32, device=cuda)
+    logits = t.verify(ids, lens).float().cpu().numpy()
+    assert int(lens[0]) == L0 + R
+    kc = [np.zeros((cfg.n_kv_heads, cap, cfg.head_dim), np.float32) for _ in t.layers]
+    vc = [np.zeros((cfg.n_kv_heads, cap, cfg.head_dim), np.float32) for _ in t.layers]
+    for li, (k, v) in enumerate(full):
+        kc[li][:, :L0] = k.float().numpy()
+        vc[li][:, :L0] = v.float().numpy()
+    del full
+    ow, oc = t.oracle_weights(), t.oracle_config()
+    ref_p = oracle.verify_forward(ow, oc, ids.cpu().numpy(), [c.copy() for c in kc],
+                                  [c.copy() for c in vc], L0, round_p=True)
+    ref = oracle.verify_forward(ow, oc, ids.cpu().numpy(), kc, vc, L0)
+    err, ties = _compare(oracle, logits, ref, ref_p)
+    # random-init logits at vocab 151936 have top-2 gaps of ~0.2 on average, so a few rows fall
+    # inside twice the max logit error (near-ties, reported); most rows must be decided
+    print(f"max logit err {err:.4f}, near-tie rows {ties} of {R}")
+    assert ties <= R - 4, f"only {R - ties} decided rows"
+    lens.fill_(L0)
+    logits_t = t.verify(ids, lens)
+    out = t.accept_and_rollback(t.b["logits_full"][:R], ids, lens)
+    torch.cuda.synchronize()
+    tt = oracle.argmax_first(logits_t.float().cpu().numpy())
+    n, committed, _ = oracle.accept(ids[1:].cpu().numpy(), tt)
+    assert int(out["n"][0]) == n and int(out["next"][0]) == committed[-1]
+    assert int(lens[0]) == L0 + n + 1

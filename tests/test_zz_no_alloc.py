@@ -11,6 +11,7 @@ The file is named so that pytest collects it last.
 
 import ctypes as C
 
+import numpy as np
 import pytest
 import torch
 
@@ -32,7 +33,7 @@ def _noalloc(q, k, v, scale, causal):
     return out
 
 
-def test_noalloc_matches_the_workspace_entry_point_twice():
+def test_noalloc_matches_the_workspace_entry_point_twice(oracle):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     _lib.ensure_init(0)
@@ -51,6 +52,13 @@ def test_noalloc_matches_the_workspace_entry_point_twice():
         err = float((got.float() - ref.float()).abs().max())
         tol = 1e-2 * float(ref.float().abs().max())
         assert err <= tol, f"call {call}: max |diff| {err} > {tol}"
+        if call == 0:
+            # and against the CPU oracle's attention at this 32k-key shape
+            bits = lambda t: t.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+            want = oracle.sdpa(bits(q), bits(k), bits(v), scale, True)
+            err_o = float(np.abs(got.float().cpu().numpy() - want).max())
+            tol_o = 1e-2 * float(np.abs(want).max())
+            assert err_o <= tol_o, f"vs oracle: max |diff| {err_o} > {tol_o}"
     assert _lib.device_status(0) == 0
 
 
