@@ -35,6 +35,17 @@
 //    per-warp arrive for its own rows. The owner sums the halves of each rank, then the ranks,
 //    in fixed order (double-buffered; deterministic, and a row's result never depends on how
 //    many rows ride with it), then the shared epilogue runs on them.
+//  * tcgen05 consumers (template flag TC, DSPARK_QMM_ST_TC=1): eight dequantization warps write
+//    each row's weights fully dequantized (w = scale * q + bias, one rounding to bf16) into
+//    double-buffered A buffers in tensor memory, one MMA warp accumulates the whole K slice of
+//    a tile into a D buffer (M = 128 tile rows, N = 16 or 32 staged x rows), and the epilogue
+//    warps read D once per tile and push it like the partials above. Correct (row-count
+//    invariant within a row class) but slower at these row counts, for a measured reason: on
+//    B200 one kind::f16 MMA with M = 128, K = 16 takes ~100-150 SM cycles whatever N is up to
+//    128 and however many independent accumulators are in flight, i.e. the tensor core takes in
+//    only ~20 weights per cycle as the 128-row A operand, where HBM delivers ~45 per cycle per
+//    SM; mma.m16n8k16 with the weights as the 16-row A operand takes in ~59 per cycle at 16 rows
+//    (microbenchmarks, 2026-12-02). The same consumers are the right shape once x has 128+ rows.
 // Every mbarrier wait is time-bounded (a failed wait records an error in the device status word
 // and the kernel drains without further waits on other agents).
 #include <algorithm>
@@ -58,14 +69,15 @@ constexpr int WARP_TMA = NWC;           // the producer warp
 constexpr int NWE = 4;                  // epilogue warps
 constexpr int WARP_EPI = NWC + 1;
 constexpr int NTHR = (NWC + 1 + NWE) * 32;
+constexpr int WARP_MMA = NWC + 1 + NWE;  // tcgen05 engine: the MMA-issuing warp
+constexpr int NTHR_TC = NTHR + 32;
 constexpr int NC = NWC * 32;
 constexpr int NE = NWE * 32;
 constexpr int PSTR = TN + 4;            // fp32 row stride of partial / reduced tiles
 constexpr int STG = TN * 128;           // one stage: a 128-byte-wide box of 128 rows
 constexpr int SCB = TN * 16;            // 8 groups of bf16 scales (or biases) for 128 rows
 constexpr int KBLK = 512;               // k per scale block (8 groups)
-constexpr int kTcBuf = 4;               // tcgen05 A/D buffer pairs per warpgroup, at most
-constexpr int kTcBars = 2 * kTcBuf;     // their completion barriers, two warpgroups
+constexpr int kTcBars = 16;             // tcgen05 engine barriers (A full / empty, D full / empty)
 constexpr int kXBlocks = 16;            // x staging blocks of 512 k per K slice (kslice <= 8192)
 
 template <int BITS>
@@ -117,8 +129,7 @@ __host__ __device__ inline Layout layout(int bits, int mt, int kslice, int nslot
   L.xs = off;  // row-major rows of XP bytes (mma.sync), or 8-k blocks of tc_rows rows (tcgen05)
   off += tc ? (kslice / 8) * tc_rows(mt) * 16 : rp * x_pitch(kslice);
   off = (off + 15) & ~15;
-  L.nw = off;  // the K slice of the RMSNorm weight (tcgen05 prologue)
-  if (tc) off += kslice * 2;
+  L.nw = off;  // (unused)
   L.sx = off;
   off += (kslice / 64) * rp * 4;
   off = (off + 15) & ~15;
@@ -144,209 +155,227 @@ __device__ __forceinline__ int row_perm(int g) {
   return BITS == 4 ? (((g & 3) << 1) | (g >> 2)) : (((g & 1) << 2) | (g >> 1));
 }
 
-// tcgen05 consumers (two warpgroups of 4 warps; warpgroup wg takes the groups gi = wg, wg + 2, ...
-// of every stage). Thread t of a warpgroup owns tile row t == TMEM lane t: it dequantizes its
-// row's 64 weights of a group into registers and writes them to an A buffer in tensor memory
-// (one tcgen05.st); after a warpgroup barrier one elected thread issues the group's MMAs
-// (M = 128 rows, N = the staged x rows, K = 16 per instruction; x is read by the tensor core from
-// shared memory) into a D buffer and commits them to an mbarrier. With two A/D buffer pairs the
-// thread folds group q-2's product (acc += scale*P + (bias - MAGIC*scale)*sum_k x, in fp32, in
-// issue order) while the tensor core works on group q-1. Each warpgroup pushes its k half of the
-// tile like the mma.sync partials; the owner sums them (warpgroup 0 + warpgroup 1).
-template <int BITS, int MT>
-__device__ __forceinline__ void consume_tc(const QmmParams& p, uint8_t* ring, uint8_t* sring,
-                                           uint8_t* xs, const float* sx, float* part,
-                                           uint64_t* full, uint64_t* empty, uint64_t* ready,
-                                           uint64_t* freeb, uint64_t* tcbar, uint32_t tmem,
-                                           int ntl, int nsb, int nst, int S, int SS, int cs,
-                                           int rank, bool& ok) {
-  constexpr int RP = 8 * MT;
-  constexpr int NM = MT <= 2 ? 16 : 32;            // MMA N
-  constexpr int GPS = Tr<BITS>::GPS;
+// bf16x2 helpers of the tcgen05 dequantization (round to nearest once per result)
+__device__ __forceinline__ uint32_t bf2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// the bf16 of group g of a block's 8 packed values, in both halves
+__device__ __forceinline__ uint32_t bf2_dup(uint4 v, int g) {
+  const int w = g >> 1;
+  const uint32_t x = w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
+  return __byte_perm(x, 0u, (g & 1) ? 0x3232u : 0x1010u);
+}
+
+// tcgen05 engine, dequantization warps (two warpgroups of 4). Thread t of warp w owns tile row
+// r = 32 * (w % 4) + t == TMEM lane r; warpgroup wg takes the k half wg of every stage (64 bytes
+// of the row). Per stage it loads those bytes from the ring (four conflict-free 16-byte loads
+// through the 128-byte swizzle), releases the slot, and writes the row's weights fully
+// dequantized, w = scale * q + bias rounded once to bf16 (q = (128 + q) - 128 exactly from the
+// magic-exponent extraction, then one bf16x2 FMA), into one of its two A buffers in tensor
+// memory, in the k order the staged x uses (4-bit: 0,4,1,5,2,6,3,7 inside each 8-block; 8-bit:
+// 0,2,1,3 inside each 4-block, q = lo + 16 hi exactly). The MMA warp's commit frees a buffer.
+template <int BITS>
+__device__ __forceinline__ void dequant_tc(const QmmParams& p, uint8_t* ring, uint8_t* sring,
+                                           uint64_t* full, uint64_t* empty, uint64_t* afull,
+                                           uint64_t* aempty, uint32_t tmem, int ntl, int nsb,
+                                           int S, int SS, bool& ok) {
   constexpr int SPS = Tr<BITS>::SPS;
-  constexpr int GH = GPS / 2;                      // groups per warpgroup per stage
-  constexpr float MAGIC = Tr<BITS>::MAGIC;
-  constexpr int ACOLS = BITS == 4 ? 32 : 64;       // TMEM columns of one group's A
-  // A/D buffer pairs per warpgroup. A warpgroup takes exactly 4 groups per scale block
-  // (SPS * GH == 4), so with NB dividing 4 the buffer of every group is a compile-time index.
-  constexpr int NB = BITS == 4 ? 4 : 2;
-  static_assert(SPS * GH == 4 && 4 % NB == 0, "buffer rotation");
-  constexpr int PER = NB * ACOLS + NB * NM;        // TMEM columns per warpgroup
-  constexpr uint32_t IDESC = tcg::idesc_bf16(NM);
-  static_assert(2 * PER <= 512, "TMEM budget");
+  constexpr int GPS = Tr<BITS>::GPS;
+  constexpr int ACOLS = BITS == 4 ? 64 : 32;  // TMEM columns of a half stage (2 bf16 each)
+  constexpr uint32_t M128 = 0x43004300u;      // (128, 128) in bf16x2
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tid = threadIdx.x;
   const int wg = warp >> 2, wq = warp & 3;
-  const int row = wq * 32 + lane;                  // tile row == TMEM lane
-  const uint32_t lane_off = uint32_t(wq * 32) << 16;
-  const uint32_t ta = tmem + uint32_t(wg * PER) + lane_off;   // A buffers
-  const uint32_t td = ta + NB * ACOLS;                        // D buffers
-  const uint64_t bd0 = tcg::smem_desc(smem_u32(xs), NM * 16, 128);
-  static_assert(NB <= kTcBuf, "completion barriers per warpgroup");
-  uint64_t* mdone = tcbar + wg * kTcBuf;
+  const int row = wq * 32 + lane;
+  const uint32_t ta = tmem + (uint32_t(wq * 32) << 16) + uint32_t(wg * 2 * ACOLS);
   const uint32_t ring_a = smem_u32(ring);
   const uint32_t sring_a = smem_u32(sring);
-  const int nclus = gridDim.y;
-  int q = 0;  // groups this warpgroup has issued (continuous over tiles: barrier phases)
-
+  int g = 0, slot = 0, phase = 0, sslot = 0;
   for (int j = 0; j < ntl; ++j) {
-    float acc[RP];
-#pragma unroll
-    for (int m = 0; m < RP; ++m) acc[m] = 0.f;
-    const int q0 = q;
-    // fold state of the buffers: scale, bias - MAGIC*scale, group index (compile-time indexed)
-    float fs[NB], fc[NB];
-    int fg[NB];
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      fs[b] = 0.f;
-      fc[b] = 0.f;
-      fg[b] = 0;
-    }
-    auto fold = [&](int qq, int b) {  // b == qq % NB, a compile-time constant at every call
-      // the tensor core always finishes (its operands are local): wait even after a failure
-      mbar_wait(&mdone[b], (qq / NB) & 1, p.status, kErrWaitMma);
-      tcg::tc_fence_after();
-      float d[NM];
-      tcg::tmem_ld16(td + uint32_t(b * NM), d);
-      if (NM == 32) tcg::tmem_ld16(td + uint32_t(b * NM + 16), d + 16);
-      tcg::tmem_wait_ld();
-      const float s = fs[b], c = fc[b];
-      const float* X = sx + fg[b] * RP;
-#pragma unroll
-      for (int m = 0; m < RP; m += 4) {
-        const float4 x4 = *reinterpret_cast<const float4*>(X + m);
-        fma2(acc[m], acc[m + 1], c, c, x4.x, x4.y);
-        fma2(acc[m + 2], acc[m + 3], c, c, x4.z, x4.w);
-        fma2(acc[m], acc[m + 1], s, s, d[m], d[m + 1]);
-        fma2(acc[m + 2], acc[m + 3], s, s, d[m + 2], d[m + 3]);
-      }
-    };
-
     for (int sb = 0; sb < nsb; ++sb) {
       uint4 sv4 = make_uint4(0u, 0u, 0u, 0u), bv4 = sv4;
-#pragma unroll
-      for (int si = 0; si < SPS; ++si) {
-        const int st = sb * SPS + si;
-        const int g = j * nst + st;
-        const int slot = g % S;
-        if (ok) ok = mbar_wait(&full[slot], (g / S) & 1, p.status, kErrWaitFull);
+#pragma unroll 1
+      for (int si = 0; si < SPS; ++si, ++g) {
+        if (ok) ok = mbar_wait(&full[slot], uint32_t(phase), p.status, kErrWaitFull);
         if (si == 0) {  // this row's scales / biases of the block's 8 groups
-          const uint32_t sa = sring_a + uint32_t(((j * nsb + sb) % SS) * 2 * SCB) + uint32_t(row * 16);
+          const uint32_t sa = sring_a + uint32_t(sslot * 2 * SCB + row * 16);
           sv4 = lds128(sa);
           bv4 = lds128(sa + SCB);
+          if (++sslot == SS) sslot = 0;
         }
+        uint32_t wd[16];
         const uint32_t wrow = ring_a + uint32_t(slot * STG + row * 128);
 #pragma unroll
-        for (int gg = 0; gg < GH; ++gg) {
-          const int gi = wg + 2 * gg;          // group inside the stage
-          const int gl = st * GPS + gi;        // group inside the K slice
-          const int gb = si * GPS + gi;        // group inside the scale block
-          // this row's scale and bias of the group (word gb/2 of the block, selected by value)
-          const int wsel = gb >> 1;
-          const uint32_t sw = wsel == 0 ? sv4.x : wsel == 1 ? sv4.y : wsel == 2 ? sv4.z : sv4.w;
-          const uint32_t bw = wsel == 0 ? bv4.x : wsel == 1 ? bv4.y : wsel == 2 ? bv4.z : bv4.w;
-          const float sv = (gb & 1) ? bf16_hi(sw) : bf16_lo(sw);
-          const float cv = ((gb & 1) ? bf16_hi(bw) : bf16_lo(bw)) - MAGIC * sv;
-          const int b = (si * GH + gg) % NB;  // == q % NB (q advances by 4 per scale block)
-          // the row's packed words of the group (8 for 4-bit, 16 for 8-bit)
-          constexpr int NWD = BITS == 4 ? 8 : 16;
-          uint32_t wd[NWD];
-#pragma unroll
-          for (int h = 0; h < NWD / 4; ++h) {
-            const uint4 v = lds128(wrow + uint32_t((((NWD / 4 * gi + h) ^ (row & 7))) << 4));
-            wd[4 * h + 0] = v.x; wd[4 * h + 1] = v.y; wd[4 * h + 2] = v.z; wd[4 * h + 3] = v.w;
-          }
-          // buffer b held group q-NB: fold it (if it belongs to this tile) before reuse
-          if (q - NB >= q0) fold(q - NB, b);
-          // dequantize into the A buffer (magic-exponent bf16, exact)
-          uint32_t r[32];
-          if (BITS == 4) {
-            // word 2u+h, nibbles e and e+4 -> column 8u + 4h + e
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-              for (int h = 0; h < 2; ++h)
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  r[8 * u + 4 * h + e] = lop3_and_or(wd[2 * u + h] >> (4 * e), 0x000F000Fu, 0x43004300u);
-            tcg::tmem_st32(ta + uint32_t(b * ACOLS), r);
-          } else {
-            // word 4u+h -> columns 8u + 2h, +1 of the low plane, then of the high plane
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                r[8 * u + 2 * h] = lop3_and_or(wd[4 * u + h], 0x000F000Fu, 0x43004300u);
-                r[8 * u + 2 * h + 1] = lop3_and_or(wd[4 * u + h] >> 8, 0x000F000Fu, 0x43004300u);
-              }
-            tcg::tmem_st32(ta + uint32_t(b * ACOLS), r);
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                r[8 * u + 2 * h] = lop3_and_or(wd[4 * u + h] >> 1, 0x00780078u, 0x43804380u);
-                r[8 * u + 2 * h + 1] = lop3_and_or(wd[4 * u + h] >> 9, 0x00780078u, 0x43804380u);
-              }
-            tcg::tmem_st32(ta + uint32_t(b * ACOLS + 32), r);
-          }
-          tcg::tmem_wait_st();
-          tcg::tc_fence_before();
-          asm volatile("bar.sync %0, 128;" ::"r"(3 + wg));
-          if (wq == 0) {
-            if (tcg::elect_one()) {
-              tcg::tc_fence_after();
-              const uint32_t dd = td - lane_off + uint32_t(b * NM);
-              const uint32_t aa = ta - lane_off + uint32_t(b * ACOLS);
-#pragma unroll
-              for (int s = 0; s < 4; ++s) {
-                const uint64_t bdesc = bd0 + uint64_t((gl * 8 + 2 * s) * NM);
-                tcg::umma_ts(dd, aa + 8 * s, bdesc, IDESC, s > 0 ? 1u : 0u);
-                if (BITS == 8) tcg::umma_ts(dd, aa + 32 + 8 * s, bdesc, IDESC, 1u);
-              }
-              tcg::umma_commit(&mdone[b]);
-            }
-            __syncwarp();
-          }
-          fs[b] = sv;
-          fc[b] = cv;
-          fg[b] = gl;
-          ++q;
+        for (int h = 0; h < 4; ++h) {
+          const uint4 v = lds128(wrow + uint32_t(((4 * wg + h) ^ (row & 7)) << 4));
+          wd[4 * h + 0] = v.x; wd[4 * h + 1] = v.y; wd[4 * h + 2] = v.z; wd[4 * h + 3] = v.w;
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (lane == 0) mbar_arrive(&empty[slot]);  // the stage's bytes are in registers
+        if (++slot == S) {
+          slot = 0;
+          phase ^= 1;
+        }
+        const int ab = g & 1;
+        // the MMAs that read buffer ab two stages ago are done
+        if (g >= 2 && ok)
+          ok = mbar_wait(&aempty[wg * 2 + ab], uint32_t(((g - 2) >> 1) & 1), p.status, kErrWaitMma);
+        tcg::tc_fence_after();
+        const uint32_t dst = ta + uint32_t(ab * ACOLS);
+        uint32_t r[32];
+        if (BITS == 4) {
+          // two groups of 8 words; word u, nibbles e and e + 4 -> column 4u + e
+#pragma unroll
+          for (int gg = 0; gg < 2; ++gg) {
+            const int gb = si * GPS + wg * 2 + gg;  // group inside the scale block
+            const uint32_t s2 = bf2_dup(sv4, gb), b2 = bf2_dup(bv4, gb);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint32_t m = lop3_and_or(wd[8 * gg + u] >> (4 * e), 0x000F000Fu, M128);
+                r[4 * u + e] = bf2_fma(bf2_sub(m, M128), s2, b2);
+              }
+            tcg::tmem_st32(dst + uint32_t(32 * gg), r);
+          }
+        } else {
+          // one group of 16 words; word u -> columns 2u (k 0, 2) and 2u + 1 (k 1, 3)
+          const int gb = si * GPS + wg;
+          const uint32_t s2 = bf2_dup(sv4, gb), b2 = bf2_dup(bv4, gb);
+          constexpr uint32_t SIXTEEN = 0x41804180u;  // (16, 16)
+#pragma unroll
+          for (int u = 0; u < 16; ++u)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const uint32_t x = wd[u] >> (8 * e);
+              const uint32_t lo = bf2_sub(lop3_and_or(x, 0x000F000Fu, M128), M128);
+              const uint32_t hi = bf2_sub(lop3_and_or(x >> 4, 0x000F000Fu, M128), M128);
+              r[2 * u + e] = bf2_fma(bf2_fma(hi, SIXTEEN, lo), s2, b2);
+            }
+          tcg::tmem_st32(dst, r);
+        }
+        tcg::tmem_wait_st();
+        tcg::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[wg * 2 + ab]);
       }
     }
-    // the tile's last groups (q is a multiple of 4 here, so group q - NB + i sits in buffer i)
-#pragma unroll
-    for (int i = 0; i < NB; ++i)
-      if (q - NB + i >= q0) fold(q - NB + i, i);
-
-    // ---- push this warpgroup's k half of partial tile j into receive buffer j & 1 of each
-    // row's owner (m % cs), slot [rank][wg][m / cs]
-    const int pbuf = j & 1;
-    const int ro = owned_rows(RP, cs);
-    if (j == 0 && cs > 1) cluster_wait();  // peers' buffers and barriers exist
-    // the owners' buffer pbuf last held tile j-2: every owner must be done reading it
-    if (j >= 2 && ok)
-      ok = mbar_wait_cluster(&freeb[pbuf], ((j - 2) >> 1) & 1, p.status, kErrWaitCluster);
-    const uint32_t pa = smem_u32(part + ((pbuf * cs + rank) * 2 + wg) * ro * PSTR);
-    const uint32_t rb = smem_u32(&ready[pbuf]);
-#pragma unroll
-    for (int m = 0; m < RP; ++m) {
-      const int owner = m % cs, ml = m / cs;
-      const uint32_t a = pa + uint32_t((ml * PSTR + row) * 4);
-      if (owner == rank)
-        asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(acc[m]) : "memory");
-      else
-        st_async_f32(mapa_shared(a, owner), acc[m], mapa_shared(rb, owner));
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&ready[pbuf]);  // this warp's local rows are in place
-    (void)nclus;
-    (void)tid;
   }
-  if (ntl == 0 && cs > 1) cluster_wait();
+}
+
+// tcgen05 engine, MMA warp (one elected thread): per stage, once both warpgroups' A buffers are
+// written, the stage's MMAs (M = 128 tile rows from tensor memory, N = NM staged x rows from
+// shared memory, K = 16 each) accumulate into the tile's D buffer; a commit per buffer frees it
+// for the dequantization warps, and a commit at the tile's end hands D to the epilogue warps.
+// D is double-buffered, so tile j + 1 accumulates while tile j is read out. The first tile also
+// waits until the epilogue warps have staged each 512-k block of x.
+template <int BITS, int NM>
+__device__ __forceinline__ void mma_tc(const QmmParams& p, uint8_t* xs, uint64_t* afull,
+                                       uint64_t* aempty, uint64_t* dfull, uint64_t* dempty,
+                                       uint64_t* xrdy, uint64_t* mfin, uint32_t tmem, int ntl,
+                                       int nst, bool& ok) {
+  constexpr int KB = Tr<BITS>::KB;
+  constexpr int ACOLS = BITS == 4 ? 64 : 32;
+  constexpr int MPH = ACOLS / 8;  // MMAs per half stage
+  constexpr uint32_t IDESC = tcg::idesc_bf16(NM);
+  constexpr uint32_t DCOL = 4 * ACOLS;  // D buffers after the four A buffers
+  if (tcg::elect_one()) {
+    const uint64_t bd0 = tcg::smem_desc(smem_u32(xs), NM * 16, 128);
+    int g = 0;
+    bool issued = false;
+    for (int j = 0; j < ntl && ok; ++j) {
+      const int db = j & 1;
+      if (j >= 2) ok = mbar_wait(&dempty[db], uint32_t(((j - 2) >> 1) & 1), p.status, kErrWaitMma);
+      tcg::tc_fence_after();
+      const uint32_t dd = tmem + DCOL + uint32_t(db * NM);
+      for (int st = 0; st < nst && ok; ++st, ++g) {
+        if (j == 0 && (st * KB) % KBLK == 0)
+          ok = mbar_wait(&xrdy[(st * KB) / KBLK], 0, p.status, kErrWaitFull);
+        const int ab = g & 1;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (ok) ok = mbar_wait(&afull[h * 2 + ab], uint32_t((g >> 1) & 1), p.status, kErrWaitMma);
+          if (!ok) break;
+          tcg::tc_fence_after();
+          const uint32_t aa = tmem + uint32_t((h * 2 + ab) * ACOLS);
+#pragma unroll
+          for (int s = 0; s < MPH; ++s) {
+            const int kk = st * KB + h * (KB / 2) + 16 * s;
+            tcg::umma_ts(dd, aa + uint32_t(8 * s), bd0 + uint64_t((kk / 8) * NM), IDESC,
+                         (st | h | s) ? 1u : 0u);
+          }
+          tcg::umma_commit(&aempty[h * 2 + ab]);
+          issued = true;
+        }
+      }
+      if (ok) tcg::umma_commit(&dfull[db]);
+    }
+    // no MMA may still write tensor memory when the CTA releases it
+    if (issued) {
+      tcg::umma_commit(mfin);
+      mbar_wait(mfin, 0, p.status, kErrWaitMma);
+    }
+  }
+  __syncwarp();
+}
+
+// Stage k block kb of x for the tcgen05 engine: like stage_block, but every chunk lands in the
+// K-major canonical layout the MMA reads (8-k block c of row m at (c * NM + m) * 16), rows
+// M .. NM - 1 are zero-filled, and no group sums are kept (the weights arrive dequantized).
+template <int BITS, int NM, int U>
+__device__ __forceinline__ void stage_block_tc(const QmmParams& p, uint8_t* xs, const float* rsm,
+                                               bool nrm, int kbase, int kb, int t) {
+  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+  const int c = kb * 64 + (t & 63);
+  const int k = kbase + c * 8;
+  const int xseg = int(p.x_seg);
+  int seg = 0, off = k;
+  if (xseg) {
+    seg = off / xseg;
+    off -= seg * xseg;
+  }
+  const bf16* col = p.x + long(seg) * p.x_segstride + off;
+  const uint4 w = nrm ? ldg_v4(p.norm_w + k) : z4;
+  const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w);
+  for (int m0 = t >> 6; m0 < NM; m0 += 2 * U) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      v[u] = m0 + 2 * u < p.M ? ldcg_v4(col + (size_t)(m0 + 2 * u) * p.ldx) : z4;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int m = m0 + 2 * u;
+      if (m >= NM) break;
+      uint4 vv = v[u];
+      uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
+      if (nrm && m < p.M) {
+        const float r = rsm[m];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
+                              bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
+      }
+      uint4 o;
+      if (BITS == 4) {
+        o.x = __byte_perm(vv.x, vv.z, 0x5410);
+        o.y = __byte_perm(vv.x, vv.z, 0x7632);
+        o.z = __byte_perm(vv.y, vv.w, 0x5410);
+        o.w = __byte_perm(vv.y, vv.w, 0x7632);
+      } else {
+        o.x = __byte_perm(vv.x, vv.y, 0x5410);
+        o.y = __byte_perm(vv.x, vv.y, 0x7632);
+        o.z = __byte_perm(vv.z, vv.w, 0x5410);
+        o.w = __byte_perm(vv.z, vv.w, 0x7632);
+      }
+      *reinterpret_cast<uint4*>(xs + (size_t(c) * NM + m) * 16) = o;
+    }
+  }
 }
 
 // rs[m] = rsqrt(mean of x_m^2 + eps) for rows m = m0, m0 + mstep, ... from the sums of squares
@@ -446,7 +475,7 @@ __device__ __forceinline__ void stage_block(const QmmParams& p, uint8_t* xs, int
 }
 
 template <int BITS, int MT, int EPI, bool TC, bool PEER = false>
-__global__ void __launch_bounds__(NTHR, 1)
+__global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
     qmm_st_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                   const __grid_constant__ CUtensorMap bmap, const QmmParams p) {
   constexpr int RP = 8 * MT;
@@ -473,9 +502,13 @@ __global__ void __launch_bounds__(NTHR, 1)
   uint64_t* ready = empty + S;   // [2] every local warp and every peer's bytes of a partial tile
   uint64_t* freeb = ready + 2;   // [2] every cluster CTA finished reading this CTA's partial
   uint64_t* xrdy = freeb + 2;    // [kXBlocks] k block b of the x slice is staged
-  uint64_t* tcbar = xrdy + kXBlocks;  // [2 warpgroups][kTcBuf buffers] tcgen05 MMA completion
+  uint64_t* tcbar = xrdy + kXBlocks;  // tcgen05 engine:
+  uint64_t* afull = tcbar;            // [2 warpgroups][2] A buffer written (4 warp arrivals)
+  uint64_t* aempty = tcbar + 4;       // [2][2] the MMAs reading it are done (commit)
+  uint64_t* dfull = tcbar + 8;        // [2] the tile's D is complete (commit)
+  uint64_t* dempty = tcbar + 10;      // [2] the epilogue warps have read D (NWE arrivals)
+  uint64_t* mfin = tcbar + 12;        // the MMA warp's last commit
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tcbar + kTcBars);
-  uint8_t* nws = smem + Lo.nw;
 
   const int cs = p.cs;
   const int rank = blockIdx.x;
@@ -501,12 +534,17 @@ __global__ void __launch_bounds__(NTHR, 1)
       mbar_init(&empty[s], NWC);
     }
     for (int i = 0; i < 2; ++i) {
-      // the owner's expect-tx arrive (peers' st.async bytes) + one arrive per local consumer warp
-      mbar_init(&ready[i], 1 + NWC);
+      // the owner's expect-tx arrive (peers' st.async bytes) + one arrive per local warp that
+      // stores partial rows (the consumers, or with tcgen05 the epilogue warps reading D)
+      mbar_init(&ready[i], 1 + (TC ? NWE : NWC));
       mbar_init(&freeb[i], cs);
     }
     for (int i = 0; i < kXBlocks; ++i) mbar_init(&xrdy[i], 1);
     for (int i = 0; i < kTcBars; ++i) mbar_init(&tcbar[i], 1);
+    if (TC) {
+      for (int i = 0; i < 4; ++i) mbar_init(&afull[i], 4);
+      for (int i = 0; i < 2; ++i) mbar_init(&dempty[i], NWE);
+    }
     fence_mbar_init();
   }
   if constexpr (TC) {
@@ -557,103 +595,28 @@ __global__ void __launch_bounds__(NTHR, 1)
     }
     __syncwarp();
     if (cs > 1) cluster_wait();
+  } else if (TC && warp < NWC) {
+    // ------------------------------------------------------------- tcgen05: dequantization
+    dequant_tc<BITS>(p, ring, sring, full, empty, afull, aempty, *tmem_slot, ntl, nsb, S, SS, ok);
+    if (cs > 1) cluster_wait();
+  } else if (TC && warp == WARP_MMA) {
+    // ------------------------------------------------------------- tcgen05: MMA issue
+    mma_tc<BITS, (MT <= 2 ? 16 : 32)>(p, xs, afull, aempty, dfull, dempty, xrdy, mfin, *tmem_slot,
+                                      ntl, nst, ok);
+    if (cs > 1) cluster_wait();
   } else if (warp < NWC) {
-    // ------------------------------------------------------------- consumer warps
-    const bool nrm = p.norm_w != nullptr;
+    // ------------------------------------------------------------- consumer warps (mma.sync)
     const int chunks = p.kslice / 8;
-    const int vchunks = kvalid / 8;
-    constexpr int NMX = TC ? (MT <= 2 ? 16 : 32) : RP;  // staged x rows
-    // x chunk (row m, 8-k block c): row-major for the mma.sync consumers, 8-k blocks of NMX rows
-    // (the UMMA K-major canonical layout) for the tcgen05 consumers
-    auto xoff = [&](int m, int c) { return TC ? (c * NMX + m) * 16 : m * XP + c * 16; };
-    for (int idx = tid; idx < (NMX - p.M) * chunks; idx += NC) {
+    for (int idx = tid; idx < (RP - p.M) * chunks; idx += NC) {
       const int m = p.M + idx / chunks, c = idx % chunks;
-      *reinterpret_cast<uint4*>(xs + xoff(m, c)) = make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(xs + m * XP + c * 16) = make_uint4(0u, 0u, 0u, 0u);
     }
     for (int idx = tid; idx < (RP - p.M) * (kvalid / 64); idx += NC) {
       const int g = idx / (RP - p.M), m = p.M + idx % (RP - p.M);
       sx[g * RP + m] = 0.f;
     }
-    // one 8-k chunk (row m, chunk c): apply the norm (x * rs * w rounded to bf16), permute k
-    // inside each 8-block (4-bit: 0,4,1,5,2,6,3,7) or 4-block (8-bit: 0,2,1,3) as the magic
-    // extraction orders the weights, store it, and return its sum
-    auto stage_chunk = [&](uint4 vv, uint4 w, int m, int c) -> float {
-      if (nrm) {
-        const float r = rsm[m];
-        uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
-        const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w);
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
-                              bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
-      }
-      const float sum = (bf16_lo(vv.x) + bf16_hi(vv.x)) + (bf16_lo(vv.y) + bf16_hi(vv.y)) +
-                        (bf16_lo(vv.z) + bf16_hi(vv.z)) + (bf16_lo(vv.w) + bf16_hi(vv.w));
-      uint4 o;
-      if (BITS == 4) {
-        o.x = __byte_perm(vv.x, vv.z, 0x5410);
-        o.y = __byte_perm(vv.x, vv.z, 0x7632);
-        o.z = __byte_perm(vv.y, vv.w, 0x5410);
-        o.w = __byte_perm(vv.y, vv.w, 0x7632);
-      } else {
-        o.x = __byte_perm(vv.x, vv.y, 0x5410);
-        o.y = __byte_perm(vv.x, vv.y, 0x7632);
-        o.z = __byte_perm(vv.z, vv.w, 0x5410);
-        o.w = __byte_perm(vv.z, vv.w, 0x7632);
-      }
-      *reinterpret_cast<uint4*>(xs + xoff(m, c)) = o;
-      return sum;
-    };
-    // the 8 chunks of a group of 64 sit on 8 consecutive lanes (chunk counts are multiples of
-    // 64) and their sums reduce by shuffles in a fixed order
-    auto group_sum = [&](float part, bool live, int m, int c) {
-      part += __shfl_xor_sync(0xffffffffu, part, 1);
-      part += __shfl_xor_sync(0xffffffffu, part, 2);
-      part += __shfl_xor_sync(0xffffffffu, part, 4);
-      if (live && (c & 7) == 0) sx[(c >> 3) * RP + m] = part;
-    };
-    if constexpr (!TC) {
-      // the epilogue warps stage x block by block (xrdy); the first tile waits for each block
-    } else {
-      pdl_wait();  // x (and the RMSNorm statistics) come from the previous kernel
-      if (nrm) norm_stats(p, rsm, RP, warp, NWC, lane);
-      // 16-byte copies straight into the canonical places, all in flight at once, then the
-      // same norm / permute / group-sum pass in place
-      const uint32_t xa0 = smem_u32(xs);
-      for (int idx = tid; idx < p.M * vchunks; idx += NC) {
-        const int m = idx / vchunks, c = idx - m * vchunks;
-        const int k = kbase + c * 8;
-        const int xseg = int(p.x_seg);
-        const int seg = xseg ? k / xseg : 0;
-        const bf16* src = p.x + seg * p.x_segstride + (size_t)m * p.ldx + (k - seg * xseg);
-        cp_async_16_zfill(xa0 + uint32_t(xoff(m, c)), src, true);
-      }
-      if (nrm)
-        for (int c = tid; c < vchunks; c += NC)
-          cp_async_16_zfill(smem_u32(nws) + uint32_t(c * 16), p.norm_w + kbase + c * 8, true);
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      asm volatile("cp.async.wait_all;" ::: "memory");
-      asm volatile("bar.sync 1, %0;" ::"n"(NC));
-      for (int base = 0; base < p.M * vchunks; base += NC) {
-        const int idx = base + tid;
-        const bool live = idx < p.M * vchunks;
-        const int m = live ? idx / vchunks : 0, c = live ? idx - m * vchunks : 0;
-        float part = 0.f;
-        if (live)
-          part = stage_chunk(*reinterpret_cast<const uint4*>(xs + xoff(m, c)),
-                             nrm ? *reinterpret_cast<const uint4*>(nws + c * 16)
-                                 : make_uint4(0u, 0u, 0u, 0u),
-                             m, c);
-        group_sum(part, live, m, c);
-      }
-    }
-    if constexpr (TC) fence_proxy_async_smem();  // x becomes the tensor core's B operand
+    // the epilogue warps stage x block by block (xrdy); the first tile waits for each block
     asm volatile("bar.sync 1, %0;" ::"n"(NC));
-
-    if constexpr (TC) {
-      consume_tc<BITS, MT>(p, ring, sring, xs, sx, part, full, empty, ready, freeb, tcbar,
-                           *tmem_slot, ntl, nsb, nst, S, SS, cs, rank, ok);
-    } else {
 
     // Warp w owns 32 tile rows (two 16-row MMA groups sharing one set of x fragments) and one
     // k half of every stage (GH of its GPS groups); the two halves are summed at the tile end.
@@ -847,12 +810,11 @@ __global__ void __launch_bounds__(NTHR, 1)
       if (lane == 0) mbar_arrive(&ready[pbuf]);  // this warp's local rows are in place
     }
     if (ntl == 0 && cs > 1) cluster_wait();
-    }  // mma.sync consumers
   } else {
     // ------------------------------------------------------------- epilogue warps
     pdl_wait();  // x, the statistics and the epilogues' buffers come from earlier kernels
     const int etid = tid - WARP_EPI * 32;
-    if constexpr (!TC) {
+    {
       // idle until the first tile ends: stage x for the consumers, 512 k at a time, releasing
       // each block as it lands so that the first tile's compute overlaps the rest
       if (PEER && p.wait_flag != nullptr) {  // x gathered by the producers' peer stores
@@ -867,7 +829,12 @@ __global__ void __launch_bounds__(NTHR, 1)
         asm volatile("bar.sync 2, %0;" ::"n"(NE));  // rs of every row
       }
       for (int kb = 0; kb < kvalid / KBLK; ++kb) {
-        stage_block<BITS, RP, MT == 4 ? 4 : 8>(p, xs, XP, sx, rsm, nrm, kbase, kb, etid);
+        if constexpr (TC) {
+          stage_block_tc<BITS, (MT <= 2 ? 16 : 32), 4>(p, xs, rsm, nrm, kbase, kb, etid);
+          fence_proxy_async_smem();  // the block becomes the tensor core's B operand
+        } else {
+          stage_block<BITS, RP, MT == 4 ? 4 : 8>(p, xs, XP, sx, rsm, nrm, kbase, kb, etid);
+        }
         asm volatile("bar.sync 2, %0;" ::"n"(NE));  // the block's chunks and sums are stored
         if (etid == 0) mbar_arrive(&xrdy[kb]);
       }
@@ -875,10 +842,11 @@ __global__ void __launch_bounds__(NTHR, 1)
     if (cs > 1) cluster_wait();  // peers' barriers exist before the first remote arrive
     const int ro = owned_rows(RP, cs);
     const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
-    // bytes each peer pushes into this CTA per tile: its 2 k halves of the RP / cs rows
-    // m = rank + i*cs this CTA owns (all RP rows are pushed, padding included)
+    // bytes each peer pushes into this CTA per tile: its 2 k halves (one D with tcgen05) of the
+    // RP / cs rows m = rank + i*cs this CTA owns (all RP rows are pushed, padding included)
     const int nown = RP > rank ? (RP - rank + cs - 1) / cs : 0;
-    const uint32_t peer_bytes = uint32_t((cs - 1) * nown * 2 * TN * 4);
+    constexpr int NHALF = TC ? 1 : 2;
+    const uint32_t peer_bytes = uint32_t((cs - 1) * nown * NHALF * TN * 4);
     for (int j = 0; j < ntl; ++j) {
       const int pbuf = j & 1;
       const int t = int(blockIdx.y) + j * nclus;
@@ -886,6 +854,38 @@ __global__ void __launch_bounds__(NTHR, 1)
       // the residual of this tile comes from an earlier kernel: load it before the wait
       uint32_t pre[2 * kResidRows];
       if constexpr (EPI == EPI_RESID) resid_prefetch<TN>(p, rank, cs, t * TN, NWE, WARP_EPI, pre);
+      if constexpr (TC) {
+        // read the tile's D (this warp's 32 lanes: tile rows 32 * (warp % 4) + lane, one column
+        // per x row), free it for tile j + 2, and push its rows to their owners like the
+        // mma.sync consumers push their partials (slot [rank][0][m / cs] of owner m % cs)
+        constexpr int NM = MT <= 2 ? 16 : 32;
+        const int wq = warp & 3, row = wq * 32 + lane;
+        const uint32_t dcol = uint32_t(4 * (BITS == 4 ? 64 : 32) + pbuf * NM);
+        float d[NM];
+        if (ok) ok = mbar_wait(&dfull[pbuf], uint32_t((j >> 1) & 1), p.status, kErrWaitMma);
+        tcg::tc_fence_after();
+        tcg::tmem_ld16(*tmem_slot + (uint32_t(wq * 32) << 16) + dcol, d);
+        if (NM == 32) tcg::tmem_ld16(*tmem_slot + (uint32_t(wq * 32) << 16) + dcol + 16, d + 16);
+        tcg::tmem_wait_ld();
+        tcg::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dempty[pbuf]);
+        if (j >= 2 && ok)
+          ok = mbar_wait_cluster(&freeb[pbuf], ((j - 2) >> 1) & 1, p.status, kErrWaitCluster);
+        const uint32_t pa = smem_u32(part + (pbuf * cs + rank) * 2 * ro * PSTR);
+        const uint32_t rb = smem_u32(&ready[pbuf]);
+#pragma unroll
+        for (int m = 0; m < RP; ++m) {
+          const int owner = m % cs, ml = m / cs;
+          const uint32_t a = pa + uint32_t((ml * PSTR + row) * 4);
+          if (owner == rank)
+            asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(d[m]) : "memory");
+          else
+            st_async_f32(mapa_shared(a, owner), d[m], mapa_shared(rb, owner));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[pbuf]);  // this warp's local rows are in place
+      }
       if (etid == 0) mbar_arrive_expect_tx(&ready[pbuf], peer_bytes);
       if (ok) ok = mbar_wait_cluster(&ready[pbuf], (j >> 1) & 1, p.status, kErrWaitCluster);
       // sum the partials of each owned row: the two k halves of each rank, then the ranks in
@@ -896,8 +896,9 @@ __global__ void __launch_bounds__(NTHR, 1)
         float4 s;
         for (int c = 0; c < cs; ++c) {
           const float4 h0 = *reinterpret_cast<const float4*>(&pb[((c * 2) * ro + mi) * PSTR + n4 * 4]);
-          const float4 h1 = *reinterpret_cast<const float4*>(&pb[((c * 2 + 1) * ro + mi) * PSTR + n4 * 4]);
-          const float4 v = make_float4(h0.x + h1.x, h0.y + h1.y, h0.z + h1.z, h0.w + h1.w);
+          const float4 h1 = TC ? make_float4(0.f, 0.f, 0.f, 0.f)
+                               : *reinterpret_cast<const float4*>(&pb[((c * 2 + 1) * ro + mi) * PSTR + n4 * 4]);
+          const float4 v = TC ? h0 : make_float4(h0.x + h1.x, h0.y + h1.y, h0.z + h1.z, h0.w + h1.w);
           if (c == 0) {
             s = v;
           } else {
@@ -1034,7 +1035,8 @@ static int launch_st(const QmmParams& p, const QmmPlan& pl, cudaStream_t stream)
   const int ntiles = (p.N + st::TN - 1) / st::TN;
   int nclus = pl.clusters > 0 ? pl.clusters : sm_count(current_device()) / pl.cs;
   nclus = std::max(1, std::min(nclus, ntiles));
-  DSPARK_CUDA_TRY(launch_ex(kern, dim3(pl.cs, nclus), dim3(st::NTHR), (size_t)smem, stream, pl.cs,
+  DSPARK_CUDA_TRY(launch_ex(kern, dim3(pl.cs, nclus), dim3(TC ? st::NTHR_TC : st::NTHR),
+                            (size_t)smem, stream, pl.cs,
                             true, wmap, smap, bmap, p),
                   "qmm_st: launch");
   return DSPARK_OK;
