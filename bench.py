@@ -23,6 +23,13 @@ Multi-GPU (torchrun, one process per GPU): each rank runs independent requests o
 replica of the weights (data-parallel requests, no collective in the timed work): weak
 scaling. ``--impl reference`` times the reference arm: the CPU restatement of the path (the
 reference itself is MLX/Metal-only and cannot run here) on rank 0.
+
+The line also carries, at the same N, the two other multi-GPU configurations: ``tp``
+(configs[3]: the Qwen3-32B-shaped 8-bit target at 32k context with every projection
+column-sharded over the N ranks and NCCL all-gathers between them, strong scaling; with the
+per-GPU HBM fraction and one layer's gathers timed alone) and ``batch`` (configs[4]: 256
+requests of the continuous-batching engine partitioned data-parallel over the N ranks). Each
+is its own device-timed measurement (max over ranks); ``--no-extras`` skips them.
 """
 
 from __future__ import annotations
@@ -52,6 +59,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip e2e/roofline extras")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the tensor-parallel and batch-engine measurements of the line")
     ap.add_argument("--micro", choices=["qmm", "attn"], default=None,
                     help="run one kernel's microbench alone (ncu small cases)")
     ap.add_argument("--rows", type=int, nargs="+", default=[1, 4, 8, 16])
@@ -71,9 +80,9 @@ def parse():
     ap.add_argument("--tp-comm", choices=["fused", "p2p", "nccl"], default="nccl",
                     help="--tp gathers: fused into the projections' peer stores, separate "
                          "peer-memory launches (dspark_p2p_allgather), or NCCL")
-    ap.add_argument("--batch-requests", type=int, default=64,
-                    help="requests in the whole job (256 in configs[4]; the KV of 256 "
-                         "requests is ~147 GB, so N=1 runs a sample)")
+    ap.add_argument("--batch-requests", type=int, default=256,
+                    help="requests in the whole job (256 in configs[4]; their KV is ~151 GB, "
+                         "split over the ranks)")
     return ap.parse_args()
 
 
@@ -266,13 +275,7 @@ def run_ours(args):
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+    group = _dist_setup(world, dev)
     import mlx_dspark_b200  # noqa: F401
     from mlx_dspark_b200 import _lib
     from mlx_dspark_b200.target import QWEN3_8B, Target, VerifyGraph
@@ -360,6 +363,13 @@ def run_ours(args):
         except Exception as e:  # noqa: BLE001 — the baseline must not sink the bench line
             out["cpu_baseline"] = {"value": None, "error": f"{type(e).__name__}: {e}"}
     vg.graph = None
+    if not args.quick and not args.no_extras:
+        # the other two multi-GPU configurations, at this job's N: tensor parallelism (configs[3],
+        # strong scaling) and the data-parallel batch engine; every rank runs both
+        del vg, t
+        torch.cuda.empty_cache()
+        out["tp"] = tp_measure(8, 3, world, rank, dev, group)
+        out["batch"] = batch_measure(256, 6, 2, world, rank, dev)
     if world > 1:
         import torch.distributed as dist
 
@@ -554,36 +564,36 @@ def run_micro(args):
                       "device_status": _lib.device_status(0)}), flush=True)
 
 
-def run_batch(args):
-    """BASELINE configs[4] at this job's scale: ``--batch-requests`` requests (prompt lengths
-    log-uniform 256-16k, seeded) placed data-parallel over the ranks by summed KV length; each
-    step every request verifies a block of U{8..16} rows and keeps a seeded accept length
-    U{0..block-1} (random-init weights never accept a random draft). Value = committed tokens
-    per second over the whole job (sum of accepted + 1), device-timed, max over ranks."""
-    import numpy as np
-    import torch
-
-    from mlx_dspark_b200.batch_engine import SpecBatch, partition_requests
-    from mlx_dspark_b200.target import QWEN3_8B, Target
-
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+def _dist_setup(world: int, dev, timeout_s: int = 300):
     if world > 1:
         import datetime
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    import mlx_dspark_b200  # noqa: F401
-    from mlx_dspark_b200 import _lib
+        if not dist.is_initialized():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s),
+                                    device_id=dev)
+        return dist.group.WORLD
+    return None
 
-    _lib.ensure_init(local)
+
+def batch_measure(n_req: int, steps: int, warmup: int, world: int, rank: int, dev) -> dict:
+    """``n_req`` requests (prompt lengths log-uniform 256-16k, seeded)
+    placed data-parallel over the ranks by summed KV length (no collective in the data path);
+    each step every request verifies a block of U{8..16} rows and keeps a seeded accept length
+    U{0..block-1} (random-init weights never accept a random draft). Value = committed tokens
+    per second over the whole job (sum of accepted + 1), device-timed, max over ranks."""
+    import numpy as np
+    import torch
+
+    from mlx_dspark_b200 import _lib
+    from mlx_dspark_b200.batch_engine import SpecBatch, partition_requests
+    from mlx_dspark_b200.target import QWEN3_8B, Target
+
     rng = np.random.default_rng(2024)
-    n_req = int(args.batch_requests)
     lengths = [int(x) for x in np.exp(rng.uniform(np.log(256), np.log(16384), n_req))]
     mine = partition_requests(lengths, world)[rank]
-    total = args.warmup + args.steps
+    total = warmup + steps
     my_len = [lengths[i] for i in mine]
     caps = [L + 17 * (total + 1) for L in my_len]
     B = len(mine)
@@ -603,23 +613,27 @@ def run_batch(args):
     drafts = torch.randint(0, QWEN3_8B.vocab, (total, B, 16), device=dev, dtype=torch.int32,
                            generator=g)
     acc_dev = torch.from_numpy(accs.astype(np.int32)).to(dev)
+    launches0 = int(_lib.lib.dspark_launch_count())
 
     def step(i):
         eng.step(drafts[i], [int(x) for x in blocks[i]], forced_accept=acc_dev[i])
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
     barrier(world)
+    l0 = int(_lib.lib.dspark_launch_count())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(args.warmup, total):
+    for i in range(warmup, total):
         step(i)
     e1.record()
     torch.cuda.synchronize()
+    launches = int(_lib.lib.dspark_launch_count()) - l0
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
-    committed = float((accs[args.warmup :] + 1).sum())
-    rows = float(blocks[args.warmup :].sum())
+    committed = float((accs[warmup:] + 1).sum())
+    rows = float(blocks[warmup:].sum())
+    kv_bytes = 2 * QWEN3_8B.n_layers * QWEN3_8B.n_kv_heads * QWEN3_8B.head_dim * 2 * sum(my_len)
     if world > 1:
         import torch.distributed as dist
 
@@ -627,20 +641,37 @@ def run_batch(args):
         dist.all_reduce(tot)
         committed, rows = float(tot[0]), float(tot[1])
     secs = ms / 1e3
-    kv_bytes = 2 * QWEN3_8B.n_layers * QWEN3_8B.n_kv_heads * QWEN3_8B.head_dim * 2 * sum(my_len)
-    out = {"metric": "batch-engine committed tok/s (Qwen3-8B 4-bit, continuous batching)",
-           "value": round(committed / secs, 1), "unit": "tok/s", "n_gpus": world,
-           "steps": args.steps, "warmup": args.warmup,
-           "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
-           "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-           "data": "synthetic (random-init weights, random K/V prefixes, seeded blocks/accepts)",
-           "config": {"workload": f"BASELINE configs[4] at {n_req} requests (prompts "
-                                  "log-uniform 256-16k, blocks U{8..16}, accepts U{0..block-1})",
-                      "requests": n_req, "requests_rank0": B,
-                      "parallelism": f"dp{world} (requests partitioned by KV length)"},
-           "verify_rows_per_s": round(rows / secs, 1),
-           "rank0_kv_gb": round(kv_bytes / 1e9, 2),
-           "device_status": _lib.device_status(local)}
+    st = _lib.device_status(dev.index)
+    del eng, t, drafts
+    torch.cuda.empty_cache()
+    _ = launches0
+    return {"metric": "batch-engine committed tok/s (Qwen3-8B 4-bit, continuous batching)",
+            "value": round(committed / secs, 1), "unit": "tok/s", "n_gpus": world,
+            "steps": steps, "warmup": warmup, "ms_per_step": round(ms / steps, 3),
+            "scaling": "strong",
+            "config": {"workload": f"BASELINE configs[4] at {n_req} requests (prompts "
+                                   "log-uniform 256-16k, blocks U{8..16}, accepts U{0..block-1})",
+                       "requests": n_req, "requests_rank0": B,
+                       "parallelism": f"dp{world} (requests partitioned by KV length)"},
+            "verify_rows_per_s": round(rows / secs, 1), "rank0_kv_gb": round(kv_bytes / 1e9, 2),
+            "gpu_launches_rank0": launches, "device_status": st}
+
+
+def run_batch(args):
+    """``--batch``: the batch-engine measurement alone (prints its JSON line)."""
+    import torch
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    _dist_setup(world, dev)
+    import mlx_dspark_b200  # noqa: F401
+    from mlx_dspark_b200 import _lib
+
+    _lib.ensure_init(local)
+    out = batch_measure(int(args.batch_requests), args.steps, args.warmup, world, rank, dev)
+    out.update(higher_is_better=True, vs_baseline=None, dtype="bf16",
+               data="synthetic (random-init weights, random K/V prefixes, seeded blocks/accepts)")
     if world > 1:
         import torch.distributed as dist
 
@@ -649,43 +680,30 @@ def run_batch(args):
         print(json.dumps(out), flush=True)
 
 
-def run_tp(args):
+def tp_measure(steps: int, warmup: int, world: int, rank: int, dev, group, *, context: int = 32768,
+               comm: str = "nccl") -> dict:
     """Qwen3-32B-shaped 8-bit target (64 layers, hidden 5120, GQA 64/8),
-    one request verifying 16-row blocks at 32k context, projections column-sharded over the
-    ranks with all-gathers between them (mlx_dspark_b200.target_tp; NCCL by default, the
-    fastest measured; --tp-comm fused / p2p for the peer-memory transports). A step = verify
-    forward + argmax + accept + rollback to a seeded accept length, captured in one CUDA graph
-    (collectives included). value = verified rows per second of the one request (strong
-    scaling: the same work at every N)."""
+    one request verifying 16-row blocks at ``context`` tokens, projections column-sharded over
+    the ranks with all-gathers between them (mlx_dspark_b200.target_tp; NCCL by default). A step =
+    verify forward + argmax + accept + rollback to a seeded accept length, captured in one CUDA
+    graph (collectives included). value = verified rows per second of the one request (strong
+    scaling: the same work at every N). Also: the gathers' own cost, timed with CUDA events
+    around one layer's four gathers (eager, the same buffers and sizes)."""
     import numpy as np
     import torch
 
+    from mlx_dspark_b200 import _lib
     from mlx_dspark_b200.target import QWEN3_32B
     from mlx_dspark_b200.target_tp import TPTarget
 
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    group = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-        group = dist.group.WORLD
-    import mlx_dspark_b200  # noqa: F401
-    from mlx_dspark_b200 import _lib
-
-    _lib.ensure_init(local)
-    cfg, ctx, R = QWEN3_32B, int(args.tp_context), ROWS
+    cfg, ctx, R = QWEN3_32B, int(context), ROWS
     t = TPTarget(cfg, rank, world, group=group, kv_cap=ctx + R * 18, seed=1, max_rows=R,
-                 device=dev, comm=args.tp_comm)
+                 device=dev, comm=comm)
     g = torch.Generator(device=dev).manual_seed(7)
     for L in t.layers:
         L["k_cache"][:, :ctx].normal_(generator=g)
         L["v_cache"][:, :ctx].normal_(generator=g)
-    total = args.warmup + args.steps
+    total = warmup + steps
     rng = np.random.default_rng(99)
     acc = rng.integers(0, R, total)
     ids_all = torch.randint(0, cfg.vocab, (total, R), device=dev, dtype=torch.int32, generator=g)
@@ -727,39 +745,92 @@ def run_tp(args):
         nrej.copy_(nrej_all[i : i + 1])
         graph.replay()
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(args.warmup, total):
+    for i in range(warmup, total):
         step(i)
     e1.record()
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    # one layer's four gathers (attention output, hidden pack, activations, hidden pack), eager
+    b = t.b
+    gather_us = None
+    if t.comm in ("nccl", "p2p", "local"):
+        def gathers():
+            t._gather("attn", 0, b["attn"])
+            t._gather("pack", 0, b["pack"])
+            t._gather("act", 0, b["act"])
+            t._gather("pack", 1, b["pack"])
+
+        for _ in range(3):
+            gathers()
+        torch.cuda.synchronize()
+        barrier(world)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(20):
+            gathers()
+        g1.record()
+        torch.cuda.synchronize()
+        gather_us = max_over_ranks(g0.elapsed_time(g1) * 1e3 / 20, world, dev)
     secs = ms / 1e3
     w_bytes = cfg.weight_bytes() / world
     kv_bytes = 2 * cfg.n_layers * (cfg.n_kv_heads // world) * cfg.head_dim * 2 * (ctx + 8 * R)
-    res = {"metric": "verify-block tok/s at Qwen3-32B-shaped 8-bit M=16 (32k context), "
-                     "tensor-parallel", "value": round(args.steps * R / secs, 1), "unit": "tok/s",
-           "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-           "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-           "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-           "data": "synthetic (random-init N(0,0.02) weights quantized MLX-affine 8-bit g64; "
-                   "random tokens; random bf16 KV prefix)",
-           "config": {"workload": "qwen3-32b-shape 8-bit verify, 16-row blocks at 32k context "
-                                  "(BASELINE configs[3])",
-                      "parallelism": f"tp{world} (column-sharded projections, heads per rank, "
-                                     + ("NCCL all-gathers)" if t.comm == "nccl" else
-                                        "peer-memory all-gathers)" if t.comm == "p2p" else
-                                        "gathers fused into the projections' peer stores)"
-                                        if t.comm == "fused" else "no collectives)")},
-           "per_gpu_hbm_bytes_per_step": int(w_bytes + kv_bytes),
-           "per_gpu_hbm_gbs": round((w_bytes + kv_bytes) / (ms / args.steps / 1e3) / 1e9, 1),
-           "gpu_launches": launches * args.steps, "device_status": _lib.device_status(local)}
+    pk = peaks()
+    per_gpu_gbs = (w_bytes + kv_bytes) / (ms / steps / 1e3) / 1e9
+    st = _lib.device_status(dev.index)
     del graph
     t.close()
+    del t
+    torch.cuda.empty_cache()
+    n_gathers = 4 * cfg.n_layers + 1 if world > 1 else 0
+    return {"metric": "verify-block tok/s at Qwen3-32B-shaped 8-bit M=16 (32k context), "
+                      "tensor-parallel", "value": round(steps * R / secs, 1), "unit": "tok/s",
+            "n_gpus": world, "steps": steps, "warmup": warmup,
+            "ms_per_step": round(ms / steps, 4), "scaling": "strong",
+            "config": {"workload": f"qwen3-32b-shape 8-bit verify, 16-row blocks at {ctx} "
+                                   "context (BASELINE configs[3])",
+                       "parallelism": f"tp{world} (column-sharded projections, heads per rank, "
+                                      + {"nccl": "NCCL all-gathers)",
+                                         "p2p": "peer-memory all-gathers)",
+                                         "fused": "gathers fused into the projections' peer "
+                                                  "stores)",
+                                         "local": "no collectives)"}[t_comm(world, comm)]},
+            "per_gpu_hbm_bytes_per_step": int(w_bytes + kv_bytes),
+            "per_gpu_hbm_gbs": round(per_gpu_gbs, 1),
+            "per_gpu_hbm_frac": round(per_gpu_gbs / pk["hbm_gbs"], 3),
+            "gathers_per_block": n_gathers,
+            "one_layer_gathers_us": None if gather_us is None else round(gather_us, 2),
+            "gathers_us_per_block_est": None if gather_us is None or world == 1
+            else round(gather_us * cfg.n_layers, 1),
+            "gpu_launches": launches * steps, "device_status": st}
+
+
+def t_comm(world: int, comm: str) -> str:
+    return comm if world > 1 else "local"
+
+
+def run_tp(args):
+    """``--tp``: the tensor-parallel measurement alone (prints its JSON line)."""
+    import torch
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = _dist_setup(world, dev)
+    import mlx_dspark_b200  # noqa: F401
+    from mlx_dspark_b200 import _lib
+
+    _lib.ensure_init(local)
+    res = tp_measure(args.steps, args.warmup, world, rank, dev, group,
+                     context=int(args.tp_context), comm=args.tp_comm)
+    res.update(higher_is_better=True, vs_baseline=None, dtype="bf16",
+               data="synthetic (random-init N(0,0.02) weights quantized MLX-affine 8-bit g64; "
+                    "random tokens; random bf16 KV prefix)")
     if world > 1:
         import torch.distributed as dist
 
