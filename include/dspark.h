@@ -169,14 +169,29 @@ int dspark_qmm_plan_rows(int N, int K, int bits, int rows, int out[7]);
  * row i sees keys <= L - qL + i. tree_anc (uint32 [B*qL], optional) switches to the
  * tree-verify rule: every key < L - qL, and key L - qL + j iff bit j of anc[i]
  * (src/mlx_dspark/multirow_attn.py:184-195). kv_len (device int32 [B], optional) gives a
- * per-row key count <= L. D in {64, 128}. workspace may be NULL when
- * dspark_verify_attn_workspace() returns 0 for the shape. */
+ * per-row key count <= L. D in {64, 128, 256}. bf16 tensors (dspark_verify_attn_dt takes the
+ * element type). workspace may be NULL when dspark_verify_attn_workspace() returns 0 for the
+ * shape. */
 int dspark_verify_attn(const void* q, const int64_t q_strides[3], const void* k,
                        const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
                        int B, int Hq, int Hk, int qL, int D, int L, const int32_t* kv_len,
                        float scale, int causal, const uint32_t* tree_anc, void* out,
                        const int64_t o_strides[3], void* workspace, size_t ws_bytes,
                        void* stream);
+
+/* Element types of dspark_verify_attn_dt. */
+#define DSPARK_DTYPE_BF16 0
+#define DSPARK_DTYPE_F16 1
+
+/* dspark_verify_attn for q/k/v/out of element type `dtype` (bf16 or fp16, the two input types
+ * multirow_sdpa serves, src/mlx_dspark/multirow_attn.py:304; the probabilities are rounded
+ * to that type for P.V as the reference kernel does, :136-140). Same shapes and rules. */
+int dspark_verify_attn_dt(int dtype, const void* q, const int64_t q_strides[3], const void* k,
+                          const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
+                          int B, int Hq, int Hk, int qL, int D, int L, const int32_t* kv_len,
+                          float scale, int causal, const uint32_t* tree_anc, void* out,
+                          const int64_t o_strides[3], void* workspace, size_t ws_bytes,
+                          void* stream);
 
 /* dspark_verify_attn for callers that cannot allocate device memory (no workspace argument).
  * This entry point has no counterpart in the reference: it exists for code that is being

@@ -111,6 +111,8 @@ _SIGS = {
     "dspark_qmm_plan_rows": (i32, [i32, i32, i32, i32, P_int]),
     "dspark_verify_attn": (i32, [vp, P_i64, vp, P_i64, vp, P_i64, i32, i32, i32, i32, i32, i32,
                                  vp, f32, i32, vp, vp, P_i64, vp, sz, vp]),
+    "dspark_verify_attn_dt": (i32, [i32, vp, P_i64, vp, P_i64, vp, P_i64, i32, i32, i32, i32,
+                                    i32, i32, vp, f32, i32, vp, vp, P_i64, vp, sz, vp]),
     "dspark_verify_attn_noalloc": (i32, [vp, P_i64, vp, P_i64, vp, P_i64, i32, i32, i32, i32, i32,
                                          i32, vp, f32, i32, vp, vp, P_i64, vp]),
     "dspark_verify_attn_workspace": (sz, [i32, i32, i32, i32, i32, i32]),

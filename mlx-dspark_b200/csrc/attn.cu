@@ -25,6 +25,8 @@
 #include <mutex>
 #include <tuple>
 
+#include <cuda_fp16.h>
+
 #include "attn.h"
 #include "common.cuh"
 #include "host_common.h"
@@ -32,8 +34,36 @@
 namespace dspark {
 namespace attn {
 
-constexpr int KT = 64;     // keys per stage
+constexpr int KT = 64;     // keys per stage (head_dim <= 128)
 constexpr int NSLOT = 3;   // ring depth
+
+// keys per stage: 32 for head_dim 256, so that the three-slot ring of padded K/V rows fits
+__host__ __device__ constexpr int ktile(int d) { return d > 128 ? 32 : KT; }
+
+// bf16 (or, with F16, fp16) tensor-core MMA D[16x8] += A[16x16] B[16x8] with fp32 accumulation
+template <bool F16>
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  if constexpr (F16) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    mma_bf16_16816(c, a0, a1, a2, a3, b0, b1);
+  }
+}
+
+// two fp32 values rounded to the input type (bf16 or fp16) and packed low-first
+template <bool F16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (F16) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    return pack_bf16x2(lo, hi);
+  }
+}
 
 // Workspace row of one partial: D accumulators, then m and l, padded to 16 bytes so the
 // accumulators are written with aligned 16-byte stores.
@@ -43,7 +73,7 @@ constexpr int kWsRow = D + 4;
 template <int D>
 struct AttnSmem {
   static constexpr int ROWB = D * 2 + 16;           // padded row (bank-conflict-free ldmatrix)
-  static constexpr int STG = 2 * KT * ROWB;          // K tile + V tile
+  static constexpr int STG = 2 * ktile(D) * ROWB;    // K tile + V tile
   static constexpr int RING = NSLOT * STG;
 };
 
@@ -82,15 +112,21 @@ __device__ __forceinline__ int64_t q_base(const AttnParams& p, int b, const int6
   return p.row_start ? int64_t(p.row_start[b]) * si : int64_t(b) * sb;
 }
 
-template <int D, int NRT, int KS>
-__global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnParams p) {
-  constexpr int NC = NRT * KS;
+// DS warps share each (row tile, key slot): all of them compute the scores over the whole
+// head_dim and each keeps D / DS output columns (DS = 2 for head_dim 256 bounds the registers).
+// F16: fp16 inputs and output (the MMA type and the rounding of P follow the input type).
+template <int D, int NRT, int KS, int DS, bool F16>
+__global__ void __launch_bounds__((NRT * KS * DS + 1) * 32) attn_kernel(const AttnParams p) {
+  constexpr int NC = NRT * KS * DS;
   constexpr int RPG = NRT * 16;
   constexpr int ROWB = AttnSmem<D>::ROWB;
   constexpr int STG = AttnSmem<D>::STG;
-  constexpr int KPW = KT / KS;         // keys per warp per stage (64 or 32)
+  constexpr int KTD = ktile(D);        // keys per stage
+  constexpr int KPW = KTD / KS;        // keys per warp per stage (64 or 32)
   constexpr int KB = 32;               // keys per softmax step
-  constexpr int NDT = D / 8;           // n8 tiles of the output
+  static_assert(KPW % KB == 0, "key slots of whole softmax steps");
+  constexpr int DW = D / DS;           // output columns per warp
+  constexpr int NDT = DW / 8;          // n8 tiles of the warp's output
   constexpr int NKK = D / 16;          // k16 steps of Q.K^T
 
   extern __shared__ __align__(128) uint8_t smem[];
@@ -131,7 +167,7 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
   const int split = g_grp * p.ns + sidx_c;
   const int k0 = min(Lb, split * p.chunk);
   const int kend = min(Lb, k0 + p.chunk);
-  const int nst = (kend - k0 + KT - 1) / KT;
+  const int nst = (kend - k0 + KTD - 1) / KTD;
 
   const bf16* kb_ptr = p.k + (p.kv_off ? p.kv_off[b] : int64_t(b) * p.k_sb) + int64_t(hk) * p.k_sh;
   const bf16* vb_ptr = p.v + (p.kv_off ? p.kv_off[b] : int64_t(b) * p.v_sb) + int64_t(hk) * p.v_sh;
@@ -141,8 +177,8 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
     // 16-byte cp.async copies, lanes on consecutive chunks of a row (coalesced); keys past
     // the split's end are zero-filled without a read, so masked keys always hold finite
     // values. Each lane's copies of a stage complete on full[slot] (32 arrivals).
-    constexpr int CPR = D * 2 / 16;          // 16-byte chunks per row (16 or 8)
-    constexpr int RPI = 32 / CPR;            // rows per warp instruction (2 or 4)
+    constexpr int CPR = D * 2 / 16;          // 16-byte chunks per row (32, 16 or 8)
+    constexpr int RPI = 32 / CPR;            // rows per warp instruction (1, 2 or 4)
     const int rsub = lane / CPR, ch = lane % CPR;
     const uint32_t ring_a = smem_u32(ring);
     bool ok = true;
@@ -150,17 +186,17 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
       const int slot = st % NSLOT;
       if (st >= NSLOT) ok = mbar_wait(&empty[slot], ((st / NSLOT) - 1) & 1, p.status, kErrWaitKVEmpty);
       if (!ok) break;
-      const int kt = k0 + st * KT;
+      const int kt = k0 + st * KTD;
       uint32_t dk = ring_a + slot * STG + rsub * ROWB + ch * 16;
       const bf16* kp = kb_ptr + int64_t(kt + rsub) * p.k_ss + ch * 8;
       const bf16* vp = vb_ptr + int64_t(kt + rsub) * p.v_ss + ch * 8;
       const int64_t kstep = int64_t(RPI) * p.k_ss, vstep = int64_t(RPI) * p.v_ss;
       int key = kt + rsub;
 #pragma unroll 8
-      for (int i = 0; i < KT / RPI; ++i) {
+      for (int i = 0; i < KTD / RPI; ++i) {
         const bool valid = key < kend;
         cp_async_16_zfill(dk, valid ? kp : kb_ptr, valid);
-        cp_async_16_zfill(dk + KT * ROWB, valid ? vp : vb_ptr, valid);
+        cp_async_16_zfill(dk + KTD * ROWB, valid ? vp : vb_ptr, valid);
         dk += RPI * ROWB;
         kp += kstep;
         vp += vstep;
@@ -174,7 +210,7 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ consumer warps
-    const int rt = warp % NRT, kslot = warp / NRT;
+    const int rt = warp % NRT, kslot = (warp / NRT) % KS, ds = warp / (NRT * KS);
     const int gid = lane >> 2, tig = lane & 3;
     const int r0 = rt * 16 + gid, r1 = r0 + 8;             // rows within the group
     const int pr0 = rg * RPG + r0, pr1 = rg * RPG + r1;    // packed rows
@@ -219,8 +255,8 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
       const int slot = st % NSLOT;
       if (ok) ok = mbar_wait(&full[slot], (st / NSLOT) & 1, p.status, kErrWaitKV);
       const uint32_t ks_a = ring_a + slot * STG;
-      const uint32_t vs_a = ks_a + KT * ROWB;
-      const int kt = k0 + st * KT;
+      const uint32_t vs_a = ks_a + KTD * ROWB;
+      const int kt = k0 + st * KTD;
 #pragma unroll
       for (int sub = 0; sub < KPW / KB; ++sub) {
         const int kl = kslot * KPW + sub * KB;   // first key of this step within the tile
@@ -236,8 +272,8 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
             const int d = kk * 16 + (mi & 1) * 8;
             uint32_t b0, b1, b2, b3;
             ldmatrix_x4(ks_a + key * ROWB + d * 2, b0, b1, b2, b3);
-            mma_bf16_16816(s[2 * jp], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
-            mma_bf16_16816(s[2 * jp + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
+            mma16816<F16>(s[2 * jp], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
+            mma16816<F16>(s[2 * jp + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
           }
         }
         // mask + online softmax (exp2 domain). Steps whose every key is visible to every row of
@@ -303,19 +339,19 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
         // O += P . V over two k16 steps of keys
 #pragma unroll
         for (int k2 = 0; k2 < 2; ++k2) {
-          const uint32_t a0 = pack_bf16x2(s[2 * k2][0], s[2 * k2][1]);
-          const uint32_t a1 = pack_bf16x2(s[2 * k2][2], s[2 * k2][3]);
-          const uint32_t a2 = pack_bf16x2(s[2 * k2 + 1][0], s[2 * k2 + 1][1]);
-          const uint32_t a3 = pack_bf16x2(s[2 * k2 + 1][2], s[2 * k2 + 1][3]);
+          const uint32_t a0 = pack2<F16>(s[2 * k2][0], s[2 * k2][1]);
+          const uint32_t a1 = pack2<F16>(s[2 * k2][2], s[2 * k2][3]);
+          const uint32_t a2 = pack2<F16>(s[2 * k2 + 1][0], s[2 * k2 + 1][1]);
+          const uint32_t a3 = pack2<F16>(s[2 * k2 + 1][2], s[2 * k2 + 1][3]);
           const int mi = lane >> 3;
           const int key = kl + k2 * 16 + (mi & 1) * 8 + (lane & 7);
 #pragma unroll
           for (int dt = 0; dt < NDT; dt += 2) {
-            const int d = (dt + (mi >> 1)) * 8;
+            const int d = ds * DW + (dt + (mi >> 1)) * 8;
             uint32_t b0, b1, b2, b3;
             ldmatrix_x4_trans(vs_a + key * ROWB + d * 2, b0, b1, b2, b3);
-            mma_bf16_16816(o[dt], a0, a1, a2, a3, b0, b1);
-            mma_bf16_16816(o[dt + 1], a0, a1, a2, a3, b2, b3);
+            mma16816<F16>(o[dt], a0, a1, a2, a3, b0, b1);
+            mma16816<F16>(o[dt + 1], a0, a1, a2, a3, b2, b3);
           }
         }
       }
@@ -335,11 +371,11 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
       float* myO = bufO + kslot * RPG * D;
 #pragma unroll
       for (int dt = 0; dt < NDT; ++dt) {
-        const int d = dt * 8 + 2 * tig;
+        const int d = ds * DW + dt * 8 + 2 * tig;
         *reinterpret_cast<float2*>(&myO[r0 * D + d]) = make_float2(o[dt][0], o[dt][1]);
         *reinterpret_cast<float2*>(&myO[r1 * D + d]) = make_float2(o[dt][2], o[dt][3]);
       }
-      if (tig == 0) {
+      if (tig == 0 && ds == 0) {
         bufM[kslot * RPG + r0] = m0;
         bufM[kslot * RPG + r1] = m1;
         bufL[kslot * RPG + r0] = l0;
@@ -364,7 +400,7 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
       }
 #pragma unroll
       for (int dt = 0; dt < NDT; ++dt) {
-        const int d = dt * 8 + 2 * tig;
+        const int d = ds * DW + dt * 8 + 2 * tig;
         float a0 = fmaf(w0[0], o[dt][0], 0.f), a1 = fmaf(w0[0], o[dt][1], 0.f);
         float a2 = fmaf(w1[0], o[dt][2], 0.f), a3 = fmaf(w1[0], o[dt][3], 0.f);
 #pragma unroll
@@ -379,7 +415,7 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
         *reinterpret_cast<float2*>(&bufO[r0 * D + d]) = make_float2(a0, a1);
         *reinterpret_cast<float2*>(&bufO[r1 * D + d]) = make_float2(a2, a3);
       }
-      if (tig == 0) {
+      if (tig == 0 && ds == 0) {
         float L0 = fmaf(w0[0], l0, 0.f), L1 = fmaf(w1[0], l1, 0.f);
 #pragma unroll
         for (int k = 1; k < KS; ++k) {
@@ -452,8 +488,8 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
       const int h = hk * G + prow / qLb, i = prow % qLb;
       bf16* dst = p.o + ob + int64_t(h) * p.o_sh + int64_t(i) * p.o_si + d4;
       uint2 pk;
-      pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-      pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+      pk.x = pack2<F16>(acc.x * inv, acc.y * inv);
+      pk.y = pack2<F16>(acc.z * inv, acc.w * inv);
       *reinterpret_cast<uint2*>(dst) = pk;
     }
   }
@@ -463,11 +499,11 @@ __global__ void __launch_bounds__((NRT * KS + 1) * 32) attn_kernel(const AttnPar
 // lane loads all ng partials of its D/32 columns at once (no dependent load chains).
 constexpr int kMergeRows = 8;  // rows (warps) per block
 
-template <int D>
+template <int D, bool F16>
 __global__ void __launch_bounds__(kMergeRows * 32) attn_merge_kernel(const AttnParams p, int rpg) {
   pdl_launch_dependents();
   pdl_wait();
-  constexpr int DPL = D / 32;  // columns per lane (4 or 2)
+  constexpr int DPL = D / 32;  // columns per lane (8, 4 or 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grow = blockIdx.x * kMergeRows + warp;  // (bhr, r) flattened
   const int bhr = grow / rpg, r = grow - bhr * rpg;
@@ -500,33 +536,31 @@ __global__ void __launch_bounds__(kMergeRows * 32) attn_merge_kernel(const AttnP
   for (int g = 0; g < p.ng; ++g) {
     const float w = __shfl_sync(0xffffffffu, wl, g);
     const float* src = base + g * gstride + lane * DPL;
-    if (DPL == 4) {
-      const float4 v = *reinterpret_cast<const float4*>(src);
-      acc[0] += w * v.x; acc[1] += w * v.y; acc[2 % DPL] += w * v.z; acc[3 % DPL] += w * v.w;
-    } else {
-      const float2 v = *reinterpret_cast<const float2*>(src);
-      acc[0] += w * v.x; acc[1] += w * v.y;
+#pragma unroll
+    for (int c = 0; c < DPL; c += 2) {
+      const float2 v = *reinterpret_cast<const float2*>(src + c);
+      acc[c] += w * v.x;
+      acc[c + 1] += w * v.y;
     }
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
   const int h = hk * G + prow / qLb, i = prow % qLb;
   bf16* dst = p.o + q_base(p, b, p.o_sb, p.o_si) + int64_t(h) * p.o_sh + int64_t(i) * p.o_si + lane * DPL;
-  if (DPL == 4) {
-    uint2 pk;
-    pk.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
-    pk.y = pack_bf16x2(acc[2 % DPL] * inv, acc[3 % DPL] * inv);
-    *reinterpret_cast<uint2*>(dst) = pk;
-  } else {
-    *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(acc[0] * inv, acc[1] * inv);
-  }
+#pragma unroll
+  for (int c = 0; c < DPL; c += 2)
+    *reinterpret_cast<uint32_t*>(dst + c) = pack2<F16>(acc[c] * inv, acc[c + 1] * inv);
 }
 
 // ------------------------------------------------------------------------------ host side
 
+// warps sharing a row tile's columns: 2 for head_dim 256 (each keeps half of the output)
+__host__ __device__ constexpr int dsplit(int d) { return d > 128 ? 2 : 1; }
+
 // Clusters of `cs` CTAs of the attention kernel for (D, nrt, ks) that the device runs at once.
 template <int D, int NRT, int KS>
 static int max_clusters_t(int cs) {
-  auto kern = attn_kernel<D, NRT, KS>;
+  constexpr int DS = dsplit(D);
+  auto kern = attn_kernel<D, NRT, KS, DS, false>;  // same shape for both input types
   constexpr int smem = attn_smem_bytes<D, NRT, KS>();
   // a refused query: portable sizes fall back to one CTA per SM, larger ones are not used
   const int fallback = cs <= 8 ? sm_count(current_device()) / cs : 0;
@@ -537,7 +571,7 @@ static int max_clusters_t(int cs) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cs, 1, 1);
-  cfg.blockDim = dim3((NRT * KS + 1) * 32);
+  cfg.blockDim = dim3((NRT * KS * DS + 1) * 32);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
@@ -567,9 +601,12 @@ static int max_clusters(int D, int nrt, int ks, int cs) {
   if (D == 64) {
     n = nrt == 1 ? max_clusters_t<64, 1, 2>(cs) : nrt == 2 ? max_clusters_t<64, 2, 2>(cs)
         : nrt == 4 ? max_clusters_t<64, 4, 2>(cs) : max_clusters_t<64, 8, 1>(cs);
-  } else {
+  } else if (D == 128) {
     n = nrt == 1 ? max_clusters_t<128, 1, 2>(cs) : nrt == 2 ? max_clusters_t<128, 2, 2>(cs)
         : nrt == 4 ? max_clusters_t<128, 4, 2>(cs) : max_clusters_t<128, 8, 1>(cs);
+  } else {
+    n = nrt == 1 ? max_clusters_t<256, 1, 1>(cs) : nrt == 2 ? max_clusters_t<256, 2, 1>(cs)
+        : max_clusters_t<256, 4, 1>(cs);
   }
   std::lock_guard<std::mutex> g(mu);
   cache[key] = n;
@@ -585,8 +622,11 @@ AttnPlan plan(int B, int Hq, int Hk, int qL, int D, int L) {
   else if (tiles <= 2) nrt = 2;
   else if (tiles <= 4) nrt = 4;
   else nrt = 8;
+  // head_dim 256: at most 4 row tiles per CTA (shared memory) and one key slot (32-key stages)
+  if (D > 128) nrt = std::min(nrt, 4);
   pl.nrt = nrt;
-  pl.ks = nrt >= 8 ? 1 : 2;
+  pl.ks = (nrt >= 8 || D > 128) ? 1 : 2;
+  const int kt = ktile(D);
   pl.nrg = (tiles + nrt - 1) / nrt;
   const int heads = B * Hk * pl.nrg;
   // key splits per head: as many CTAs as run at once in a single wave (clusters of ns CTAs
@@ -614,7 +654,7 @@ AttnPlan plan(int B, int Hq, int Hk, int qL, int D, int L) {
       const int gmax = std::min({fit, max_splits / c, 32});
       for (int g = 1; g <= gmax; ++g) {
         const int keys = (L + c * g - 1) / (c * g);
-        const int tiles = (keys + KT - 1) / KT;
+        const int tiles = (keys + KT - 1) / KT;  // 64-key units of work
         const double t = tiles * t_tile + (g > 1 ? t_merge : 0.0);
         if (t < best - 1e-9) {  // ties keep the larger cluster (tried first)
           best = t;
@@ -624,16 +664,16 @@ AttnPlan plan(int B, int Hq, int Hk, int qL, int D, int L) {
       }
     }
   }
-  int chunk = ((L + ns * ng - 1) / (ns * ng) + KT - 1) / KT * KT;
-  chunk = std::max(chunk, KT);
+  int chunk = ((L + ns * ng - 1) / (ns * ng) + kt - 1) / kt * kt;
+  chunk = std::max(chunk, kt);
   // drop splits that would start past the end
   while (ns * ng > 1 && (ns * ng - 1) * chunk >= L) {
     if (ng > 1) --ng; else --ns;
   }
   pl.ns = std::max(1, ns);
   pl.ng = std::max(1, std::min(ng, 32));  // the merge kernel holds one group per lane
-  pl.chunk = ((L + pl.ns * pl.ng - 1) / (pl.ns * pl.ng) + KT - 1) / KT * KT;
-  pl.chunk = std::max(pl.chunk, KT);
+  pl.chunk = ((L + pl.ns * pl.ng - 1) / (pl.ns * pl.ng) + kt - 1) / kt * kt;
+  pl.chunk = std::max(pl.chunk, kt);
   return pl;
 }
 
@@ -642,9 +682,10 @@ size_t workspace_bytes(const AttnPlan& pl, int B, int Hk, int D) {
   return size_t(B) * Hk * pl.nrg * pl.ng * (pl.nrt * 16) * (D + 4) * sizeof(float);
 }
 
-template <int D, int NRT, int KS>
+template <int D, int NRT, int KS, bool F16>
 static int launch_attn(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) {
-  auto kern = attn_kernel<D, NRT, KS>;
+  constexpr int DS = dsplit(D);
+  auto kern = attn_kernel<D, NRT, KS, DS, F16>;
   constexpr int smem = attn_smem_bytes<D, NRT, KS>();
   DSPARK_CUDA_TRY(configure_once(reinterpret_cast<const void*>(kern), 1, [&] {
                     cudaError_t e = cudaFuncSetAttribute(
@@ -655,31 +696,46 @@ static int launch_attn(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) 
                   }),
                   "attn: set smem / cluster attributes");
   dim3 grid(pl.ns, p.B * p.Hk * pl.nrg, pl.ng);
-  dim3 block((NRT * KS + 1) * 32);
+  dim3 block((NRT * KS * DS + 1) * 32);
   DSPARK_CUDA_TRY(launch_ex(kern, grid, block, smem, s, pl.ns, true, p), "attn: launch");
   if (pl.ng > 1) {
     const int rows = p.B * p.Hk * pl.nrg * NRT * 16;
-    DSPARK_CUDA_TRY(launch_ex(attn_merge_kernel<D>, dim3((rows + kMergeRows - 1) / kMergeRows),
-                              dim3(kMergeRows * 32), 0, s, 1, true, p, NRT * 16),
+    DSPARK_CUDA_TRY(launch_ex(attn_merge_kernel<D, F16>,
+                              dim3((rows + kMergeRows - 1) / kMergeRows), dim3(kMergeRows * 32),
+                              0, s, 1, true, p, NRT * 16),
                     "attn: merge launch");
   }
   return DSPARK_OK;
 }
 
-template <int D>
+template <int D, bool F16>
 static int dispatch_d(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) {
-  if (pl.nrt == 1 && pl.ks == 2) return launch_attn<D, 1, 2>(p, pl, s);
-  if (pl.nrt == 2 && pl.ks == 2) return launch_attn<D, 2, 2>(p, pl, s);
-  if (pl.nrt == 4 && pl.ks == 2) return launch_attn<D, 4, 2>(p, pl, s);
-  if (pl.nrt == 8 && pl.ks == 1) return launch_attn<D, 8, 1>(p, pl, s);
-  return fail(DSPARK_ERR_UNSUPPORTED, "attn: no kernel for %d row tiles x %d key slots", pl.nrt, pl.ks);
+  if constexpr (D > 128) {
+    if (pl.nrt == 1 && pl.ks == 1) return launch_attn<D, 1, 1, F16>(p, pl, s);
+    if (pl.nrt == 2 && pl.ks == 1) return launch_attn<D, 2, 1, F16>(p, pl, s);
+    if (pl.nrt == 4 && pl.ks == 1) return launch_attn<D, 4, 1, F16>(p, pl, s);
+  } else {
+    if (pl.nrt == 1 && pl.ks == 2) return launch_attn<D, 1, 2, F16>(p, pl, s);
+    if (pl.nrt == 2 && pl.ks == 2) return launch_attn<D, 2, 2, F16>(p, pl, s);
+    if (pl.nrt == 4 && pl.ks == 2) return launch_attn<D, 4, 2, F16>(p, pl, s);
+    if (pl.nrt == 8 && pl.ks == 1) return launch_attn<D, 8, 1, F16>(p, pl, s);
+  }
+  return fail(DSPARK_ERR_UNSUPPORTED, "attn: no kernel for head_dim %d, %d row tiles x %d key slots",
+              D, pl.nrt, pl.ks);
+}
+
+template <bool F16>
+static int dispatch_t(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) {
+  if (p.D == 64) return dispatch_d<64, F16>(p, pl, s);
+  if (p.D == 128) return dispatch_d<128, F16>(p, pl, s);
+  return dispatch_d<256, F16>(p, pl, s);
 }
 
 int run(AttnParams p, const AttnPlan* plan_in, cudaStream_t stream) {
   if (p.B <= 0 || p.Hq <= 0 || p.Hk <= 0 || p.Hq % p.Hk || p.qL <= 0 || p.L <= 0)
     return fail(DSPARK_ERR_ARG, "attn: bad shape B=%d Hq=%d Hk=%d qL=%d L=%d", p.B, p.Hq, p.Hk, p.qL, p.L);
-  if (p.D != 64 && p.D != 128)
-    return fail(DSPARK_ERR_UNSUPPORTED, "attn: head_dim %d not supported (64, 128)", p.D);
+  if (p.D != 64 && p.D != 128 && p.D != 256)
+    return fail(DSPARK_ERR_UNSUPPORTED, "attn: head_dim %d not supported (64, 128, 256)", p.D);
   if (p.qL > 32 && p.tree_anc)
     return fail(DSPARK_ERR_UNSUPPORTED, "attn: tree verify supports at most 32 rows");
   const uintptr_t al = reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v);
@@ -702,7 +758,7 @@ int run(AttnParams p, const AttnPlan* plan_in, cudaStream_t stream) {
     return fail(DSPARK_ERR_ARG, "attn: this launch needs a workspace of %zu bytes",
                 workspace_bytes(pl, p.B, p.Hk, p.D));
   if (p.status == nullptr) p.status = status_word(current_device());
-  return p.D == 64 ? dispatch_d<64>(p, pl, stream) : dispatch_d<128>(p, pl, stream);
+  return p.f16 ? dispatch_t<true>(p, pl, stream) : dispatch_t<false>(p, pl, stream);
 }
 
 }  // namespace attn

@@ -28,11 +28,12 @@ struct AttnParams {
   int B = 0, Hq = 0, Hk = 0, qL = 0, D = 0, L = 0;
   float scale_log2 = 0.f;              // scale * log2(e)
   int causal = 1;
+  int f16 = 0;                         // q/k/v/o hold fp16 (else bf16); the pointers carry bits
   // launch geometry
   int nrg = 1;        // row groups per (b, kv head)
   int ns = 1;         // key splits merged inside a cluster (cluster size)
   int ng = 1;         // cluster groups merged through the workspace
-  int chunk = 64;     // keys per split (multiple of 64)
+  int chunk = 64;     // keys per split (multiple of the kernel's key tile, 64 or 32)
   float* ws = nullptr;  // workspace (ng > 1): [B*Hk*nrg][ng][rows][D+2] fp32
   int* status = nullptr;
 };

@@ -358,15 +358,18 @@ size_t dspark_verify_attn_workspace(int B, int Hq, int Hk, int qL, int D, int L)
   return attn::workspace_bytes(pl, B, Hk, D);
 }
 
-int dspark_verify_attn(const void* q, const int64_t q_strides[3], const void* k,
-                       const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
-                       int B, int Hq, int Hk, int qL, int D, int L, const int32_t* kv_len,
-                       float scale, int causal, const uint32_t* tree_anc, void* out,
-                       const int64_t o_strides[3], void* workspace, size_t ws_bytes,
-                       void* stream) {
+int dspark_verify_attn_dt(int dtype, const void* q, const int64_t q_strides[3], const void* k,
+                          const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
+                          int B, int Hq, int Hk, int qL, int D, int L, const int32_t* kv_len,
+                          float scale, int causal, const uint32_t* tree_anc, void* out,
+                          const int64_t o_strides[3], void* workspace, size_t ws_bytes,
+                          void* stream) {
   if (!q || !k || !v || !out || !q_strides || !k_strides || !v_strides || !o_strides)
     return fail(DSPARK_ERR_ARG, "verify_attn: null pointer");
+  if (dtype != DSPARK_DTYPE_BF16 && dtype != DSPARK_DTYPE_F16)
+    return fail(DSPARK_ERR_UNSUPPORTED, "verify_attn: dtype %d (bf16 = 0, fp16 = 1)", dtype);
   attn::AttnParams p;
+  p.f16 = dtype == DSPARK_DTYPE_F16;
   p.q = static_cast<const bf16*>(q);
   p.q_sb = q_strides[0]; p.q_sh = q_strides[1]; p.q_si = q_strides[2];
   p.k = static_cast<const bf16*>(k);
@@ -388,6 +391,17 @@ int dspark_verify_attn(const void* q, const int64_t q_strides[3], const void* k,
     p.ws = static_cast<float*>(workspace);
   }
   return attn::run(p, &pl, as_stream(stream));
+}
+
+int dspark_verify_attn(const void* q, const int64_t q_strides[3], const void* k,
+                       const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
+                       int B, int Hq, int Hk, int qL, int D, int L, const int32_t* kv_len,
+                       float scale, int causal, const uint32_t* tree_anc, void* out,
+                       const int64_t o_strides[3], void* workspace, size_t ws_bytes,
+                       void* stream) {
+  return dspark_verify_attn_dt(DSPARK_DTYPE_BF16, q, q_strides, k, k_strides, v, v_strides, B,
+                               Hq, Hk, qL, D, L, kv_len, scale, causal, tree_anc, out, o_strides,
+                               workspace, ws_bytes, stream);
 }
 
 int dspark_verify_attn_ragged(const void* q, int64_t q_sh, int64_t q_si, const void* k,

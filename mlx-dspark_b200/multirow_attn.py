@@ -25,9 +25,10 @@ import torch
 from . import _lib
 from ._torch import elem_strides, ptr, require_cuda, stream_of
 
-MAX_D = 128
-D_SUPPORTED = (64, 128)
-_DTYPES = (torch.bfloat16,)
+MAX_D = 256
+D_SUPPORTED = (64, 128, 256)
+_DTYPES = (torch.bfloat16, torch.float16)
+_DT_CODE = {torch.bfloat16: 0, torch.float16: 1}  # DSPARK_DTYPE_BF16 / DSPARK_DTYPE_F16
 
 
 def plan(hq: int, hk: int, q_len: int, d: int, kv_len: int, batch: int = 1) -> dict:
@@ -69,6 +70,9 @@ def multirow_sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: f
     verify visibility bits over the last qL keys instead of the causal rule. ``kv_len``
     (int32 ``[B]`` on the device): per-row key counts <= L (ragged rows)."""
     require_cuda(q, k, v)
+    if q.dtype not in _DT_CODE or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise _lib.DSparkUnsupported(_lib.ERR_UNSUPPORTED,
+                                     f"dtypes {q.dtype}/{k.dtype}/{v.dtype} (bf16 or fp16)")
     B, Hq, qL, D = (int(s) for s in q.shape)
     Hk, L = int(k.shape[1]), int(k.shape[2])
     if q.stride(3) != 1:
@@ -82,8 +86,9 @@ def multirow_sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: f
         causal = False
     ws_n = workspace_bytes(Hq, Hk, qL, D, L, B)
     ws = _workspace(q.device, ws_n)
-    _lib.check(_lib.lib.dspark_verify_attn(
-        ptr(q), _lib.i64_array(elem_strides(q)), ptr(k), _lib.i64_array(elem_strides(k)),
+    _lib.check(_lib.lib.dspark_verify_attn_dt(
+        _DT_CODE[q.dtype], ptr(q), _lib.i64_array(elem_strides(q)), ptr(k),
+        _lib.i64_array(elem_strides(k)),
         ptr(v), _lib.i64_array(elem_strides(v)), B, Hq, Hk, qL, D, L, ptr(kv_len),
         float(scale), int(bool(causal)), ptr(anc), ptr(out), _lib.i64_array(elem_strides(out)),
         ptr(ws), ws_n, stream_of(q)))

@@ -37,6 +37,15 @@ static inline uint16_t f2bf(float f) {
   return (uint16_t)((c.u + 0x7FFFu + ((c.u >> 16) & 1u)) >> 16);
 }
 
+/* IEEE binary16 -> fp32 (exact) and fp32 -> binary16 round to nearest even, through the
+ * compiler's _Float16 type */
+static inline float h2f(uint16_t v) {
+  _Float16 h;
+  memcpy(&h, &v, 2);
+  return (float)h;
+}
+static inline float round_h(float f) { return (float)(_Float16)f; }
+
 int oracle_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();
@@ -112,11 +121,14 @@ static inline float dot_lanes(const float* a, const float* b, int D) {
   return s;
 }
 
-/* out (fp32) [B, Hq, qL, D] contiguous. q/k/v bf16 with element strides {b, h, row}. */
-void oracle_sdpa(const uint16_t* q, const int64_t* qs, const uint16_t* k, const int64_t* ks,
-                 const uint16_t* v, const int64_t* vs, int B, int Hq, int Hk, int qL, int L,
-                 int D, float scale, int causal, const uint32_t* anc, int round_p, float* out) {
+/* out (fp32) [B, Hq, qL, D] contiguous. q/k/v bf16 (f16 != 0: fp16) with element strides
+ * {b, h, row}. */
+void oracle_sdpa_t(const uint16_t* q, const int64_t* qs, const uint16_t* k, const int64_t* ks,
+                   const uint16_t* v, const int64_t* vs, int B, int Hq, int Hk, int qL, int L,
+                   int D, float scale, int causal, const uint32_t* anc, int round_p, int f16,
+                   float* out) {
   const int G = Hq / Hk;
+#define TO_F(x) (f16 ? h2f(x) : bf2f(x))
 #pragma omp parallel for collapse(2) schedule(dynamic)
   for (int b = 0; b < B; ++b) {
     for (int h = 0; h < Hq; ++h) {
@@ -130,13 +142,13 @@ void oracle_sdpa(const uint16_t* q, const int64_t* qs, const uint16_t* k, const 
         const uint16_t* kr = k + b * ks[0] + hk * ks[1] + (int64_t)j * ks[2];
         const uint16_t* vr = v + b * vs[0] + hk * vs[1] + (int64_t)j * vs[2];
         for (int d = 0; d < D; ++d) {
-          kf[(size_t)j * D + d] = bf2f(kr[d]);
-          vf[(size_t)j * D + d] = bf2f(vr[d]);
+          kf[(size_t)j * D + d] = TO_F(kr[d]);
+          vf[(size_t)j * D + d] = TO_F(vr[d]);
         }
       }
       for (int i = 0; i < qL; ++i) {
         const uint16_t* qr = q + b * qs[0] + h * qs[1] + (int64_t)i * qs[2];
-        for (int d = 0; d < D; ++d) qv[d] = bf2f(qr[d]);
+        for (int d = 0; d < D; ++d) qv[d] = TO_F(qr[d]);
         float mx = -INFINITY;
         for (int j = 0; j < L; ++j) {
           int ok = 1;
@@ -161,7 +173,7 @@ void oracle_sdpa(const uint16_t* q, const int64_t* qs, const uint16_t* k, const 
           den += p;
           /* round_p: the reference kernel feeds P to the P.V product in the input dtype
            * (src/mlx_dspark/multirow_attn.py:136-140); the row sum stays fp32 */
-          const float pv = round_p ? bf2f(f2bf(p)) : p;
+          const float pv = round_p ? (f16 ? round_h(p) : bf2f(f2bf(p))) : p;
           const float* vr = vf + (size_t)j * D;
           for (int d = 0; d < D; ++d) acc[d] += pv * vr[d];
         }
@@ -175,4 +187,11 @@ void oracle_sdpa(const uint16_t* q, const int64_t* qs, const uint16_t* k, const 
       free(vf);
     }
   }
+}
+#undef TO_F
+
+void oracle_sdpa(const uint16_t* q, const int64_t* qs, const uint16_t* k, const int64_t* ks,
+                 const uint16_t* v, const int64_t* vs, int B, int Hq, int Hk, int qL, int L,
+                 int D, float scale, int causal, const uint32_t* anc, int round_p, float* out) {
+  oracle_sdpa_t(q, qs, k, ks, v, vs, B, Hq, Hk, qL, L, D, scale, causal, anc, round_p, 0, out);
 }

@@ -58,6 +58,9 @@ def lib() -> C.CDLL:
         L.oracle_sdpa.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, f32,
                                   i32, vp, i32, vp]
         L.oracle_sdpa.restype = None
+        L.oracle_sdpa_t.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, f32,
+                                    i32, vp, i32, i32, vp]
+        L.oracle_sdpa_t.restype = None
         L.oracle_threads.restype = i32
         L.oracle_set_threads.argtypes = [i32]
         _lib = L
@@ -170,11 +173,12 @@ def _strides(a: np.ndarray) -> np.ndarray:
 
 
 def sdpa(q_bits, k_bits, v_bits, scale: float, causal: bool, anc=None,
-         round_p: bool = False) -> np.ndarray:
-    """fp32 [B, Hq, qL, D]. Inputs are bf16 bit patterns [B, H, rows, D] (any strides with D
-    contiguous). ``anc`` (uint32 [B, qL] or [qL]) selects the tree-verify rule. ``round_p``
-    rounds the softmax weights to bf16 for the P.V sum as the reference kernel does
-    (src/mlx_dspark/multirow_attn.py:136-140); otherwise P stays fp32."""
+         round_p: bool = False, f16: bool = False) -> np.ndarray:
+    """fp32 [B, Hq, qL, D]. Inputs are bf16 bit patterns [B, H, rows, D] (``f16``: fp16 bit
+    patterns; any strides with D contiguous). ``anc`` (uint32 [B, qL] or [qL]) selects the
+    tree-verify rule. ``round_p`` rounds the softmax weights to the input type for the P.V sum
+    as the reference kernel does (src/mlx_dspark/multirow_attn.py:136-140); otherwise P stays
+    fp32."""
     q = np.asarray(q_bits, dtype=np.uint16)
     k = np.asarray(k_bits, dtype=np.uint16)
     v = np.asarray(v_bits, dtype=np.uint16)
@@ -187,9 +191,10 @@ def sdpa(q_bits, k_bits, v_bits, scale: float, causal: bool, anc=None,
     a = None
     if anc is not None:
         a = np.ascontiguousarray(np.broadcast_to(np.asarray(anc, dtype=np.uint32), (B, qL)))
-    lib().oracle_sdpa(_ptr(q), _ptr(qs), _ptr(k), _ptr(ks), _ptr(v), _ptr(vs), B, Hq, Hk, qL, L,
-                      D, float(scale), int(bool(causal)), _ptr(a) if a is not None else None,
-                      int(bool(round_p)), _ptr(out))
+    lib().oracle_sdpa_t(_ptr(q), _ptr(qs), _ptr(k), _ptr(ks), _ptr(v), _ptr(vs), B, Hq, Hk, qL,
+                        L, D, float(scale), int(bool(causal)),
+                        _ptr(a) if a is not None else None, int(bool(round_p)), int(bool(f16)),
+                        _ptr(out))
     return out
 
 

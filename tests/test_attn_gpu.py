@@ -17,11 +17,11 @@ pytestmark = pytest.mark.gpu
 REL = 1e-2
 
 
-def _mk(B, hq, hk, q_len, L, d, slack=0, seed=0, dev="cuda"):
+def _mk(B, hq, hk, q_len, L, d, slack=0, seed=0, dev="cuda", dtype=torch.bfloat16):
     g = torch.Generator(device="cpu").manual_seed(seed)
-    q = torch.randn((B, hq, q_len, d), generator=g).to(torch.bfloat16)
-    k = torch.randn((B, hk, L + slack, d), generator=g).to(torch.bfloat16)
-    v = torch.randn((B, hk, L + slack, d), generator=g).to(torch.bfloat16)
+    q = torch.randn((B, hq, q_len, d), generator=g).to(dtype)
+    k = torch.randn((B, hk, L + slack, d), generator=g).to(dtype)
+    v = torch.randn((B, hk, L + slack, d), generator=g).to(dtype)
     q, k, v = q.to(dev), k.to(dev), v.to(dev)
     if slack:  # a cache-style view into a larger buffer
         k, v = k[:, :, :L], v[:, :, :L]
@@ -33,19 +33,26 @@ def _bits(t):
 
 
 def _ref(oracle, q, k, v, scale, causal, anc=None):
-    return oracle.sdpa(_bits(q), _bits(k), _bits(v), scale, causal, anc)
+    return oracle.sdpa(_bits(q), _bits(k), _bits(v), scale, causal, anc,
+                       f16=q.dtype == torch.float16)
 
 
 def _check(oracle, out, ref):
     o = out.float().cpu().numpy()
     mine = float(np.abs(o - ref).max())
-    ideal = float(np.abs(oracle.round_bf16(ref) - ref).max())
+    if out.dtype == torch.float16:
+        ideal = float(np.abs(ref.astype(np.float16).astype(np.float32) - ref).max())
+    else:
+        ideal = float(np.abs(oracle.round_bf16(ref) - ref).max())
     assert mine <= REL * max(float(np.abs(ref).max()), 1e-6), (mine, float(np.abs(ref).max()))
     assert mine <= 2.0 * ideal + 2e-3, (mine, ideal)
 
 
 CASES = [
     # B, hq, hk, q_len, L, d
+    (1, 24, 4, 8, 1037, 256),     # Qwen3.8 geometry (head_dim 256), off-grid tail
+    (1, 24, 4, 1, 300, 256),
+    (1, 24, 4, 16, 33000, 256),   # head_dim 256 at a long context: split-and-merge plan
     (1, 32, 8, 15, 777, 128),     # drafter-block geometry, off-grid tail
     (1, 32, 8, 2, 64, 128),
     (1, 32, 2, 16, 500, 128),     # GQA 16 -> 256 rows: row groups
@@ -80,13 +87,26 @@ def test_baseline_config(cuda, oracle, L):
     _check(oracle, out, _ref(oracle, q, k, v, 128 ** -0.5, True))
 
 
-def test_head_dim_256_is_refused_loudly(cuda):
+@pytest.mark.parametrize("B,hq,hk,q_len,L,d", [(1, 24, 4, 6, 900, 256), (1, 32, 8, 16, 2048, 128),
+                                                (2, 8, 8, 5, 129, 64)])
+def test_fp16_inputs(cuda, oracle, B, hq, hk, q_len, L, d):
+    """fp16 q/k/v (tests/test_multirow_attn.py:83-87): fp16 output, the probabilities rounded
+    to fp16 for P.V, against the oracle's fp16 restatement."""
+    from mlx_dspark_b200.multirow_attn import multirow_sdpa
+
+    q, k, v = _mk(B, hq, hk, q_len, L, d, slack=5, seed=d + L, dtype=torch.float16)
+    out = multirow_sdpa(q, k, v, scale=d ** -0.5, causal=True)
+    assert out.dtype == torch.float16 and out.shape == q.shape
+    _check(oracle, out, _ref(oracle, q, k, v, d ** -0.5, True))
+
+
+def test_head_dim_other_than_64_128_256_is_refused_loudly(cuda):
     from mlx_dspark_b200 import DSparkUnsupported
     from mlx_dspark_b200.multirow_attn import multirow_sdpa
 
-    q, k, v = _mk(1, 24, 4, 8, 300, 256)
+    q, k, v = _mk(1, 24, 4, 8, 300, 96)
     with pytest.raises(DSparkUnsupported):
-        multirow_sdpa(q, k, v, scale=256 ** -0.5, causal=True)
+        multirow_sdpa(q, k, v, scale=96 ** -0.5, causal=True)
 
 
 def test_causal_rows_see_only_their_prefix(cuda, oracle):

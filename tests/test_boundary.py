@@ -73,9 +73,12 @@ def test_attention_argument_checks_fail_loudly():
     rc = _lib.lib.dspark_verify_attn(p, s, p, s, p, s, 1, 6, 4, 2, 128, 64, None, 0.1, 1, None, p,
                                      s, None, 0, None)
     assert rc == _lib.ERR_ARG  # Hq not a multiple of Hk
-    rc = _lib.lib.dspark_verify_attn(p, s, p, s, p, s, 1, 8, 2, 2, 256, 64, None, 0.1, 1, None, p,
+    rc = _lib.lib.dspark_verify_attn(p, s, p, s, p, s, 1, 8, 2, 2, 96, 64, None, 0.1, 1, None, p,
                                      s, None, 0, None)
     assert rc == _lib.ERR_UNSUPPORTED and "head_dim" in _lib.last_error()
+    rc = _lib.lib.dspark_verify_attn_dt(7, p, s, p, s, p, s, 1, 8, 2, 2, 128, 64, None, 0.1, 1,
+                                        None, p, s, None, 0, None)
+    assert rc == _lib.ERR_UNSUPPORTED and "dtype" in _lib.last_error()
 
 
 def test_status_needs_init():
@@ -179,6 +182,9 @@ def test_multirow_eligible_gate():
     assert not eligible(*_qkv(1, 8, 2, 4, 32, 64), "causal", None, cfg)      # short KV
     assert not eligible(*_qkv(1, 16, 2, 4, 128, 64), "causal", None, cfg)    # unconfigured shape
     assert not eligible(*_qkv(1, 8, 2, 4, 128, 64, torch.float32), "causal", None, cfg)
+    assert eligible(*_qkv(1, 8, 2, 4, 128, 64, torch.float16), "causal", None, cfg)  # fp16 served
+    cfg256 = MultirowConfig((Window(24, 4, 256, min_q=1, max_q=16, min_kv=16),))
+    assert eligible(*_qkv(1, 24, 4, 8, 1037, 256), "causal", None, cfg256)  # head_dim 256
     assert cfg.window(8, 2, 64) is not None and cfg.window(8, 2, 128) is None
 
 
