@@ -31,7 +31,10 @@ WINDOW = {4: (1, 32), 8: (1, 32)}   # rows served per quantization width
 
 def fits(mod) -> bool:
     """The layout the kernel reads: 4- or 8-bit affine, groups of 64, K % 64 == 0, N % 8 == 0,
-    bf16 scales/biases (src/mlx_dspark/skinny_qmm.py:174-181)."""
+    bf16 scales/biases (src/mlx_dspark/skinny_qmm.py:174-181). The reference also accepts fp16
+    and fp32 scales; here those layers do not fit (the kernels read bf16 scales and biases, and
+    converting them would change the weights), so they stay on the stock path, a torch
+    dequantize-and-matmul with MLX's semantics."""
     try:
         w = mod["weight"]
     except (KeyError, TypeError):
@@ -71,6 +74,9 @@ def qmm(x2: torch.Tensor, weight: torch.Tensor, scales: torch.Tensor, biases: to
     """``x2 [rows, K] @ dequant(W)^T`` for gs64 affine 4/8-bit ``W`` -> bf16 ``[rows, N]``
     (src/mlx_dspark/skinny_qmm.py:239-246). ``weight`` holds the packed uint32 words (as
     int32 or uint32), ``scales`` / ``biases`` are bf16 ``[N, K/64]``."""
+    if scales.dtype != torch.bfloat16 or biases.dtype != torch.bfloat16:
+        raise _lib.DSparkUnsupported(
+            _lib.ERR_UNSUPPORTED, f"scales/biases dtype {scales.dtype}/{biases.dtype} (bf16 only)")
     require_cuda(x2, weight, scales, biases)
     if x2.dtype != torch.bfloat16:
         raise _lib.DSparkUnsupported(_lib.ERR_UNSUPPORTED, f"x dtype {x2.dtype} (bf16 only)")

@@ -76,6 +76,12 @@ class QuantizedLinear(torch.nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         bias = self.bias if "bias" in self else None
+        if self.scales.dtype != torch.bfloat16 or self.biases.dtype != torch.bfloat16:
+            # fp16 / fp32 scales: the kernels read bf16 scales, so these layers keep MLX's stock
+            # semantics (w = scale * q + bias in fp32, fp32 accumulation, output in x's type)
+            w = quant.dequantize(quant.QWeight(self.weight, self.scales, self.biases, self.bits))
+            y = (x.float() @ w.t()).to(x.dtype)
+            return y if bias is None else (y + bias.to(y.dtype))
         return _sk.quantized_matmul(x, self.weight, self.scales, self.biases, self.bits, bias)
 
     def __call__(self, x):  # class attribute the scoped patch swaps

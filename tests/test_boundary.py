@@ -245,3 +245,22 @@ def test_ctypes_mirrors_match_the_header_layout(tmp_path):
     got = dict(line.split() for line in subprocess.run([str(exe)], check=True, capture_output=True,
                                                        text=True).stdout.splitlines())
     assert {k: int(v) for k, v in got.items()} == want
+
+
+def test_fp16_and_fp32_scales_do_not_fit_the_kernel():
+    """The reference's fits() accepts bf16/fp16/fp32 scales (src/mlx_dspark/skinny_qmm.py:
+    174-181); the kernels read bf16 scales only, so other scale types are refused by fits()
+    and by qmm() (no silent misread), and such layers stay on the stock path."""
+    from mlx_dspark_b200 import DSparkUnsupported, quant, skinny_qmm, small_m_qmm
+
+    qw = quant.QWeight(torch.zeros(64, 64, dtype=torch.int32),
+                       torch.ones(64, 8, dtype=torch.bfloat16),
+                       torch.zeros(64, 8, dtype=torch.bfloat16), 4)
+    assert skinny_qmm.fits(small_m_qmm.QuantizedLinear(qw))
+    for dt in (torch.float16, torch.float32):
+        q2 = quant.QWeight(qw.wq, qw.scales.to(dt), qw.biases.to(dt), 4)
+        mod = small_m_qmm.QuantizedLinear(q2)
+        assert not skinny_qmm.fits(mod) and not small_m_qmm.eligible(mod)
+        with pytest.raises(DSparkUnsupported, match="scales"):
+            skinny_qmm.qmm(torch.zeros(2, 512, dtype=torch.bfloat16), q2.wq, q2.scales,
+                           q2.biases, 4)

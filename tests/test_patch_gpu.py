@@ -110,3 +110,26 @@ def test_patched_sdpa_tree_mask_runs_the_tree_kernel(cuda, oracle):
                       anc=np.array(anc, dtype=np.uint32))
     err = float(np.abs(out.float().cpu().numpy() - ref).max())
     assert err <= 1e-2 * float(np.abs(ref).max()), err
+
+
+@pytest.mark.parametrize("sdt", [torch.float16, torch.float32])
+def test_fp16_fp32_scales_stay_on_the_stock_path(cuda, oracle, monkeypatch, sdt):
+    """A layer whose scales are fp16 / fp32 does not fit the kernel (it reads bf16 scales):
+    inside small_m_matmul it is served by the stock dequantize-and-matmul, correctly."""
+    from mlx_dspark_b200 import quant, skinny_qmm, small_m_qmm
+
+    rng = np.random.default_rng(5)
+    N, K = 256, 1024
+    wq, sc, bi = oracle.quantize(rng.normal(0, 0.02, (N, K)).astype(np.float32), 4)
+    s32, b32 = oracle.from_bf16(sc), oracle.from_bf16(bi)
+    mod = small_m_qmm.QuantizedLinear(quant.QWeight(
+        torch.from_numpy(wq.view(np.int32)).to(cuda), torch.from_numpy(s32).to(sdt).to(cuda),
+        torch.from_numpy(b32).to(sdt).to(cuda), 4))
+    calls = []
+    monkeypatch.setattr(skinny_qmm, "call", lambda *a: calls.append(1))
+    x = oracle.to_bf16(rng.normal(0, 1, (8, K)))
+    with small_m_qmm.small_m_matmul(frozenset({id(mod)})):
+        y = mod(_bf(x, cuda))
+    assert calls == []
+    ref = oracle.qmm(x, wq, sc, bi, 4)  # bf16 scales are exact in fp16 / fp32 here
+    assert float(np.abs(y.float().cpu().numpy() - ref).max()) <= 1e-2 * float(np.abs(ref).max())
