@@ -141,6 +141,20 @@ typedef struct {
 
 int dspark_qmm_fused(const dspark_qmm_args* a, void* stream);
 
+/* Wide-M product out[M, N] = bf16(x[M, K] . dequant(W)^T) for any number of rows (prefill-width
+ * calls, the batch engine's packed rows): the weights are dequantized once per 128-row tile into
+ * tensor memory (w = scale * q + bias rounded to bf16) and multiplied with 256 x rows per
+ * tcgen05 MMA, fp32 accumulation. Replaces wide_gemm's x @ mx.dequantize(w).T
+ * (src/mlx_dspark/wide_gemm.py:1-30, the patched call at :177-193). Requires K % 512 == 0,
+ * bits in {4, 8}, group 64, x / weights / scales / biases 16-byte aligned, ldx % 8 == 0. */
+int dspark_qmm_wide(const void* x, int64_t ldx, int M, int K, const uint32_t* wq,
+                    const void* scales, const void* biases, int N, int bits, void* out,
+                    int64_t ldo, void* stream);
+
+/* Scratch bytes a wide projection of dspark_verify_forward needs: the normed x [M, K] when
+ * `norm`, and the bf16 product [M, N] when the epilogue is not DSPARK_EPI_PLAIN. */
+size_t dspark_qmm_wide_workspace(int M, int K, int N, int epilogue, int norm);
+
 /* RoPE frequencies theta^(-2i/head_dim), i < head_dim / 2, as the fused epilogue uses them. */
 int dspark_rope_inv_freq(float* inv_freq, int head_dim, float theta, void* stream);
 
@@ -356,6 +370,8 @@ typedef struct {
   void* attn_ws;    /* attention workspace (may be NULL) */
   size_t attn_ws_bytes;
   int rows_cap;     /* rows the buffers hold (0: 32) */
+  void* wide_ws;    /* scratch of the wide-M projections (NULL: 32-row launches only) */
+  size_t wide_ws_bytes;  /* >= the largest dspark_qmm_wide_workspace of the model's projections */
 } dspark_fwd_buffers;
 
 /* One verify forward (Target.verify -> _body_mlxlm + head, src/mlx_dspark/target.py:642,
@@ -366,8 +382,10 @@ typedef struct {
  * The packing arrays in `buf` (row_pos, row_kv, kv_len, row_start, q_len, kv_off) must be
  * filled for the step (dspark_pack_ragged, or dspark_verify_prepare for one request).
  * L_max / qL_max bound the requests' key counts / block rows (qL_max <= 32). R <= rows_cap:
- * a step of many requests (the batch engine) runs every projection in launches of 32 rows
- * (each re-reads the weights) and the attention over all requests at once. */
+ * a step of many requests (the batch engine) runs every projection over all R rows at once in
+ * the wide-M engine (RMSNorm applied to x, tcgen05 product, fused epilogue on the product) when
+ * R >= 64 and buf->wide_ws holds the scratch, else in launches of 32 rows (each re-reads the
+ * weights); the attention runs over all requests at once. */
 int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf,
                           const int32_t* ids, int R, int B, int qL_max, int L_max,
                           void* logits, int64_t ld_logits, void* stream);

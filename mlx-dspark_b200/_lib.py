@@ -60,7 +60,7 @@ class FwdBuffers(C.Structure):
     _fields_ = [("h", vp), ("xq", vp), ("attn", vp), ("act", vp), ("ssq_a", vp), ("ssq_b", vp),
                 ("inv_freq", vp), ("row_pos", vp), ("row_kv", vp), ("kv_len", vp),
                 ("row_start", vp), ("q_len", vp), ("kv_off", vp), ("attn_ws", vp),
-                ("attn_ws_bytes", sz), ("rows_cap", i32)]
+                ("attn_ws_bytes", sz), ("rows_cap", i32), ("wide_ws", vp), ("wide_ws_bytes", sz)]
 
 
 IPC_HANDLE_BYTES = 64
@@ -98,6 +98,8 @@ _SIGS = {
     "dspark_ipc_free": (i32, [vp]),
     "dspark_p2p_allgather": (i32, [C.POINTER(P2PGatherArgs), vp]),
     "dspark_rope_inv_freq": (i32, [vp, i32, f32, vp]),
+    "dspark_qmm_wide": (i32, [vp, i64, i32, i32, vp, vp, vp, i32, i32, vp, i64, vp]),
+    "dspark_qmm_wide_workspace": (sz, [i32, i32, i32, i32, i32]),
     "dspark_version": (i32, []),
     "dspark_last_error": (C.c_char_p, []),
     "dspark_init": (i32, [i32]),

@@ -132,7 +132,8 @@ class SpecBatch:
             ptr(fb["h"]), ptr(fb["xq"]), ptr(fb["attn"]), ptr(fb["act"]), ptr(fb["ssq_a"]),
             ptr(fb["ssq_b"]), ptr(fb["inv_freq"]), ptr(b["row_pos"]), ptr(b["row_kv"]),
             ptr(b["kv_len_new"]), ptr(b["cu_rows"]), ptr(b["block_len"]), ptr(self.slot_off),
-            ptr(fb["attn_ws"]), fb["attn_ws"].numel(), t.rows_cap)
+            ptr(fb["attn_ws"]), fb["attn_ws"].numel(), t.rows_cap,
+            ptr(fb["wide_ws"]) if t.wide_ws_bytes else None, t.wide_ws_bytes)
         self._C = C
 
     @property

@@ -309,6 +309,26 @@ int dspark_qmm_fused(const dspark_qmm_args* a, void* stream) {
   return qmm::run(p, epi, &pl, as_stream(stream));
 }
 
+int dspark_qmm_wide(const void* x, int64_t ldx, int M, int K, const uint32_t* wq,
+                    const void* scales, const void* biases, int N, int bits, void* out,
+                    int64_t ldo, void* stream) {
+  if (!x || !wq || !scales || !biases || !out) return fail(DSPARK_ERR_ARG, "qmm_wide: null pointer");
+  if (ldo < N || ldx < K) return fail(DSPARK_ERR_ARG, "qmm_wide: row strides below the row sizes");
+  qmm::QmmParams p;
+  p.x = static_cast<const bf16*>(x); p.ldx = ldx; p.M = M; p.K = K; p.N = N; p.bits = bits;
+  p.wq = wq;
+  p.scales = static_cast<const bf16*>(scales);
+  p.biases = static_cast<const bf16*>(biases);
+  p.G = K / 64;
+  p.status = status_word(current_device());
+  return qmm::wide_product(p, static_cast<bf16*>(out), ldo, as_stream(stream));
+}
+
+size_t dspark_qmm_wide_workspace(int M, int K, int N, int epilogue, int norm) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  return qmm::wide_ws_bytes(M, K, N, epilogue, norm != 0);
+}
+
 int dspark_rope_inv_freq(float* inv_freq, int head_dim, float theta, void* stream) {
   if (!inv_freq || head_dim <= 0 || head_dim % 2) return fail(DSPARK_ERR_ARG, "rope_inv_freq: bad args");
   return ops::fill_inv_freq(inv_freq, head_dim, theta, as_stream(stream));
@@ -549,7 +569,22 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf, 
   bf16* at = static_cast<bf16*>(buf->attn);
   bf16* act = static_cast<bf16*>(buf->act);
   const int kSsqStride = rows_cap;  // statistics entry e of row m at e * kSsqStride + m
-  constexpr int kChunk = 32;        // rows per projection launch
+  // many rows: every projection runs once over all R rows in the wide-M engine, given its scratch
+  const int wide_min = env_int("DSPARK_WIDE_MIN_ROWS", 64);
+  bool wide = R >= wide_min && buf->wide_ws != nullptr;
+  if (wide) {
+    size_t need = 0;
+    for (int l = 0; l < m->n_layers; ++l) {
+      const dspark_layer& L = m->layers[l];
+      need = std::max({need, qmm::wide_ws_bytes(R, H, L.qkv.N, qmm::EPI_QKROPE, true),
+                       qmm::wide_ws_bytes(R, L.o.K, L.o.N, qmm::EPI_RESID, false),
+                       qmm::wide_ws_bytes(R, H, L.gate_up.N, qmm::EPI_SWIGLU, true),
+                       qmm::wide_ws_bytes(R, L.down.K, L.down.N, qmm::EPI_RESID, false)});
+    }
+    need = std::max(need, qmm::wide_ws_bytes(R, H, m->lm_head.N, qmm::EPI_PLAIN, true));
+    wide = need <= buf->wide_ws_bytes;
+  }
+  const int kChunk = wide ? R : 32;  // rows per projection launch
 
   DSPARK_TRY(ops::fill_inv_freq(buf->inv_freq, D, m->rope_theta, s));
   DSPARK_TRY(ops::embed(ids, R, m->embed.wq, static_cast<const bf16*>(m->embed.scales),
@@ -581,8 +616,12 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf, 
       p.kv_cap = m->kv_cap;
       p.row_pos = buf->row_pos + r0; p.row_kv = buf->row_kv + r0;
       p.out = xq; p.ldo = 0;
-      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_QKROPE, mr);
-      DSPARK_TRY(qmm::run(p, qmm::EPI_QKROPE, &pl, s));
+      if (wide) {
+        DSPARK_TRY(qmm::run_wide(p, qmm::EPI_QKROPE, buf->wide_ws, buf->wide_ws_bytes, s));
+      } else {
+        qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_QKROPE, mr);
+        DSPARK_TRY(qmm::run(p, qmm::EPI_QKROPE, &pl, s));
+      }
     }
     // verify attention over each request's cache slot
     {
@@ -617,9 +656,14 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf, 
       p.biases = static_cast<const bf16*>(L.o.biases);
       p.resid = h + int64_t(r0) * H; p.ldr = H; p.out = h + int64_t(r0) * H; p.ldo = H;
       p.ssq_out = buf->ssq_b + r0; p.ssq_stride = kSsqStride;
-      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_RESID, mr);
-      ssq_n_b = pl.nw > 0 ? (p.N + 16 * pl.nw - 1) / (16 * pl.nw) : 0;  // run() rejects nw == 0
-      DSPARK_TRY(qmm::run(p, qmm::EPI_RESID, &pl, s));
+      if (wide) {
+        ssq_n_b = (p.N + 127) / 128;  // one statistics entry per 128-column epilogue tile
+        DSPARK_TRY(qmm::run_wide(p, qmm::EPI_RESID, buf->wide_ws, buf->wide_ws_bytes, s));
+      } else {
+        qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_RESID, mr);
+        ssq_n_b = pl.nw > 0 ? (p.N + 16 * pl.nw - 1) / (16 * pl.nw) : 0;  // run() rejects nw == 0
+        DSPARK_TRY(qmm::run(p, qmm::EPI_RESID, &pl, s));
+      }
     }
     // gate/up projection + post-attention RMSNorm + SwiGLU
     for (int r0 = 0; r0 < R; r0 += kChunk) {
@@ -633,8 +677,12 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf, 
       p.norm_w = static_cast<const bf16*>(L.post_norm);
       p.ssq_in = buf->ssq_b + r0; p.ssq_n = ssq_n_b; p.ssq_stride = kSsqStride; p.eps = m->rms_eps;
       p.out = act + int64_t(r0) * I; p.ldo = I; p.n_act = I;
-      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_SWIGLU, mr);
-      DSPARK_TRY(qmm::run(p, qmm::EPI_SWIGLU, &pl, s));
+      if (wide) {
+        DSPARK_TRY(qmm::run_wide(p, qmm::EPI_SWIGLU, buf->wide_ws, buf->wide_ws_bytes, s));
+      } else {
+        qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_SWIGLU, mr);
+        DSPARK_TRY(qmm::run(p, qmm::EPI_SWIGLU, &pl, s));
+      }
     }
     // down projection + residual + statistics for the next input norm
     for (int r0 = 0; r0 < R; r0 += kChunk) {
@@ -646,9 +694,14 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf, 
       p.biases = static_cast<const bf16*>(L.down.biases);
       p.resid = h + int64_t(r0) * H; p.ldr = H; p.out = h + int64_t(r0) * H; p.ldo = H;
       p.ssq_out = buf->ssq_a + r0; p.ssq_stride = kSsqStride;
-      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_RESID, mr);
-      ssq_n = pl.nw > 0 ? (p.N + 16 * pl.nw - 1) / (16 * pl.nw) : 0;  // run() rejects nw == 0
-      DSPARK_TRY(qmm::run(p, qmm::EPI_RESID, &pl, s));
+      if (wide) {
+        ssq_n = (p.N + 127) / 128;
+        DSPARK_TRY(qmm::run_wide(p, qmm::EPI_RESID, buf->wide_ws, buf->wide_ws_bytes, s));
+      } else {
+        qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_RESID, mr);
+        ssq_n = pl.nw > 0 ? (p.N + 16 * pl.nw - 1) / (16 * pl.nw) : 0;  // run() rejects nw == 0
+        DSPARK_TRY(qmm::run(p, qmm::EPI_RESID, &pl, s));
+      }
     }
     ssq_cur = buf->ssq_a;
   }
@@ -664,8 +717,12 @@ int dspark_verify_forward(const dspark_model* m, const dspark_fwd_buffers* buf, 
     p.norm_w = static_cast<const bf16*>(m->final_norm);
     p.ssq_in = ssq_cur + r0; p.ssq_n = ssq_n; p.ssq_stride = kSsqStride; p.eps = m->rms_eps;
     p.out = static_cast<bf16*>(logits) + int64_t(r0) * ld_logits; p.ldo = ld_logits;
-    qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_PLAIN, mr);
-    DSPARK_TRY(qmm::run(p, qmm::EPI_PLAIN, &pl, s));
+    if (wide) {
+      DSPARK_TRY(qmm::run_wide(p, qmm::EPI_PLAIN, buf->wide_ws, buf->wide_ws_bytes, s));
+    } else {
+      qmm::QmmPlan pl = cached_plan(p.N, p.K, p.bits, qmm::EPI_PLAIN, mr);
+      DSPARK_TRY(qmm::run(p, qmm::EPI_PLAIN, &pl, s));
+    }
   }
   return DSPARK_OK;
 }

@@ -113,5 +113,12 @@ int st_max_clusters(int cs, int smem);
 QmmPlan plan(int N, int K, int bits, int epi, int min_tn, int rt = 2);
 int run(const QmmParams& p, int epi, const QmmPlan* plan, cudaStream_t stream);
 
+// Wide-M engine (qmm_wide.cu, tcgen05): y = bf16(x . dequant(W)^T) for any M (K % 512 == 0),
+// and the full projection (RMSNorm prologue applied to x first, fused epilogue applied to the
+// product after) with scratch `ws` of wide_ws_bytes(M, K, N, epi, norm) bytes.
+int wide_product(const QmmParams& p, __nv_bfloat16* y, long ldy, cudaStream_t s);
+size_t wide_ws_bytes(int M, int K, int N, int epi, bool norm);
+int run_wide(const QmmParams& p, int epi, void* ws, size_t ws_bytes, cudaStream_t s);
+
 }  // namespace qmm
 }  // namespace dspark

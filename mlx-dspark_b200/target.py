@@ -197,6 +197,16 @@ class Target:
         ws = int(_lib.lib.dspark_verify_attn_workspace(B, Hq, cfg.n_kv_heads, 32, D,
                                                        self.kv_cap))
         self.buf["attn_ws"] = torch.empty(max(ws, 16), dtype=torch.uint8, **e)
+        # scratch of the wide-M projections (forwards of 64+ packed rows): normed x + product
+        wide = 0
+        if R >= 64:
+            W = _lib.lib.dspark_qmm_wide_workspace
+            qkv_n = (Hq + 2 * cfg.n_kv_heads) * D
+            wide = max(W(R, H, qkv_n, _lib.EPI_QKROPE, 1), W(R, Hq * D, H, _lib.EPI_RESID, 0),
+                       W(R, H, 2 * I, _lib.EPI_SWIGLU, 1), W(R, I, H, _lib.EPI_RESID, 0),
+                       W(R, H, cfg.vocab, _lib.EPI_PLAIN, 1))
+        self.buf["wide_ws"] = torch.empty(max(int(wide), 16), dtype=torch.uint8, **e)
+        self.wide_ws_bytes = int(wide)
         self.logits = torch.empty((R, cfg.vocab), dtype=torch.bfloat16, **e)
         self.rows_cap = rows_cap
 
@@ -221,7 +231,8 @@ class Target:
             ptr(b["h"]), ptr(b["xq"]), ptr(b["attn"]), ptr(b["act"]), ptr(b["ssq_a"]),
             ptr(b["ssq_b"]), ptr(b["inv_freq"]), ptr(b["row_pos"]), ptr(b["row_kv"]),
             ptr(b["kv_len"]), ptr(b["row_start"]), ptr(b["q_len"]), ptr(b["kv_off"]),
-            ptr(b["attn_ws"]), b["attn_ws"].numel(), self.rows_cap)
+            ptr(b["attn_ws"]), b["attn_ws"].numel(), self.rows_cap,
+            ptr(b["wide_ws"]) if self.wide_ws_bytes else None, self.wide_ws_bytes)
 
     def slot_offset(self, slot: int) -> int:
         """Element offset of a request slot inside each layer's K/V pool."""

@@ -116,3 +116,48 @@ def test_many_steps_lengths_track_accepts(cuda):
         want = [w + a + 1 for w, a in zip(want, acc)]
     torch.cuda.synchronize()
     assert eng.lens.cpu().tolist() == want
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_spec_batch_step_wide_rows_match_per_request_oracle(cuda, oracle, monkeypatch, bits):
+    """More than 64 packed rows: every projection runs once over all rows in the wide-M engine
+    (RMSNorm applied to x, tcgen05 product, fused epilogue on the product). Each request's logits
+    still match the oracle's single-request forward; the same step through the 32-row launches
+    (wide engine switched off) agrees with it within the forward's bar."""
+    caps = [300, 700, 96, 500, 260, 410, 180]
+    lengths = [120, 533, 40, 300, 17, 222, 99]
+    blocks = [17, 9, 13, 16, 12, 15, 11]      # 93 packed rows
+    t, eng, kvs = _engine(cuda, caps, lengths, seed=10 + bits, bits=bits, max_rows=128)
+    assert t.wide_ws_bytes > 0
+    cfg = t.cfg
+    g = torch.Generator(device=cuda).manual_seed(8)
+    drafts = torch.randint(0, cfg.vocab, (eng.B, 16), device=cuda, dtype=torch.int32,
+                           generator=g)
+    pending = eng.pending.clone()
+    lens0 = eng.lens.clone()
+    out = eng.step(drafts, blocks)
+    torch.cuda.synchronize()
+    R = sum(blocks)
+    cu = out["cu_rows"].cpu().numpy()
+    logits = t.logits[:R].float().cpu().numpy()
+    ow, oc = t.oracle_weights(), t.oracle_config()
+    for b, (L0, blk) in enumerate(zip(lengths, blocks)):
+        ids = np.concatenate([[int(pending[b])], drafts[b, : blk - 1].cpu().numpy()])
+        kc = [np.zeros((cfg.n_kv_heads, caps[b], cfg.head_dim), np.float32) for _ in t.layers]
+        vc = [np.zeros((cfg.n_kv_heads, caps[b], cfg.head_dim), np.float32) for _ in t.layers]
+        for li, (k, v) in enumerate(kvs[b]):
+            kc[li][:, :L0] = k.float().cpu().numpy()
+            vc[li][:, :L0] = v.float().cpu().numpy()
+        ref_p = oracle.verify_forward(ow, oc, ids, [c.copy() for c in kc],
+                                      [c.copy() for c in vc], L0, round_p=True)
+        ref = oracle.verify_forward(ow, oc, ids, kc, vc, L0)
+        _compare(oracle, logits[cu[b] : cu[b + 1]], ref, ref_p)
+    # the same step with the wide engine off (32-row launches): same logits within the bar
+    eng.lens.copy_(lens0)
+    eng.pending.copy_(pending)
+    monkeypatch.setenv("DSPARK_WIDE_MIN_ROWS", "100000")
+    eng.step(drafts, blocks)
+    torch.cuda.synchronize()
+    small = t.logits[:R].float().cpu().numpy()
+    rel = float(np.linalg.norm(small - logits) / np.linalg.norm(small))
+    assert rel <= 2e-2, rel
