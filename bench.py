@@ -354,6 +354,7 @@ def run_ours(args):
         out["roofline"] = roofline(t, dev, pk)
         out["qmm_microbench"] = qmm_microbench(dev, pk)
         out["attn_microbench"] = attn_microbench(dev, pk)
+        out["wide_microbench"] = wide_microbench(dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             cb = cpu_forward_times(steps=2, warmup=1)
@@ -506,6 +507,36 @@ def qmm_microbench(dev, pk, rows=(1, 4, 8, 16), bits=4, n=4096, k=4096, copies=4
         gbs = _qmm_bytes(n, k, M, bits) / per / 1e9
         res[f"M{M}"] = {"us": round(per * 1e6, 3), "gbs": round(gbs, 1),
                         "frac": round(gbs / pk["hbm_gbs"], 3)}
+    return res
+
+
+def wide_microbench(dev, rows=(256, 1024, 3072), n=24576, k=4096, bits=4, reps=5) -> dict:
+    """The wide-M engine (dspark_qmm_wide, tcgen05) at the gate/up shape of the Qwen3-8B-shaped
+    model for batch-engine row counts: TFLOP/s against the measured cuBLAS bf16 peak
+    (MEASURED_PEAKS.json, burst figure for a kernel timed alone). Compute-bound from ~256 rows
+    (the weights are re-read from L2 by every 256-row x tile, not from HBM)."""
+    import torch
+
+    from mlx_dspark_b200 import quant, wide_gemm
+
+    p = ROOT / "MEASURED_PEAKS.json"
+    peak = float(json.loads(p.read_text())["bf16_tflops"]) if p.exists() else 1590.0
+    g = torch.Generator(device=dev).manual_seed(3)
+    w = quant.random_qweight(n, k, bits, device=dev, generator=g)
+    res = {"shape": f"{n}x{k} {bits}-bit", "peak_tflops": peak,
+           "peak_source": "measured" if p.exists() else "fallback"}
+    for M in rows:
+        x = torch.randn((M, k), device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty((M, n), dtype=torch.bfloat16, device=dev)
+
+        def burst():
+            for _ in range(4):
+                wide_gemm.wide(x, w.wq, w.scales, w.biases, bits, out=out)
+
+        per = _graph_time(burst, reps, dev) / 4
+        tf = 2.0 * M * n * k / per / 1e12
+        res[f"M{M}"] = {"us": round(per * 1e6, 2), "tflops": round(tf, 1),
+                        "frac": round(tf / peak, 3)}
     return res
 
 

@@ -3,7 +3,7 @@
 Modules mirror the reference operator surface (``src/mlx_dspark/``):
 
 * :mod:`.skinny_qmm` / :mod:`.small_m_qmm` — small-M affine-quantized matmul and its scoped
-  dispatch (K1),
+  dispatch (K1); :mod:`.wide_gemm` — the wide-M (prefill / batch) quantized GEMM on tcgen05,
 * :mod:`.multirow_attn` — multi-row causal GQA verify attention (K2),
 * :mod:`.kvcache` / :mod:`.batch_engine` — per-row KV cache with in-place rollback (K3) and
   the ragged continuous-batching step built on the device (K4),

@@ -264,3 +264,43 @@ def test_fp16_and_fp32_scales_do_not_fit_the_kernel():
         with pytest.raises(DSparkUnsupported, match="scales"):
             skinny_qmm.qmm(torch.zeros(2, 512, dtype=torch.bfloat16), q2.wq, q2.scales,
                            q2.biases, 4)
+
+
+# ----------------------------------------------------------------- wide-M surface (wide_gemm)
+
+def test_wide_matmul_patch_scope_restore_and_nesting():
+    """Mirrors tests/test_wide_gemm.py: disabled is a no-op, the patch applies and restores
+    (also on an exception), nesting is a no-op, the row floor is kept."""
+    from mlx_dspark_b200 import wide_gemm as wg
+
+    orig = wg.QuantizedLinear.__call__
+    with wg.wide_matmul(None):
+        assert not wg.active()
+    with wg.wide_matmul(0):
+        assert not wg.active()
+    with wg.wide_matmul(8):
+        assert wg.active() and wg._min_rows == wg.SAFE_MIN_ROWS
+        with wg.wide_matmul(512):
+            assert wg._min_rows == wg.SAFE_MIN_ROWS  # nested: the outer setting stands
+    assert wg.QuantizedLinear.__call__ is orig and not wg.active()
+    with pytest.raises(RuntimeError), wg.wide_matmul(64):
+        raise RuntimeError("boom")
+    assert not wg.active() and wg.QuantizedLinear.__call__ is orig
+    with pytest.raises(Exception, match="cpu_split"), wg.wide_matmul(64, cpu_split={"fracs": {1: 0.3}}):
+        pass
+
+
+def test_wide_eligibility():
+    from mlx_dspark_b200 import quant, small_m_qmm, wide_gemm as wg
+
+    def mod(k, bits=4, sdt=torch.bfloat16):
+        qw = quant.QWeight(torch.zeros(128, k * bits // 32, dtype=torch.int32),
+                           torch.ones(128, k // 64, dtype=sdt), torch.zeros(128, k // 64, dtype=sdt),
+                           bits)
+        return small_m_qmm.QuantizedLinear(qw)
+
+    assert wg._eligible(mod(4096)) and wg._eligible(mod(1536, 8))
+    assert not wg._eligible(mod(576))                     # K % 512 != 0
+    assert not wg._eligible(mod(4096, sdt=torch.float16))  # bf16 scales only
+    assert wg.shape_key(mod(4096)) == "4096x128x4"
+    assert wg.widest_quantized_linear([mod(1024), mod(4096)])["weight"].shape[1] == 512

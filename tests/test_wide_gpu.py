@@ -52,3 +52,30 @@ def test_wide_refuses_unaligned_k(cuda):
     rc = _lib.lib.dspark_qmm_wide(t.data_ptr(), 576, 64, 576, t.data_ptr(), t.data_ptr(),
                                   t.data_ptr(), 128, 4, t.data_ptr(), 128, None)
     assert rc == _lib.ERR_UNSUPPORTED and "512" in _lib.last_error()
+
+
+def test_wide_matmul_route_runs_the_kernel(cuda, oracle, monkeypatch):
+    """A QuantizedLinear called 300 rows wide inside wide_matmul(64) takes the wide kernel
+    (src/mlx_dspark/wide_gemm.py:173-193) and matches the oracle; a 40-row call stays on the
+    stock path; verified_shapes admits the shape."""
+    from mlx_dspark_b200 import _lib, quant, small_m_qmm, wide_gemm as wg
+
+    rng = np.random.default_rng(3)
+    N, K = 1536, 4096
+    wq, sc, bi = oracle.quantize(rng.normal(0, 0.02, (N, K)).astype(np.float32), 4)
+    mod = small_m_qmm.QuantizedLinear(quant.QWeight(
+        torch.from_numpy(wq.view(np.int32)).to(cuda), _bf(sc, cuda), _bf(bi, cuda), 4))
+    calls = []
+    real = wg.wide
+    monkeypatch.setattr(wg, "wide", lambda *a, **k: calls.append(a[0].shape[0]) or real(*a, **k))
+    x = oracle.to_bf16(rng.normal(0, 1, (300, K)))
+    xt = _bf(x, cuda).reshape(2, 150, K)
+    with wg.wide_matmul(64):
+        y = mod(xt)
+        mod(xt[:, :20])  # 40 rows: below the floor
+    assert calls == [300]
+    ref = oracle.qmm(x, wq, sc, bi, 4)
+    got = y.reshape(300, N).float().cpu().numpy()
+    assert float(np.abs(got - ref).max()) <= 1e-2 * float(np.abs(ref).max())
+    assert wg.verified_shapes([mod], 64, widths=(256,)) == [wg.shape_key(mod)]
+    assert _lib.device_status(cuda.index or 0) == 0
