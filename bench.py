@@ -61,7 +61,7 @@ def parse():
     ap.add_argument("--quick", action="store_true", help="skip e2e/roofline extras")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the tensor-parallel and batch-engine measurements of the line")
-    ap.add_argument("--micro", choices=["qmm", "attn"], default=None,
+    ap.add_argument("--micro", choices=["qmm", "attn", "attnq", "wide"], default=None,
                     help="run one kernel's microbench alone (ncu small cases)")
     ap.add_argument("--rows", type=int, nargs="+", default=[1, 4, 8, 16])
     ap.add_argument("--bits", type=int, default=4)
@@ -355,6 +355,7 @@ def run_ours(args):
         out["qmm_microbench"] = qmm_microbench(dev, pk)
         out["attn_microbench"] = attn_microbench(dev, pk)
         out["wide_microbench"] = wide_microbench(dev)
+        out["attn_q_microbench"] = attn_q_microbench(dev, pk)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             cb = cpu_forward_times(steps=2, warmup=1)
@@ -571,6 +572,42 @@ def attn_microbench(dev, pk, lengths=(1024, 4096, 16384, 32768), reps=10) -> dic
     return res
 
 
+def attn_q_microbench(dev, pk, lengths=(2048, 32768), bits=(8, 4), reps=10) -> dict:
+    """Verify attention over a quantized KV cache (the reference's kv_bits, mlx-lm's
+    QuantizedKVCache, group 64): GQA 32/8, head_dim 128, 16 causal rows. Algorithmic bytes =
+    K + V codes and their bf16 scales / biases + q + out = 8 * L * 2 * (128 * bits / 8 + 8) +
+    262144; distinct caches rotated so that >= ~400 MB streams per replay (> 3x L2)."""
+    import torch
+
+    from mlx_dspark_b200.kvcache import QuantizedKVCache
+
+    g = torch.Generator(device=dev).manual_seed(5)
+    res = {}
+    for nb in bits:
+        for L in lengths:
+            nbytes = 8 * L * 2 * (128 * nb // 8 + 8) + 262144
+            copies = max(3, -(-400_000_000 // nbytes))
+            q = torch.randn((1, 32, 16, 128), device=dev, generator=g).to(torch.bfloat16)
+            caches = []
+            for _ in range(copies):
+                c = QuantizedKVCache(1, 8, L, 128, nb, device=dev)
+                kv = torch.randn((1, 8, L, 128), device=dev, generator=g).to(torch.bfloat16)
+                c.update(kv, kv)
+                caches.append(c)
+            out = torch.empty_like(q)
+
+            def burst():
+                for c in caches:
+                    c.attention(q, scale=128 ** -0.5, causal=True, out=out)
+
+            per = _graph_time(burst, reps, dev) / copies
+            gbs = nbytes / per / 1e9
+            res[f"b{nb}_L{L}"] = {"us": round(per * 1e6, 3), "gbs": round(gbs, 1),
+                                  "frac": round(gbs / pk["hbm_gbs"], 3), "bytes": nbytes}
+            del caches
+    return res
+
+
 def run_micro(args):
     """``--micro qmm|attn``: one kernel's microbench alone (the small cases profiled with ncu).
     Prints one JSON line."""
@@ -587,6 +624,14 @@ def run_micro(args):
         r = qmm_microbench(dev, pk, rows=tuple(args.rows), bits=args.bits, n=args.n, k=args.k,
                            copies=args.copies, reps=args.reps)
         cfg = {"bits": args.bits, "n": args.n, "k": args.k, "copies": args.copies}
+    elif args.micro == "attnq":
+        r = attn_q_microbench(dev, pk, lengths=tuple(args.lengths), bits=(args.bits,),
+                              reps=args.reps)
+        cfg = {"hq": 32, "hk": 8, "qL": 16, "d": 128, "kv_bits": args.bits}
+    elif args.micro == "wide":
+        r = wide_microbench(dev, rows=tuple(args.rows), n=args.n, k=args.k, bits=args.bits,
+                            reps=args.reps)
+        cfg = {"bits": args.bits, "n": args.n, "k": args.k}
     else:
         r = attn_microbench(dev, pk, lengths=tuple(args.lengths), reps=args.reps)
         cfg = {"hq": 32, "hk": 8, "qL": 16, "d": 128}

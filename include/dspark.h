@@ -257,6 +257,40 @@ int dspark_kv_append(const void* k_new, const int64_t kn_strides[3], const void*
                      void* v_cache, const int64_t vc_strides[3], int32_t* lens, int B, int H,
                      int T, int D, int elem_size, int cap, void* stream);
 
+/* Quantized KV cache (the reference's kv_bits, src/mlx_dspark/target.py:166-185: mlx-lm's
+ * QuantizedKVCache with group size 64): keys and values stored MLX-affine quantized per group of
+ * 64 along head_dim, packed uint32 words [.., L, D*bits/32] (LSB-first, the weight format) with
+ * bf16 scales and biases [.., L, D/64], value = scale * q + bias. K and V share strides. */
+typedef struct {
+  uint32_t* kq;            /* key codes */
+  void* ks;                /* key scales (bf16) */
+  void* kb;                /* key biases (bf16) */
+  uint32_t* vq;
+  void* vs;
+  void* vb;
+  int64_t q_strides[3];    /* element strides {batch, head, row} of the code words (uint32) */
+  int64_t s_strides[3];    /* element strides {batch, head, row} of the scales / biases */
+  int bits;                /* 4 or 8 */
+} dspark_qkv;
+
+/* dspark_kv_append into a quantized cache: each new K/V row (bf16, strides {b, h, t}) is
+ * quantized per group of 64 (scale = max((max - min) / (2^bits - 1), 1e-8) in fp32, bias = min,
+ * q = round-half-even((x - bias) / scale) clamped, scale and bias stored as bf16) at row
+ * lens[b] + t, then lens[b] += T. Replaces QuantizedKVCache.update_and_fetch's
+ * mx.quantize of the block (src/mlx_dspark/target.py:182). D in {64, 128}. */
+int dspark_kv_append_q(const void* k_new, const int64_t kn_strides[3], const void* v_new,
+                       const int64_t vn_strides[3], const dspark_qkv* cache, int32_t* lens, int B,
+                       int H, int T, int D, int cap, void* stream);
+
+/* dspark_verify_attn over a quantized cache (mlx-lm's quantized_scaled_dot_product_attention
+ * route for QuantizedKVCache layers): the K/V tiles are dequantized (scale * q + bias, rounded to
+ * bf16) in shared memory and the same verify attention runs on them; q / out bf16 as in
+ * dspark_verify_attn. D in {64, 128}, bits in {4, 8}. */
+int dspark_verify_attn_q(const void* q, const int64_t q_strides[3], const dspark_qkv* kv, int B,
+                         int Hq, int Hk, int qL, int D, int L, const int32_t* kv_len, float scale,
+                         int causal, void* out, const int64_t o_strides[3], void* workspace,
+                         size_t ws_bytes, void* stream);
+
 /* In-place rollback: lens[b] = max(0, lens[b] - n_rejected[b]) on the device. Metadata only;
  * the next append overwrites the tail. Replaces KVCache.trim / Target.rollback
  * (src/mlx_dspark/target.py:679-698) and BatchCache.trim (src/mlx_dspark/batch_engine.py:220-224). */

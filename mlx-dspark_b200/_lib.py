@@ -88,6 +88,12 @@ class QmmArgs(C.Structure):
                 ("wait_state", vp)]
 
 
+class QKV(C.Structure):
+    """``dspark_qkv`` (include/dspark.h): a quantized K/V cache."""
+    _fields_ = [("kq", vp), ("ks", vp), ("kb", vp), ("vq", vp), ("vs", vp), ("vb", vp),
+                ("q_strides", i64 * 3), ("s_strides", i64 * 3), ("bits", i32)]
+
+
 EPI_PLAIN, EPI_RESID, EPI_SWIGLU, EPI_QKROPE = range(4)
 
 _SIGS = {
@@ -125,6 +131,10 @@ _SIGS = {
     "dspark_kv_append": (i32, [vp, P_i64, vp, P_i64, vp, P_i64, vp, P_i64, vp, i32, i32, i32, i32,
                                i32, i32, vp]),
     "dspark_kv_rollback": (i32, [vp, vp, i32, vp]),
+    "dspark_kv_append_q": (i32, [vp, P_i64, vp, P_i64, C.POINTER(QKV), vp, i32, i32, i32, i32,
+                                 i32, vp]),
+    "dspark_verify_attn_q": (i32, [vp, P_i64, C.POINTER(QKV), i32, i32, i32, i32, i32, i32, vp,
+                                   f32, i32, vp, P_i64, vp, sz, vp]),
     "dspark_kv_move_row": (i32, [vp, P_i64, vp, P_i64, vp, i32, i32, i32, i32, i32, i32, vp]),
     "dspark_argmax": (i32, [vp, i64, i32, i32, vp, vp]),
     "dspark_accept": (i32, [vp, vp, vp, i32, vp, vp, vp, vp]),

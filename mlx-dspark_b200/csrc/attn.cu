@@ -115,9 +115,17 @@ __device__ __forceinline__ int64_t q_base(const AttnParams& p, int b, const int6
 // DS warps share each (row tile, key slot): all of them compute the scores over the whole
 // head_dim and each keeps D / DS output columns (DS = 2 for head_dim 256 bounds the registers).
 // F16: fp16 inputs and output (the MMA type and the rounding of P follow the input type).
-template <int D, int NRT, int KS, int DS, bool F16>
-__global__ void __launch_bounds__((NRT * KS * DS + 1) * 32) attn_kernel(const AttnParams p) {
+// QB (4 or 8): the K/V cache is MLX-affine quantized (p.kq / p.vq codes, bf16 scales / biases);
+// four producer warps load the codes with 16-byte loads, dequantize (scale * q + bias, rounded to
+// bf16) into the same padded ring rows, and arrive on the stage's barrier.
+template <int QB>
+__host__ __device__ constexpr int n_producers() { return QB ? 4 : 1; }
+
+template <int D, int NRT, int KS, int DS, bool F16, int QB = 0>
+__global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
+    attn_kernel(const AttnParams p) {
   constexpr int NC = NRT * KS * DS;
+  constexpr int NP = n_producers<QB>();
   constexpr int RPG = NRT * 16;
   constexpr int ROWB = AttnSmem<D>::ROWB;
   constexpr int STG = AttnSmem<D>::STG;
@@ -153,7 +161,7 @@ __global__ void __launch_bounds__((NRT * KS * DS + 1) * 32) attn_kernel(const At
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NSLOT; ++s) {
-      mbar_init(&full[s], 32);  // one asynchronous arrival per producer lane
+      mbar_init(&full[s], 32 * NP);  // one arrival per producer lane
       mbar_init(&empty[s], NC);
     }
     fence_mbar_init();
@@ -172,7 +180,79 @@ __global__ void __launch_bounds__((NRT * KS * DS + 1) * 32) attn_kernel(const At
   const bf16* kb_ptr = p.k + (p.kv_off ? p.kv_off[b] : int64_t(b) * p.k_sb) + int64_t(hk) * p.k_sh;
   const bf16* vb_ptr = p.v + (p.kv_off ? p.kv_off[b] : int64_t(b) * p.v_sb) + int64_t(hk) * p.v_sh;
 
-  if (warp == NC) {
+  if (QB != 0 && warp >= NC) {
+    // ------------------------------------------------------------------ quantized producers
+    constexpr int NPT = NP * 32;
+    constexpr int QBE = QB ? QB : 8;           // (the branch is compiled, dead, for QB = 0)
+    constexpr int CPR = D * QBE / 8 / 16;      // 16-byte code chunks per row
+    constexpr int VPC = 128 / QBE;             // values per chunk (16 or 32)
+    constexpr int NCH = 2 * KTD * CPR;         // chunks per stage, K then V
+    constexpr int PER = NCH / NPT;             // chunks per producer thread per stage
+    static_assert(NCH % NPT == 0, "whole chunks per producer thread");
+    const int pt = (warp - NC) * 32 + lane;
+    const uint32_t* kqp = p.kq + int64_t(b) * p.kq_sb + int64_t(hk) * p.kq_sh;
+    const uint32_t* vqp = p.vq + int64_t(b) * p.kq_sb + int64_t(hk) * p.kq_sh;
+    const int64_t sofs = int64_t(b) * p.ks_sb + int64_t(hk) * p.ks_sh;
+    bool ok = true;
+    for (int st = 0; st < nst && ok; ++st) {
+      const int slot = st % NSLOT;
+      if (st >= NSLOT) ok = mbar_wait(&empty[slot], ((st / NSLOT) - 1) & 1, p.status, kErrWaitKVEmpty);
+      if (!ok) break;
+      const int kt = k0 + st * KTD;
+      constexpr int BATCH = PER < 4 ? PER : 4;  // chunks in flight per thread
+#pragma unroll
+      for (int i0 = 0; i0 < PER; i0 += BATCH) {
+        uint4 pk[BATCH];
+        float sc[BATCH], bi[BATCH];
+#pragma unroll
+        for (int i = 0; i < BATCH; ++i) {
+          const int c = pt + (i0 + i) * NPT;
+          const int kv = c / (KTD * CPR), rem = c - kv * (KTD * CPR);
+          const int row = rem / CPR, ch = rem - row * CPR;
+          const int key = kt + row;
+          const bool valid = key < kend;
+          const uint32_t* qb = (kv ? vqp : kqp) + int64_t(key) * p.kq_ss;
+          pk[i] = valid ? ldg_v4(qb + ch * 4) : make_uint4(0u, 0u, 0u, 0u);
+          const int64_t so = sofs + int64_t(key) * p.ks_ss + (ch * VPC) / 64;
+          sc[i] = valid ? bf2f((kv ? p.vsc : p.ksc)[so]) : 0.f;
+          bi[i] = valid ? bf2f((kv ? p.vbi : p.kbi)[so]) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < BATCH; ++i) {
+          const int c = pt + (i0 + i) * NPT;
+          const int kv = c / (KTD * CPR), rem = c - kv * (KTD * CPR);
+          const int row = rem / CPR, ch = rem - row * CPR;
+          uint8_t* dst = ring + slot * STG + kv * KTD * ROWB + row * ROWB + ch * VPC * 2;
+          const uint32_t w[4] = {pk[i].x, pk[i].y, pk[i].z, pk[i].w};
+#pragma unroll
+          for (int e8 = 0; e8 < VPC / 8; ++e8) {
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              // values 2e', 2e' + 1 of the chunk, e' = 4 e8 + e. A code c becomes the float
+              // 2^23 + c by placing it in the mantissa of 0x4B000000 (one byte permute for 8-bit
+              // codes, a shift and a mask for 4-bit), minus 2^23 exactly: no int->float convert.
+              constexpr int PERW = 32 / QBE;               // values per word
+              const int v0 = 2 * (4 * e8 + e), v1 = v0 + 1;
+              uint32_t m0, m1;
+              if (QBE == 8) {
+                m0 = __byte_perm(w[v0 / PERW], 0x4B000000u, 0x7540u + (v0 % PERW));
+                m1 = __byte_perm(w[v1 / PERW], 0x4B000000u, 0x7540u + (v1 % PERW));
+              } else {
+                m0 = lop3_and_or(w[v0 / PERW] >> ((v0 % PERW) * 4), 0xFu, 0x4B000000u);
+                m1 = lop3_and_or(w[v1 / PERW] >> ((v1 % PERW) * 4), 0xFu, 0x4B000000u);
+              }
+              const float f0 = __uint_as_float(m0) - 8388608.0f;
+              const float f1 = __uint_as_float(m1) - 8388608.0f;
+              o[e] = pack_bf16x2(fmaf(sc[i], f0, bi[i]), fmaf(sc[i], f1, bi[i]));
+            }
+            *reinterpret_cast<uint4*>(dst + 16 * e8) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+      }
+      mbar_arrive(&full[slot]);
+    }
+  } else if (warp == NC) {
     // ------------------------------------------------------------------ producer warp
     // 16-byte cp.async copies, lanes on consecutive chunks of a row (coalesced); keys past
     // the split's end are zero-filled without a read, so masked keys always hold finite
@@ -682,10 +762,10 @@ size_t workspace_bytes(const AttnPlan& pl, int B, int Hk, int D) {
   return size_t(B) * Hk * pl.nrg * pl.ng * (pl.nrt * 16) * (D + 4) * sizeof(float);
 }
 
-template <int D, int NRT, int KS, bool F16>
+template <int D, int NRT, int KS, bool F16, int QB = 0>
 static int launch_attn(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) {
   constexpr int DS = dsplit(D);
-  auto kern = attn_kernel<D, NRT, KS, DS, F16>;
+  auto kern = attn_kernel<D, NRT, KS, DS, F16, QB>;
   constexpr int smem = attn_smem_bytes<D, NRT, KS>();
   DSPARK_CUDA_TRY(configure_once(reinterpret_cast<const void*>(kern), 1, [&] {
                     cudaError_t e = cudaFuncSetAttribute(
@@ -696,7 +776,7 @@ static int launch_attn(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) 
                   }),
                   "attn: set smem / cluster attributes");
   dim3 grid(pl.ns, p.B * p.Hk * pl.nrg, pl.ng);
-  dim3 block((NRT * KS * DS + 1) * 32);
+  dim3 block((NRT * KS * DS + n_producers<QB>()) * 32);
   DSPARK_CUDA_TRY(launch_ex(kern, grid, block, smem, s, pl.ns, true, p), "attn: launch");
   if (pl.ng > 1) {
     const int rows = p.B * p.Hk * pl.nrg * NRT * 16;
@@ -724,6 +804,15 @@ static int dispatch_d(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) {
               D, pl.nrt, pl.ks);
 }
 
+template <int D, int QB>
+static int dispatch_q(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) {
+  if (pl.nrt == 1 && pl.ks == 2) return launch_attn<D, 1, 2, false, QB>(p, pl, s);
+  if (pl.nrt == 2 && pl.ks == 2) return launch_attn<D, 2, 2, false, QB>(p, pl, s);
+  if (pl.nrt == 4 && pl.ks == 2) return launch_attn<D, 4, 2, false, QB>(p, pl, s);
+  if (pl.nrt == 8 && pl.ks == 1) return launch_attn<D, 8, 1, false, QB>(p, pl, s);
+  return fail(DSPARK_ERR_UNSUPPORTED, "attn: no quantized-KV kernel for %d row tiles", pl.nrt);
+}
+
 template <bool F16>
 static int dispatch_t(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) {
   if (p.D == 64) return dispatch_d<64, F16>(p, pl, s);
@@ -738,9 +827,22 @@ int run(AttnParams p, const AttnPlan* plan_in, cudaStream_t stream) {
     return fail(DSPARK_ERR_UNSUPPORTED, "attn: head_dim %d not supported (64, 128, 256)", p.D);
   if (p.qL > 32 && p.tree_anc)
     return fail(DSPARK_ERR_UNSUPPORTED, "attn: tree verify supports at most 32 rows");
-  const uintptr_t al = reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v);
-  if ((al & 15) || ((p.k_sb | p.k_sh | p.k_ss | p.v_sb | p.v_sh | p.v_ss) & 7))
-    return fail(DSPARK_ERR_UNSUPPORTED, "attn: K/V rows must be 16-byte aligned (strides %% 8 == 0)");
+  if (p.qbits) {
+    if (p.qbits != 4 && p.qbits != 8) return fail(DSPARK_ERR_UNSUPPORTED, "attn: %d-bit KV", p.qbits);
+    if (p.D != 64 && p.D != 128)
+      return fail(DSPARK_ERR_UNSUPPORTED, "attn: quantized KV needs head_dim 64 or 128 (got %d)", p.D);
+    if (p.f16 || p.kv_off || p.tree_anc)
+      return fail(DSPARK_ERR_UNSUPPORTED, "attn: quantized KV serves bf16, dense rows, causal / full rules");
+    if (!p.kq || !p.vq || !p.ksc || !p.kbi || !p.vsc || !p.vbi)
+      return fail(DSPARK_ERR_ARG, "attn: null quantized K/V pointer");
+    const uintptr_t qa = reinterpret_cast<uintptr_t>(p.kq) | reinterpret_cast<uintptr_t>(p.vq);
+    if ((qa & 15) || ((p.kq_sb | p.kq_sh | p.kq_ss) & 3))
+      return fail(DSPARK_ERR_UNSUPPORTED, "attn: K/V code rows must be 16-byte aligned");
+  } else {
+    const uintptr_t al = reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v);
+    if ((al & 15) || ((p.k_sb | p.k_sh | p.k_ss | p.v_sb | p.v_sh | p.v_ss) & 7))
+      return fail(DSPARK_ERR_UNSUPPORTED, "attn: K/V rows must be 16-byte aligned (strides %% 8 == 0)");
+  }
   if ((reinterpret_cast<uintptr_t>(p.q) & 3) || (reinterpret_cast<uintptr_t>(p.o) & 7) ||
       ((p.q_sb | p.q_sh | p.q_si) & 1) || ((p.o_sb | p.o_sh | p.o_si) & 3))
     return fail(DSPARK_ERR_UNSUPPORTED, "attn: q rows need 4-byte and output rows 8-byte alignment");
@@ -758,6 +860,10 @@ int run(AttnParams p, const AttnPlan* plan_in, cudaStream_t stream) {
     return fail(DSPARK_ERR_ARG, "attn: this launch needs a workspace of %zu bytes",
                 workspace_bytes(pl, p.B, p.Hk, p.D));
   if (p.status == nullptr) p.status = status_word(current_device());
+  if (p.qbits) {
+    if (p.D == 64) return p.qbits == 8 ? dispatch_q<64, 8>(p, pl, stream) : dispatch_q<64, 4>(p, pl, stream);
+    return p.qbits == 8 ? dispatch_q<128, 8>(p, pl, stream) : dispatch_q<128, 4>(p, pl, stream);
+  }
   return p.f16 ? dispatch_t<true>(p, pl, stream) : dispatch_t<false>(p, pl, stream);
 }
 

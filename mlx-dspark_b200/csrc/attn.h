@@ -36,6 +36,16 @@ struct AttnParams {
   int chunk = 64;     // keys per split (multiple of the kernel's key tile, 64 or 32)
   float* ws = nullptr;  // workspace (ng > 1): [B*Hk*nrg][ng][rows][D+2] fp32
   int* status = nullptr;
+  // quantized K/V (qbits 4 or 8; k / v unused): codes [.., L, D*qbits/32] uint32 at strides
+  // {kq_sb, kq_sh, kq_ss} (words), bf16 scales / biases at {ks_sb, ks_sh, ks_ss} (elements)
+  int qbits = 0;
+  const uint32_t* kq = nullptr;
+  const uint32_t* vq = nullptr;
+  const __nv_bfloat16* ksc = nullptr;
+  const __nv_bfloat16* kbi = nullptr;
+  const __nv_bfloat16* vsc = nullptr;
+  const __nv_bfloat16* vbi = nullptr;
+  int64_t kq_sb = 0, kq_sh = 0, kq_ss = 0, ks_sb = 0, ks_sh = 0, ks_ss = 0;
 };
 
 struct AttnPlan {

@@ -413,6 +413,38 @@ int dspark_verify_attn_dt(int dtype, const void* q, const int64_t q_strides[3], 
   return attn::run(p, &pl, as_stream(stream));
 }
 
+int dspark_verify_attn_q(const void* q, const int64_t q_strides[3], const dspark_qkv* kv, int B,
+                         int Hq, int Hk, int qL, int D, int L, const int32_t* kv_len, float scale,
+                         int causal, void* out, const int64_t o_strides[3], void* workspace,
+                         size_t ws_bytes, void* stream) {
+  if (!q || !kv || !out || !q_strides || !o_strides)
+    return fail(DSPARK_ERR_ARG, "verify_attn_q: null pointer");
+  attn::AttnParams p;
+  p.q = static_cast<const bf16*>(q);
+  p.q_sb = q_strides[0]; p.q_sh = q_strides[1]; p.q_si = q_strides[2];
+  p.o = static_cast<bf16*>(out);
+  p.o_sb = o_strides[0]; p.o_sh = o_strides[1]; p.o_si = o_strides[2];
+  p.qbits = kv->bits;
+  p.kq = kv->kq; p.vq = kv->vq;
+  p.ksc = static_cast<const bf16*>(kv->ks); p.kbi = static_cast<const bf16*>(kv->kb);
+  p.vsc = static_cast<const bf16*>(kv->vs); p.vbi = static_cast<const bf16*>(kv->vb);
+  p.kq_sb = kv->q_strides[0]; p.kq_sh = kv->q_strides[1]; p.kq_ss = kv->q_strides[2];
+  p.ks_sb = kv->s_strides[0]; p.ks_sh = kv->s_strides[1]; p.ks_ss = kv->s_strides[2];
+  p.kv_len = kv_len;
+  p.B = B; p.Hq = Hq; p.Hk = Hk; p.qL = qL; p.D = D; p.L = L;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.causal = causal;
+  attn::AttnPlan pl = attn::plan(B, Hq, Hk, qL, D, L);
+  if (D > 128) return fail(DSPARK_ERR_UNSUPPORTED, "verify_attn_q: head_dim %d (64, 128)", D);
+  const size_t need = attn::workspace_bytes(pl, B, Hk, D);
+  if (need > 0) {
+    if (workspace == nullptr || ws_bytes < need)
+      return fail(DSPARK_ERR_ARG, "verify_attn_q: needs %zu bytes of workspace (got %zu)", need, ws_bytes);
+    p.ws = static_cast<float*>(workspace);
+  }
+  return attn::run(p, &pl, as_stream(stream));
+}
+
 int dspark_verify_attn(const void* q, const int64_t q_strides[3], const void* k,
                        const int64_t k_strides[3], const void* v, const int64_t v_strides[3],
                        int B, int Hq, int Hk, int qL, int D, int L, const int32_t* kv_len,

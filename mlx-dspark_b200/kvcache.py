@@ -15,6 +15,8 @@ the mirror with :meth:`sync_offsets`.
 
 from __future__ import annotations
 
+import ctypes as C
+
 import torch
 
 from . import _lib
@@ -146,3 +148,72 @@ def rollback(lens: torch.Tensor, n_rejected: torch.Tensor) -> None:
     require_cuda(lens, n_rejected)
     _lib.check(_lib.lib.dspark_kv_rollback(ptr(lens), ptr(n_rejected), int(lens.numel()),
                                            stream_of(lens)))
+
+
+class QuantizedKVCache:
+    """A quantized per-row KV cache for one layer (the reference's ``kv_bits`` path,
+    src/mlx_dspark/target.py:166-185: mlx-lm's ``QuantizedKVCache(group_size=64, bits)``).
+
+    Keys and values are stored MLX-affine quantized per group of 64 along head_dim: code words
+    ``uint32 [B, H, cap, D*bits/32]`` and bf16 scales / biases ``[B, H, cap, D/64]``. ``lens``
+    (device int32 ``[B]``) is each row's cached length; :meth:`update` quantizes a block of new
+    rows at those lengths (``dspark_kv_append_q``), :meth:`trim` is the same metadata-only
+    rollback as the bf16 cache, and :meth:`attention` runs the verify attention over the
+    quantized rows (``dspark_verify_attn_q``)."""
+
+    def __init__(self, B: int, H: int, cap: int, D: int, bits: int = 8, device="cuda"):
+        if bits not in (4, 8) or D not in (64, 128):
+            raise _lib.DSparkUnsupported(_lib.ERR_UNSUPPORTED, f"{bits}-bit KV, head_dim {D}")
+        self.B, self.H, self.cap, self.D, self.bits = int(B), int(H), int(cap), int(D), int(bits)
+        w = D * bits // 32
+        dev = torch.device(device)
+        u32 = dict(dtype=torch.int32, device=dev)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.kq = torch.zeros((B, H, cap, w), **u32)
+        self.vq = torch.zeros((B, H, cap, w), **u32)
+        self.ks = torch.zeros((B, H, cap, D // 64), **bf)
+        self.kb = torch.zeros((B, H, cap, D // 64), **bf)
+        self.vs = torch.zeros((B, H, cap, D // 64), **bf)
+        self.vb = torch.zeros((B, H, cap, D // 64), **bf)
+        self.lens = torch.zeros(B, dtype=torch.int32, device=dev)
+        require_cuda(self.kq)
+        self._c = _lib.QKV(ptr(self.kq), ptr(self.ks), ptr(self.kb), ptr(self.vq), ptr(self.vs),
+                           ptr(self.vb), (C.c_int64 * 3)(*elem_strides(self.kq)),
+                           (C.c_int64 * 3)(*elem_strides(self.ks)), self.bits)
+
+    @property
+    def offset(self) -> list[int]:
+        return [int(x) for x in self.lens.tolist()]
+
+    def update(self, k_new: torch.Tensor, v_new: torch.Tensor) -> None:
+        """Quantize ``[B, H, T, D]`` bf16 rows into each row's next T positions."""
+        require_cuda(k_new, v_new)
+        B, H, T, D = (int(s) for s in k_new.shape)
+        _lib.check(_lib.lib.dspark_kv_append_q(
+            ptr(k_new), _lib.i64_array(elem_strides(k_new)), ptr(v_new),
+            _lib.i64_array(elem_strides(v_new)), C.byref(self._c), ptr(self.lens), B, H, T, D,
+            self.cap, stream_of(k_new)))
+
+    def trim(self, n_rejected: torch.Tensor) -> None:
+        """``lens -= n_rejected`` clamped at 0 on the device (metadata only)."""
+        _lib.check(_lib.lib.dspark_kv_rollback(ptr(self.lens), ptr(n_rejected), self.B,
+                                               stream_of(self.lens)))
+
+    def attention(self, q: torch.Tensor, *, scale: float, causal: bool = True,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+        """Verify attention of ``q [B, Hq, qL, D]`` (bf16) over each row's ``lens[b]`` cached
+        keys (the quantized_scaled_dot_product_attention route of mlx-lm for this cache)."""
+        from .multirow_attn import _workspace, workspace_bytes
+
+        require_cuda(q)
+        B, Hq, qL, D = (int(s) for s in q.shape)
+        if out is None:
+            out = torch.empty_like(q)
+        L = self.cap
+        ws_n = workspace_bytes(Hq, self.H, qL, D, L, B)
+        ws = _workspace(q.device, ws_n)
+        _lib.check(_lib.lib.dspark_verify_attn_q(
+            ptr(q), _lib.i64_array(elem_strides(q)), C.byref(self._c), B, Hq, self.H, qL, D, L,
+            ptr(self.lens), float(scale), int(bool(causal)), ptr(out),
+            _lib.i64_array(elem_strides(out)), ptr(ws), ws_n, stream_of(q)))
+        return out

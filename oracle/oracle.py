@@ -425,3 +425,43 @@ def verify_forward(weights: dict, cfg: dict, ids, kcache: list, vcache: list, L0
     x = rmsnorm(h, weights["final_norm"], eps)
     lm = weights["lm_head"]
     return qmm(to_bf16(x), lm["wq"], lm["scales"], lm["biases"], lm["bits"])
+
+
+# ----------------------------------------------------------------------------- quantized KV
+
+def quantize_rows(x, bits: int):
+    """Quantize rows [..., D] per group of 64 (the build's affine quantizer, as the device
+    append kernel does): returns (codes uint32 [..., D*bits/32], scales u16 bf16 [..., D/64],
+    biases u16 bf16). Same rule as :func:`quantize` (fp32 scale for the codes, bf16 storage)."""
+    x = np.asarray(x, dtype=np.float32)
+    lead, D = x.shape[:-1], x.shape[-1]
+    wq, sc, bi = quantize(x.reshape(-1, D), bits)
+    return (wq.reshape(*lead, D * bits // 32), sc.reshape(*lead, D // 64),
+            bi.reshape(*lead, D // 64))
+
+
+def sdpa_q(q_bits, kq, ks, kb, vq, vs, vb, bits: int, lens, scale: float, causal: bool):
+    """Verify attention over a quantized cache (mlx-lm's quantized SDPA for QuantizedKVCache):
+    K / V dequantized exactly in fp32 (scale * q + bias), fp32 softmax. q bf16 bit patterns
+    [B, Hq, qL, D]; codes [B, Hk, cap, D*bits/32]; row b sees its first lens[b] keys, causal
+    rule key <= lens[b] - qL + i. Returns fp32 [B, Hq, qL, D]."""
+    q = from_bf16(np.asarray(q_bits, dtype=np.uint16))
+    B, Hq, qL, D = q.shape
+    Hk = kq.shape[1]
+    G = Hq // Hk
+    out = np.zeros((B, Hq, qL, D), np.float32)
+    for b in range(B):
+        L = int(lens[b])
+        for hk in range(Hk):
+            K = dequantize(kq[b, hk, :L], ks[b, hk, :L], kb[b, hk, :L], bits)
+            V = dequantize(vq[b, hk, :L], vs[b, hk, :L], vb[b, hk, :L], bits)
+            for g in range(G):
+                s = q[b, hk * G + g] @ K.T * np.float32(scale)
+                if causal:
+                    j = np.arange(L)[None, :]
+                    i = np.arange(qL)[:, None]
+                    s = np.where(j <= L - qL + i, s, -np.inf)
+                s = s - s.max(axis=1, keepdims=True)
+                p = np.exp(s)
+                out[b, hk * G + g] = (p / p.sum(axis=1, keepdims=True)) @ V
+    return out

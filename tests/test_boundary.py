@@ -216,7 +216,7 @@ def test_tree_bits():
 
 _MIRRORS = {"QWeight": "dspark_qweight", "Layer": "dspark_layer", "Model": "dspark_model",
             "FwdBuffers": "dspark_fwd_buffers", "P2PGatherArgs": "dspark_p2p_gather_args",
-            "QmmArgs": "dspark_qmm_args"}
+            "QmmArgs": "dspark_qmm_args", "QKV": "dspark_qkv"}
 
 
 def test_ctypes_mirrors_match_the_header_layout(tmp_path):
