@@ -422,40 +422,55 @@ def _qmm_bytes(n, k, m, bits):
     return n * k * bits // 8 + n * (k // 64) * 4 + m * k * 2 + m * n * 2
 
 
-def _profiled_traffic():
-    """DRAM bytes (read + write) per launch of the roofline kernel, from the committed ncu
-    summary of the same kernel and shape (profiles/qmm_st_gate_up_4bit_m16.md)."""
-    import re
-
-    f = ROOT / "profiles" / "qmm_st_gate_up_4bit_m16.md"
-    if not f.exists():
-        return None
-    m = re.search(r"traffic per launch\) \| ([\d,]+) bytes", f.read_text())
-    return int(m.group(1).replace(",", "")) if m else None
+# DRAM bytes (read + write) of one launch of the step's gate/up instance (RMSNorm prologue,
+# SwiGLU epilogue, 16 rows), from an ncu capture of the verify step itself:
+#   python bench.py --steps 3 --warmup 3 --quick --no-cpu-baseline --no-extras
+#   ncu --clock-control none --kernel-name-base demangled -k "regex:qmm_st_kernel<\\(int\\)4, \\(int\\)2, \\(int\\)2"
+#       -s 8 -c 1 --section SpeedOfLight --section MemoryWorkloadAnalysis <the same command>
+# dram__bytes.sum.per_second 1.638085 TB/s x gpu__time_duration.sum 34.752 us (cold, under ncu)
+GATEUP_SWIGLU_TRAFFIC = 56_926_730
 
 
 def roofline(t, dev, pk) -> dict:
-    """Dominant kernel: the gate/up QMM (N = 24576, K = 4096, 16 rows). Back-to-back launches
-    over all 36 layers' weights (2 GB, no L2 reuse), CUDA events on the launching stream."""
+    """Dominant kernel: the step's gate/up QMM instance (N = 24576, K = 4096, 16 rows, RMSNorm
+    prologue from per-tile statistics, SwiGLU epilogue), launched back to back on all 36 layers'
+    weights (2 GB, no L2 reuse), CUDA events on the launching stream."""
+    import ctypes as C
+
     import torch
 
-    from mlx_dspark_b200 import skinny_qmm
+    from mlx_dspark_b200 import _lib
+    from mlx_dspark_b200._torch import ptr
 
     cfg = t.cfg
-    x = torch.randn((ROWS, cfg.hidden), device=dev).to(torch.bfloat16)
-    out = torch.empty((ROWS, 2 * cfg.intermediate), dtype=torch.bfloat16, device=dev)
-    ws = [L["gate_up"] for L in t.layers]
+    H, I = cfg.hidden, cfg.intermediate
+    g = torch.Generator(device=dev).manual_seed(2)
+    x = torch.randn((ROWS, H), device=dev, generator=g).to(torch.bfloat16)
+    ssq = (x.float() ** 2).reshape(ROWS, H // 128, 128).sum(-1).t().contiguous()  # [tiles, rows]
+    act = torch.empty((ROWS, I), dtype=torch.bfloat16, device=dev)
+    args = []
+    for L in t.layers:
+        w = L["gate_up"]
+        a = _lib.QmmArgs()
+        a.x, a.ldx, a.M, a.K, a.N, a.bits = ptr(x), H, ROWS, H, 2 * I, w.bits
+        a.wq, a.scales, a.biases = ptr(w.wq), ptr(w.scales), ptr(w.biases)
+        a.out, a.ldo, a.epilogue, a.n_act = ptr(act), I, _lib.EPI_SWIGLU, I
+        a.norm_w, a.ssq_in, a.ssq_n, a.ssq_stride = ptr(L["post_norm"]), ptr(ssq), H // 128, ROWS
+        a.eps = cfg.rms_eps
+        args.append(a)
 
     def burst():
-        for w in ws:
-            skinny_qmm.qmm(x, w.wq, w.scales, w.biases, w.bits, out=out)
+        s = torch.cuda.current_stream(dev).cuda_stream
+        for a in args:
+            _lib.check(_lib.lib.dspark_qmm_fused(C.byref(a), s))
 
-    per = _graph_time(burst, 10, dev) / len(ws)
-    nbytes = _qmm_bytes(2 * cfg.intermediate, cfg.hidden, ROWS, cfg.bits)
+    per = _graph_time(burst, 10, dev) / len(args)
+    nbytes = _qmm_bytes(2 * I, H, ROWS, cfg.bits)
     ach = nbytes / per / 1e9
-    return {"kernel": "qmm_st_kernel<4, 2, EPI> (gate/up 24576x4096, 4-bit, 16 rows)", "bound": "hbm",
+    return {"kernel": "qmm_st_kernel<4, 2, EPI_SWIGLU> (gate/up 24576x4096, 4-bit, 16 rows, "
+                      "RMSNorm prologue)", "bound": "hbm",
             "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-            "frac": round(ach / pk["hbm_gbs"], 3), "traffic": _profiled_traffic(),
+            "frac": round(ach / pk["hbm_gbs"], 3), "traffic": GATEUP_SWIGLU_TRAFFIC,
             "algorithmic_bytes_per_launch": nbytes, "us_per_launch": round(per * 1e6, 2),
             "peak_source": pk["src"]}
 

@@ -384,30 +384,41 @@ __device__ __forceinline__ void stage_block_tc(const QmmParams& p, uint8_t* xs, 
 // sits between the loads. One warp per row.
 __device__ __forceinline__ void norm_stats(const QmmParams& p, float* rsm, int rp, int m0,
                                            int mstep, int lane) {
-  for (int m = m0; m < rp; m += mstep) {
-    float ss = 0.f;
-    if (m < p.M) {
-      const int sg = p.ssq_seg;
-      int sseg = 0, soff = lane;
-      if (sg) {
-        sseg = lane / sg;
-        soff = lane - sseg * sg;
-      }
-      for (int e = lane; e < p.ssq_n; e += 32) {
-        const long at = sg ? sseg * p.ssq_segstride + long(soff) * p.ssq_stride
-                           : long(e) * p.ssq_stride;
-        ss += __ldcg(&p.ssq_in[at + m]);
-        soff += 32;
-        if (sg)
-          while (soff >= sg) {
-            soff -= sg;
-            ++sseg;
-          }
-      }
-    }
+  // every row's loads are issued before any reduction (one global-memory latency in all, not
+  // one per row); each row's entries are still summed in the same order (lane-strided, then a
+  // fixed shuffle tree), so the result is unchanged
+  constexpr int MAXR = 8;  // rows per warp: rp <= 32 rows over mstep >= 4 warps
+  float ss[MAXR];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) rsm[m] = m < p.M ? rsqrtf(ss / float(p.K) + p.eps) : 0.f;
+  for (int i = 0; i < MAXR; ++i) ss[i] = 0.f;
+  const int sg = p.ssq_seg;
+  int sseg = 0, soff = lane;
+  if (sg) {
+    sseg = lane / sg;
+    soff = lane - sseg * sg;
+  }
+  for (int e = lane; e < p.ssq_n; e += 32) {
+    const long at = sg ? sseg * p.ssq_segstride + long(soff) * p.ssq_stride
+                       : long(e) * p.ssq_stride;
+#pragma unroll
+    for (int i = 0; i < MAXR; ++i) {
+      const int m = m0 + i * mstep;
+      if (m < rp && m < p.M) ss[i] += __ldcg(&p.ssq_in[at + m]);
+    }
+    soff += 32;
+    if (sg)
+      while (soff >= sg) {
+        soff -= sg;
+        ++sseg;
+      }
+  }
+#pragma unroll
+  for (int i = 0; i < MAXR; ++i) {
+    const int m = m0 + i * mstep;
+    float v = ss[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0 && m < rp) rsm[m] = m < p.M ? rsqrtf(v / float(p.K) + p.eps) : 0.f;
   }
 }
 
