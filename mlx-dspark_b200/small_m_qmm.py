@@ -106,7 +106,9 @@ def shape_key(mod) -> str:
 
 
 def _mma_call(self, x):  # small_m_qmm.py:71-80
-    if _active_ids is None or id(self) not in _active_ids or x.dtype != torch.bfloat16:
+    # an allow-listed layer the kernel cannot read (fp16 / fp32 scales) keeps the stock path
+    if (_active_ids is None or id(self) not in _active_ids or x.dtype != torch.bfloat16
+            or not _sk.fits(self)):
         return _orig_call(self, x)
     M = 1
     for d in x.shape[:-1]:
