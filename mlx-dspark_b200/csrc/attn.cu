@@ -170,15 +170,38 @@ __global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
   pdl_launch_dependents();
   pdl_wait();  // q and the freshly appended cache rows come from the previous kernel
 
-  const int Lb = p.kv_len ? p.kv_len[b] : p.L;
-  const int qLb = p.q_len ? p.q_len[b] : p.qL;
+  // The request's scalars (keys, query rows, cache offset, first packed row). When they come
+  // from device arrays, one thread reads them and shares them through shared memory: every CTA
+  // of the launch reads the same words at the same moment, and one request per CTA instead of
+  // one per warp keeps their L2 line from queueing (the four loads issue together).
+  int64_t* scal = reinterpret_cast<int64_t*>(empty + NSLOT);  // in the layout's 128-byte tail
+  const bool dev_scalars = p.kv_len || p.q_len || p.kv_off || p.row_start;
+  if (dev_scalars) {
+    if (threadIdx.x == 0) {
+      const int lb = p.kv_len ? p.kv_len[b] : p.L;
+      const int ql = p.q_len ? p.q_len[b] : p.qL;
+      const int64_t ko = p.kv_off ? p.kv_off[b] : 0;
+      const int rs = p.row_start ? p.row_start[b] : 0;
+      scal[0] = lb;
+      scal[1] = ql;
+      scal[2] = ko;
+      scal[3] = rs;
+    }
+    __syncthreads();
+  }
+  const int Lb = dev_scalars ? int(scal[0]) : p.L;
+  const int qLb = dev_scalars ? int(scal[1]) : p.qL;
+  // q_base of this request: packed rows (row_start) or batch strides
+  auto qbase = [&](int64_t sb, int64_t si) {
+    return p.row_start ? scal[3] * si : int64_t(b) * sb;
+  };
   const int split = g_grp * p.ns + sidx_c;
   const int k0 = min(Lb, split * p.chunk);
   const int kend = min(Lb, k0 + p.chunk);
   const int nst = (kend - k0 + KTD - 1) / KTD;
 
-  const bf16* kb_ptr = p.k + (p.kv_off ? p.kv_off[b] : int64_t(b) * p.k_sb) + int64_t(hk) * p.k_sh;
-  const bf16* vb_ptr = p.v + (p.kv_off ? p.kv_off[b] : int64_t(b) * p.v_sb) + int64_t(hk) * p.v_sh;
+  const bf16* kb_ptr = p.k + (p.kv_off ? scal[2] : int64_t(b) * p.k_sb) + int64_t(hk) * p.k_sh;
+  const bf16* vb_ptr = p.v + (p.kv_off ? scal[2] : int64_t(b) * p.v_sb) + int64_t(hk) * p.v_sh;
 
   if (QB != 0 && warp >= NC) {
     // ------------------------------------------------------------------ quantized producers
@@ -311,7 +334,7 @@ __global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
     // Q fragments in registers
     uint32_t qf[NKK][4];
     {
-      const int64_t qb = q_base(p, b, p.q_sb, p.q_si);
+      const int64_t qb = qbase(p.q_sb, p.q_si);
       const bf16* q0 = pr0 < nrows ? p.q + qb + int64_t(hk * G + pr0 / qLb) * p.q_sh + int64_t(qi0) * p.q_si : nullptr;
       const bf16* q1 = pr1 < nrows ? p.q + qb + int64_t(hk * G + pr1 / qLb) * p.q_sh + int64_t(qi1) * p.q_si : nullptr;
 #pragma unroll
@@ -531,7 +554,7 @@ __global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
     }
     cluster_sync_all();  // pushes visible to their owners
   }
-  const int64_t ob = q_base(p, b, p.o_sb, p.o_si);
+  const int64_t ob = qbase(p.o_sb, p.o_si);
   const int nrows = G * qLb;
   for (int idx = threadIdx.x; idx < ro * (D / 4); idx += blockDim.x) {
     const int rl = idx / (D / 4), d4 = (idx % (D / 4)) * 4;

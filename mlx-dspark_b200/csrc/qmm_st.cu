@@ -422,6 +422,53 @@ __device__ __forceinline__ void norm_stats(const QmmParams& p, float* rsm, int r
   }
 }
 
+// Row width (floats, a multiple of 4) of the statistics block staged by norm_stats_staged, or 0
+// when the block does not qualify (segmented, unaligned, or larger than the scratch).
+__device__ __forceinline__ int ssq_stage_width(const QmmParams& p, int rp, int scratch_floats) {
+  const int w = (min(p.M, rp) + 3) & ~3;
+  if (p.ssq_seg || (reinterpret_cast<uintptr_t>(p.ssq_in) & 15) || (p.ssq_stride & 3) ||
+      w > p.ssq_stride || p.ssq_n * w > scratch_floats)
+    return 0;
+  return w;
+}
+
+// norm_stats for a contiguous statistics block. The block (ssq_n entries x the launch's rows, a
+// few KB) is read by every CTA of the launch at the same moment; per-row strided loads made
+// hundreds of line requests per CTA, which queued at the lines' L2 slices (measured: ~2.5 us for
+// the one round trip). Here the epilogue threads first copy it into shared memory with 16-byte
+// loads (a few line requests per CTA), then each warp sums its rows from there in the same order
+// as norm_stats (lane-strided over entries, then the fixed shuffle tree): the same rs bits.
+__device__ __forceinline__ void norm_stats_staged(const QmmParams& p, float* rsm, int rp, int w,
+                                                  float* scratch, int etid, int m0, int mstep,
+                                                  int lane) {
+  const int w4 = w / 4;
+  for (int i = etid; i < p.ssq_n * w4; i += NE) {
+    const int e = i / w4, c = i - e * w4;
+    *reinterpret_cast<float4*>(&scratch[e * w + c * 4]) =
+        __ldcg(reinterpret_cast<const float4*>(&p.ssq_in[long(e) * p.ssq_stride + c * 4]));
+  }
+  asm volatile("bar.sync 2, %0;" ::"n"(NE));  // the block is staged
+  constexpr int MAXR = 8;
+  float ss[MAXR];
+#pragma unroll
+  for (int i = 0; i < MAXR; ++i) ss[i] = 0.f;
+  for (int e = lane; e < p.ssq_n; e += 32) {
+#pragma unroll
+    for (int i = 0; i < MAXR; ++i) {
+      const int m = m0 + i * mstep;
+      if (m < rp && m < p.M) ss[i] += scratch[e * w + m];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < MAXR; ++i) {
+    const int m = m0 + i * mstep;
+    float v = ss[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0 && m < rp) rsm[m] = m < p.M ? rsqrtf(v / float(p.K) + p.eps) : 0.f;
+  }
+}
+
 // Stage k block kb (512 k: chunks c = 64kb .. 64kb + 63 of the K slice) of every row of x into
 // shared memory (rows of XP bytes), by 128 threads: thread t takes chunk column 64kb + t % 64 and
 // rows t / 64, t / 64 + 2, ..., U loads in flight at once (16-byte global loads). Each chunk is
@@ -836,7 +883,12 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
       }
       const bool nrm = p.norm_w != nullptr;
       if (nrm) {
-        norm_stats(p, rsm, RP, warp - WARP_EPI, NWE, lane);
+        // `red` (the reduced-tile scratch) is free until the first tile's epilogue
+        const int sw = ssq_stage_width(p, RP, RP * PSTR);
+        if (sw)
+          norm_stats_staged(p, rsm, RP, sw, red, etid, warp - WARP_EPI, NWE, lane);
+        else
+          norm_stats(p, rsm, RP, warp - WARP_EPI, NWE, lane);
         asm volatile("bar.sync 2, %0;" ::"n"(NE));  // rs of every row
       }
       for (int kb = 0; kb < kvalid / KBLK; ++kb) {
