@@ -693,6 +693,18 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
     const uint32_t xa = smem_u32(xs) + uint32_t(g8 * XP + t4 * 32);
     // swizzled byte offset of (row, logical 16-byte chunk c) inside a stage
     auto wofs = [](int row, int c) { return uint32_t(row * 128 + ((c ^ (row & 7)) << 4)); };
+    // 4-bit: the thread's weight offsets inside a stage are the same every stage (row group,
+    // row half, group of the warp's k half): computed once, not per load
+    uint32_t woff[2][2][GH];
+#pragma unroll
+    for (int rg = 0; rg < 2; ++rg)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int gg = 0; gg < GH; ++gg)
+          woff[rg][h][gg] = BITS == 4 ? wofs(rows[rg][h], (half * GH + gg) * 2 + (t4 >> 1)) +
+                                            uint32_t((t4 & 1) * 8)
+                                      : 0u;
 
     // ring slot and phase of the next stage, scale slot of the next block (counted, not divided)
     int slot = 0, phase = 0, sslot = 0;
@@ -755,10 +767,8 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
                 for (int i = 0; i < 4; ++i) pr[mt][i] = 0.f;
               if (BITS == 4) {
                 // 8 bytes of each row: group bytes 8*t4 .. 8*t4+7 = k 16*t4 .. 16*t4+15
-                const int c = gi * 2 + (t4 >> 1);
-                const uint32_t lo8 = uint32_t((t4 & 1) * 8);
-                const uint2 w0 = lds64(wb + wofs(r0, c) + lo8);
-                const uint2 w1 = lds64(wb + wofs(r1, c) + lo8);
+                const uint2 w0 = lds64(wb + woff[rg][0][gg]);
+                const uint2 w1 = lds64(wb + woff[rg][1][gg]);
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
                   const uint32_t x0 = (s < 2) ? w0.x : w0.y;
