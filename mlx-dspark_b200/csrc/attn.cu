@@ -727,6 +727,15 @@ AttnPlan plan(int B, int Hq, int Hk, int qL, int D, int L) {
   else nrt = 8;
   // head_dim 256: at most 4 row tiles per CTA (shared memory) and one key slot (32-key stages)
   if (D > 128) nrt = std::min(nrt, 4);
+  // Up to 4k keys, two row tiles per CTA (twice the row groups, each streaming the head's keys,
+  // the second from L2) beat four. Measured at 16 rows x 4 heads per KV head, 1k / 2k / 4k keys:
+  // 10.4 / 12.9 / 18.4 us with four row tiles, 8.9 / 11.9 / 16.9 us with two; at 32k keys four
+  // win (56.8 against 66.5 us). DSPARK_ATTN_NRT (1, 2 or 4) forces a cap, for tuning.
+  const int force_nrt = env_int("DSPARK_ATTN_NRT", 0);
+  if (force_nrt == 1 || force_nrt == 2 || (force_nrt == 4 && D <= 128))
+    nrt = std::min(nrt, force_nrt);
+  else if (D <= 128 && L <= 4096)
+    nrt = std::min(nrt, 2);
   pl.nrt = nrt;
   pl.ks = (nrt >= 8 || D > 128) ? 1 : 2;
   const int kt = ktile(D);
