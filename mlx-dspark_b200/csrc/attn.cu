@@ -21,6 +21,7 @@
 // when more splits are needed than a cluster holds) cluster groups merge through a workspace.
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -95,9 +96,22 @@ __host__ __device__ constexpr int attn_recv_bytes() {
   return (NRT * 16 + 16) * (D + 4) * 4;
 }
 
+// + 1 KB: the base is aligned to 1024 bytes in the kernel (128-byte swizzled TMA destinations)
 template <int D, int NRT, int KS>
 __host__ __device__ constexpr int attn_smem_bytes() {
-  return attn_core_bytes<D, NRT, KS>() + attn_recv_bytes<D, NRT>();
+  return attn_core_bytes<D, NRT, KS>() + attn_recv_bytes<D, NRT>() + 1024;
+}
+
+// Byte offset of (key, d) inside a K or V tile. The cp.async ring keeps padded rows of ROWB
+// bytes; the TMA ring (TM) keeps D/64 boxes of [KTD keys x 128 bytes] with the 128-byte swizzle
+// (16-byte chunk c of a row r stored at chunk c ^ (r & 7)), so the 8 rows one ldmatrix phase
+// reads always sit on 8 different bank groups. d is a multiple of 8.
+template <bool TM, int KTD, int ROWB>
+__device__ __forceinline__ uint32_t kv_off_in_tile(int key, int d) {
+  if constexpr (TM)
+    return uint32_t((d >> 6) * (KTD * 128) + key * 128 + ((((d >> 3) & 7) ^ (key & 7)) << 4));
+  else
+    return uint32_t(key * ROWB + d * 2);
 }
 
 // 2^x by the hardware approximation (ex2.approx.ftz: ~2 ulp; exact 0 for -inf)
@@ -121,9 +135,12 @@ __device__ __forceinline__ int64_t q_base(const AttnParams& p, int b, const int6
 template <int QB>
 __host__ __device__ constexpr int n_producers() { return QB ? 4 : 1; }
 
-template <int D, int NRT, int KS, int DS, bool F16, int QB = 0>
-__global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
-    attn_kernel(const AttnParams p) {
+// TM: K/V tiles arrive by 2-D tensor-map copies (*kmap / *vmap over [.., L, D], no multicast)
+// issued by one producer thread, instead of the producer warp's 16-byte cp.async copies. The
+// body is shared by two entry points, so the default (cp.async) launch carries no tensor maps.
+template <int D, int NRT, int KS, int DS, bool F16, int QB, bool TM>
+__device__ __forceinline__ void attn_body(const CUtensorMap* kmap, const CUtensorMap* vmap,
+                                          const AttnParams& p) {
   constexpr int NC = NRT * KS * DS;
   constexpr int NP = n_producers<QB>();
   constexpr int RPG = NRT * 16;
@@ -137,7 +154,12 @@ __global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
   constexpr int NDT = DW / 8;          // n8 tiles of the warp's output
   constexpr int NKK = D / 16;          // k16 steps of Q.K^T
 
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // the 128-byte swizzled TMA destinations need 1024-byte alignment (the allocation has 1 KB of
+  // slack); the cp.async layout keeps the base as it is
+  uint8_t* smem = TM ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                  ~uintptr_t(1023))
+                     : smem_raw;
   uint8_t* ring = smem;
   constexpr int BODY = attn_core_bytes<D, NRT, KS>() - (2 * KS + 2) * RPG * 4 - 2 * NSLOT * 8 - 128;
   float* bufO = reinterpret_cast<float*>(smem);            // [KS][RPG][D] (aliases the ring)
@@ -161,7 +183,7 @@ __global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NSLOT; ++s) {
-      mbar_init(&full[s], 32 * NP);  // one arrival per producer lane
+      mbar_init(&full[s], TM ? 1 : 32 * NP);  // the TMA thread's expect-tx, or every producer lane
       mbar_init(&empty[s], NC);
     }
     fence_mbar_init();
@@ -275,6 +297,33 @@ __global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
       }
       mbar_arrive(&full[slot]);
     }
+  } else if (TM && warp == NC) {
+    // ------------------------------------------------------------------ TMA producer thread
+    // Per stage, D/64 boxes of [KTD keys x 64 dims] for K and the same for V, all on
+    // full[slot]. Keys past the tensor's L are zero-filled by the copy; keys in [kend, L) are
+    // real cache rows, masked in the scores and zeroed in the consumers' V fragments.
+    if (lane == 0) {
+      uint8_t* const ring0 = ring;
+      bool ok = true;
+      for (int st = 0; st < nst && ok; ++st) {
+        const int slot = st % NSLOT;
+        if (st >= NSLOT) ok = mbar_wait(&empty[slot], ((st / NSLOT) - 1) & 1, p.status, kErrWaitKVEmpty);
+        if (!ok) break;
+        const int kt = k0 + st * KTD;
+        uint8_t* kd = ring0 + slot * STG;
+        uint8_t* vd = kd + KTD * D * 2;
+        mbar_arrive_expect_tx(&full[slot], uint32_t(2 * KTD * D * 2));
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx) {
+          tma_load_4d(kd + bx * KTD * 128, kmap, &full[slot], bx * 64, kt, hk, b);
+          tma_load_4d(vd + bx * KTD * 128, vmap, &full[slot], bx * 64, kt, hk, b);
+        }
+      }
+      // never leave with copies in flight: wait (bounded) for the last stages issued
+      for (int st = max(0, nst - NSLOT); st < nst && ok; ++st)
+        mbar_wait(&full[st % NSLOT], (st / NSLOT) & 1, p.status, kErrWaitKV);
+    }
+    __syncwarp();
   } else if (warp == NC) {
     // ------------------------------------------------------------------ producer warp
     // 16-byte cp.async copies, lanes on consecutive chunks of a row (coalesced); keys past
@@ -358,7 +407,7 @@ __global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
       const int slot = st % NSLOT;
       if (ok) ok = mbar_wait(&full[slot], (st / NSLOT) & 1, p.status, kErrWaitKV);
       const uint32_t ks_a = ring_a + slot * STG;
-      const uint32_t vs_a = ks_a + KTD * ROWB;
+      const uint32_t vs_a = ks_a + (TM ? KTD * D * 2 : KTD * ROWB);
       const int kt = k0 + st * KTD;
 #pragma unroll
       for (int sub = 0; sub < KPW / KB; ++sub) {
@@ -374,7 +423,7 @@ __global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
             const int key = kl + jp * 16 + (mi >> 1) * 8 + (lane & 7);
             const int d = kk * 16 + (mi & 1) * 8;
             uint32_t b0, b1, b2, b3;
-            ldmatrix_x4(ks_a + key * ROWB + d * 2, b0, b1, b2, b3);
+            ldmatrix_x4(ks_a + kv_off_in_tile<TM, KTD, ROWB>(key, d), b0, b1, b2, b3);
             mma16816<F16>(s[2 * jp], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
             mma16816<F16>(s[2 * jp + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
           }
@@ -452,7 +501,19 @@ __global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
           for (int dt = 0; dt < NDT; dt += 2) {
             const int d = ds * DW + (dt + (mi >> 1)) * 8;
             uint32_t b0, b1, b2, b3;
-            ldmatrix_x4_trans(vs_a + key * ROWB + d * 2, b0, b1, b2, b3);
+            ldmatrix_x4_trans(vs_a + kv_off_in_tile<TM, KTD, ROWB>(key, d), b0, b1, b2, b3);
+            if (TM && !interior) {
+              // keys >= kend hold real cache rows (or the next split's): their P is 0, and
+              // their V values are zeroed so that nothing non-finite reaches the MMA. b0 / b2
+              // hold keys base + 2 tig, + 1; b1 / b3 hold base + 8 + 2 tig, + 1 (low half first).
+              const int kb0 = kt + kl + k2 * 16 + 2 * tig;
+              const uint32_t m0 = (kb0 < kend ? 0xFFFFu : 0u) | (kb0 + 1 < kend ? 0xFFFF0000u : 0u);
+              const uint32_t m1 = (kb0 + 8 < kend ? 0xFFFFu : 0u) | (kb0 + 9 < kend ? 0xFFFF0000u : 0u);
+              b0 &= m0;
+              b2 &= m0;
+              b1 &= m1;
+              b3 &= m1;
+            }
             mma16816<F16>(o[dt], a0, a1, a2, a3, b0, b1);
             mma16816<F16>(o[dt + 1], a0, a1, a2, a3, b2, b3);
           }
@@ -596,6 +657,19 @@ __global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
       *reinterpret_cast<uint2*>(dst) = pk;
     }
   }
+}
+
+template <int D, int NRT, int KS, int DS, bool F16, int QB = 0>
+__global__ void __launch_bounds__((NRT * KS * DS + n_producers<QB>()) * 32)
+    attn_kernel(const __grid_constant__ AttnParams p) {
+  attn_body<D, NRT, KS, DS, F16, QB, false>(nullptr, nullptr, p);
+}
+
+template <int D, int NRT, int KS, int DS, bool F16>
+__global__ void __launch_bounds__((NRT * KS * DS + 1) * 32)
+    attn_kernel_tma(const __grid_constant__ CUtensorMap kmap,
+                    const __grid_constant__ CUtensorMap vmap, const __grid_constant__ AttnParams p) {
+  attn_body<D, NRT, KS, DS, F16, 0, true>(&kmap, &vmap, p);
 }
 
 // Cross-cluster merge of the ng partials (only when ng > 1): one warp per packed row, every
@@ -794,22 +868,55 @@ size_t workspace_bytes(const AttnPlan& pl, int B, int Hk, int D) {
   return size_t(B) * Hk * pl.nrg * pl.ng * (pl.nrt * 16) * (D + 4) * sizeof(float);
 }
 
+// Tensor maps over K and V as [B][Hk][L][D] (dims innermost first), boxes of [KTD keys x 64
+// dims] with the 128-byte swizzle. Only for the dense bf16 / fp16 layout (no per-request cache
+// offsets) and when the driver accepts the strides; otherwise the cp.async producer serves.
+template <int D>
+static bool kv_maps(const AttnParams& p, CUtensorMap* km, CUtensorMap* vm) {
+  if (p.qbits || p.kv_off || env_int("DSPARK_ATTN_TMA", 0) == 0) return false;
+  const uint64_t bs_k = uint64_t(p.B > 1 ? p.k_sb : p.k_sh * p.Hk) * 2;
+  const uint64_t bs_v = uint64_t(p.B > 1 ? p.v_sb : p.v_sh * p.Hk) * 2;
+  const uint64_t dims[4] = {uint64_t(D), uint64_t(p.L), uint64_t(p.Hk), uint64_t(p.B)};
+  const uint64_t ks[3] = {uint64_t(p.k_ss) * 2, uint64_t(p.k_sh) * 2, bs_k};
+  const uint64_t vs[3] = {uint64_t(p.v_ss) * 2, uint64_t(p.v_sh) * 2, bs_v};
+  const uint32_t box[4] = {64u, uint32_t(ktile(D)), 1u, 1u};
+  return encode_tmap_nd(km, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, p.k, dims, ks, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B) &&
+         encode_tmap_nd(vm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, p.v, dims, vs, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <typename Kern>
+static cudaError_t configure_attn(Kern kern, int smem) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+}
+
 template <int D, int NRT, int KS, bool F16, int QB = 0>
 static int launch_attn(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) {
   constexpr int DS = dsplit(D);
-  auto kern = attn_kernel<D, NRT, KS, DS, F16, QB>;
   constexpr int smem = attn_smem_bytes<D, NRT, KS>();
-  DSPARK_CUDA_TRY(configure_once(reinterpret_cast<const void*>(kern), 1, [&] {
-                    cudaError_t e = cudaFuncSetAttribute(
-                        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-                    if (e != cudaSuccess) return e;
-                    return cudaFuncSetAttribute(
-                        kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-                  }),
-                  "attn: set smem / cluster attributes");
   dim3 grid(pl.ns, p.B * p.Hk * pl.nrg, pl.ng);
   dim3 block((NRT * KS * DS + n_producers<QB>()) * 32);
-  DSPARK_CUDA_TRY(launch_ex(kern, grid, block, smem, s, pl.ns, true, p), "attn: launch");
+  CUtensorMap km, vm;
+  bool tma = false;
+  if constexpr (QB == 0) tma = kv_maps<D>(p, &km, &vm);
+  if (tma) {
+    if constexpr (QB == 0) {
+      auto kern = attn_kernel_tma<D, NRT, KS, DS, F16>;
+      DSPARK_CUDA_TRY(configure_once(reinterpret_cast<const void*>(kern), 1,
+                                     [&] { return configure_attn(kern, smem); }),
+                      "attn: set smem / cluster attributes");
+      DSPARK_CUDA_TRY(launch_ex(kern, grid, block, smem, s, pl.ns, true, km, vm, p), "attn: launch");
+    }
+  } else {
+    auto kern = attn_kernel<D, NRT, KS, DS, F16, QB>;
+    DSPARK_CUDA_TRY(configure_once(reinterpret_cast<const void*>(kern), 1,
+                                   [&] { return configure_attn(kern, smem); }),
+                    "attn: set smem / cluster attributes");
+    DSPARK_CUDA_TRY(launch_ex(kern, grid, block, smem, s, pl.ns, true, p), "attn: launch");
+  }
   if (pl.ng > 1) {
     const int rows = p.B * p.Hk * pl.nrg * NRT * 16;
     DSPARK_CUDA_TRY(launch_ex(attn_merge_kernel<D, F16>,

@@ -42,6 +42,13 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, 
                     uint64_t dim1, uint64_t stride1_bytes, uint32_t box0, uint32_t box1,
                     CUtensorMapSwizzle swz);
 
+// A rank-`rank` tiled tensor map (dims innermost first, strides of dims 1.. in bytes). Returns
+// false, without recording an error, when the driver refuses it: callers fall back to another
+// data path.
+bool encode_tmap_nd(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
+                    const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                    CUtensorMapSwizzle swz);
+
 // Integer environment override (tuning knobs); `dflt` when unset.
 int env_int(const char* name, int dflt);
 

@@ -87,6 +87,35 @@ def test_baseline_config(cuda, oracle, L):
     _check(oracle, out, _ref(oracle, q, k, v, 128 ** -0.5, True))
 
 
+@pytest.mark.parametrize("B,hq,hk,q_len,L,d", [(1, 24, 4, 8, 1037, 256), (1, 32, 8, 16, 2048, 128),
+                                               (2, 8, 8, 5, 129, 64), (1, 32, 8, 16, 33000, 128),
+                                               (3, 32, 8, 16, 2049, 128)])
+def test_tensor_map_producer_matches_oracle(cuda, oracle, monkeypatch, B, hq, hk, q_len, L, d):
+    """The optional tensor-map K/V producer (DSPARK_ATTN_TMA=1: 128-byte swizzled boxes,
+    out-of-range keys zero-filled by the copy, keys past a split's end zeroed in the V
+    fragments) gives the oracle's result, on cache views with slack rows too."""
+    from mlx_dspark_b200.multirow_attn import multirow_sdpa
+
+    monkeypatch.setenv("DSPARK_ATTN_TMA", "1")
+    q, k, v = _mk(B, hq, hk, q_len, L, d, slack=37, seed=L + d)
+    out = multirow_sdpa(q, k, v, scale=d ** -0.5, causal=True)
+    _check(oracle, out, _ref(oracle, q, k, v, d ** -0.5, True))
+
+
+@pytest.mark.parametrize("nrt", [1, 2, 4])
+@pytest.mark.parametrize("L", [2048, 6000])
+def test_row_tile_caps_agree(cuda, oracle, monkeypatch, nrt, L):
+    """Every row-tile count the planner may pick (two up to 4k keys by default, four beyond;
+    DSPARK_ATTN_NRT forces a cap) gives the oracle's result: fewer row tiles per CTA only
+    re-partition the packed rows into more row groups."""
+    from mlx_dspark_b200.multirow_attn import multirow_sdpa
+
+    monkeypatch.setenv("DSPARK_ATTN_NRT", str(nrt))
+    q, k, v = _mk(1, 32, 8, 16, L, 128, slack=11, seed=nrt * 7 + L)
+    out = multirow_sdpa(q, k, v, scale=128 ** -0.5, causal=True)
+    _check(oracle, out, _ref(oracle, q, k, v, 128 ** -0.5, True))
+
+
 @pytest.mark.parametrize("B,hq,hk,q_len,L,d", [(1, 24, 4, 6, 900, 256), (1, 32, 8, 16, 2048, 128),
                                                 (2, 8, 8, 5, 129, 64)])
 def test_fp16_inputs(cuda, oracle, B, hq, hk, q_len, L, d):
@@ -131,6 +160,27 @@ def test_per_row_kv_lengths(cuda, oracle):
     lens = [900, 413, 12]
     kv_len = torch.tensor(lens, dtype=torch.int32, device=cuda)
     out = multirow_sdpa(q, k, v, scale=d ** -0.5, causal=True, kv_len=kv_len)
+    for b, Lb in enumerate(lens):
+        ref = _ref(oracle, q[b : b + 1], k[b : b + 1, :, :Lb], v[b : b + 1, :, :Lb], d ** -0.5,
+                   True)
+        _check(oracle, out[b : b + 1], ref)
+
+
+@pytest.mark.parametrize("tma", ["0", "1"])
+def test_non_finite_cache_tail_is_never_read_into_the_result(cuda, oracle, monkeypatch, tma):
+    """Cache rows past each request's kv_len may hold anything (here NaN): both K/V producers
+    keep them out of the result (zero-filled copies, or zeroed V fragments behind a mask)."""
+    from mlx_dspark_b200.multirow_attn import multirow_sdpa
+
+    monkeypatch.setenv("DSPARK_ATTN_TMA", tma)
+    B, hq, hk, qL, L, d = 2, 32, 8, 16, 1500, 128
+    q, k, v = _mk(B, hq, hk, qL, L, d, seed=21)
+    lens = [1500, 700]
+    k[1, :, 700:] = float("nan")
+    v[1, :, 700:] = float("nan")
+    kv_len = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    out = multirow_sdpa(q, k, v, scale=d ** -0.5, causal=True, kv_len=kv_len)
+    assert bool(torch.isfinite(out.float()).all())
     for b, Lb in enumerate(lens):
         ref = _ref(oracle, q[b : b + 1], k[b : b + 1, :, :Lb], v[b : b + 1, :, :Lb], d ** -0.5,
                    True)
