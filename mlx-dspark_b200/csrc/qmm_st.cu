@@ -509,8 +509,6 @@ __device__ __forceinline__ void stage_block(const QmmParams& p, uint8_t* xs, int
           pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
                               bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
       }
-      float part = (bf16_lo(vv.x) + bf16_hi(vv.x)) + (bf16_lo(vv.y) + bf16_hi(vv.y)) +
-                   (bf16_lo(vv.z) + bf16_hi(vv.z)) + (bf16_lo(vv.w) + bf16_hi(vv.w));
       uint4 o;
       if (BITS == 4) {
         o.x = __byte_perm(vv.x, vv.z, 0x5410);
@@ -524,10 +522,39 @@ __device__ __forceinline__ void stage_block(const QmmParams& p, uint8_t* xs, int
         o.w = __byte_perm(vv.z, vv.w, 0x7632);
       }
       *reinterpret_cast<uint4*>(xs + m * XP + c * 16) = o;
-      part += __shfl_xor_sync(0xffffffffu, part, 1);
-      part += __shfl_xor_sync(0xffffffffu, part, 2);
-      part += __shfl_xor_sync(0xffffffffu, part, 4);
-      if ((c & 7) == 0) sx[(c >> 3) * RP + m] = part;
+    }
+  }
+  (void)sx;
+}
+
+// The per-group sums of a staged k block (8 groups of 64 k, every row), sx[g * RP + m] = sum_k
+// x[m, k], on the tensor core: mma.m16n8k16 with an all-ones A operand and the consumers' own x
+// fragments as B (two k16 steps per 16-byte load, 8 rows per n tile) sums 16 k of 8 rows per
+// instruction, where per-element unpacking and shuffle trees cost ~20 instructions per 16-byte
+// chunk of every row in the staging warps. Epilogue warp w (of 4) takes groups 2w, 2w + 1 of the
+// block; lanes 0-3 write the rows' sums. Reads the block after every staging thread stored it.
+template <int RP>
+__device__ __forceinline__ void group_sums_mma(const uint8_t* xs, int XP, float* sx, int kb,
+                                               int we, int lane) {
+  constexpr int MT = RP / 8;
+  constexpr uint32_t ONES = 0x3F803F80u;  // bf16 1.0 in both halves
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const uint32_t xa = smem_u32(xs) + uint32_t(g8 * XP + t4 * 32);
+#pragma unroll
+  for (int gi = 0; gi < 2; ++gi) {
+    const int gl = kb * 8 + we * 2 + gi;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const uint32_t a = xa + uint32_t(mt * 8 * XP + gl * 128);
+      const uint4 q0 = lds128(a);
+      const uint4 q1 = lds128(a + 16);
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_bf16_16816(d, ONES, ONES, ONES, ONES, q0.x, q0.y);
+      mma_bf16_16816(d, ONES, ONES, ONES, ONES, q0.z, q0.w);
+      mma_bf16_16816(d, ONES, ONES, ONES, ONES, q1.x, q1.y);
+      mma_bf16_16816(d, ONES, ONES, ONES, ONES, q1.z, q1.w);
+      if (g8 == 0)
+        *reinterpret_cast<float2*>(sx + gl * RP + mt * 8 + 2 * t4) = make_float2(d[0], d[1]);
     }
   }
 }
@@ -907,6 +934,8 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
           fence_proxy_async_smem();  // the block becomes the tensor core's B operand
         } else {
           stage_block<BITS, RP, MT == 4 ? 4 : 8>(p, xs, XP, sx, rsm, nrm, kbase, kb, etid);
+          asm volatile("bar.sync 2, %0;" ::"n"(NE));  // the block's chunks are stored
+          group_sums_mma<RP>(xs, XP, sx, kb, warp - WARP_EPI, lane);
         }
         asm volatile("bar.sync 2, %0;" ::"n"(NE));  // the block's chunks and sums are stored
         if (etid == 0) mbar_arrive(&xrdy[kb]);
