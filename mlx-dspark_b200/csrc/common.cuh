@@ -361,6 +361,16 @@ __device__ __forceinline__ void fma2(float& a0, float& a1, float b0, float b1, f
       : "f"(b0), "f"(b1), "f"(c0), "f"(c1));
 }
 
+// (a0, a1) *= (b0, b1): two independent round-to-nearest fp32 products in one instruction
+__device__ __forceinline__ void mul2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb;\n\t"
+      "mov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+      "mul.rn.f32x2 ra, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
+
 // ------------------------------------------------------------------ shared-memory vector loads
 
 __device__ __forceinline__ uint32_t lds32(uint32_t addr) {

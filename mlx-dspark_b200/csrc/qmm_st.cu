@@ -491,23 +491,39 @@ __device__ __forceinline__ void stage_block(const QmmParams& p, uint8_t* xs, int
   const bf16* col = p.x + long(seg) * p.x_segstride + off;
   const uint4 w = nrm ? ldg_v4(p.norm_w + k) : z4;
   const uint32_t* pw = reinterpret_cast<const uint32_t*>(&w);
+  // row pointers and shared-memory addresses advance by increments (no per-row 64-bit products)
+  const size_t rstep = size_t(2) * size_t(p.ldx);
+  float wl[4], wh[4];  // the chunk's norm weights, unpacked once
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    wl[e] = bf16_lo(pw[e]);
+    wh[e] = bf16_hi(pw[e]);
+  }
   for (int m0 = t >> 6; m0 < p.M; m0 += 2 * U) {  // the row parity is uniform in a warp
     uint4 v[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u)
-      v[u] = m0 + 2 * u < p.M ? ldcg_v4(col + (size_t)(m0 + 2 * u) * p.ldx) : z4;
+    const bf16* rp = col + size_t(m0) * size_t(p.ldx);
+    const int nu = min(U, (p.M - m0 + 1) >> 1);  // rows of this pass (uniform in a warp)
 #pragma unroll
     for (int u = 0; u < U; ++u) {
+      v[u] = u < nu ? ldcg_v4(rp) : z4;
+      rp += rstep;
+    }
+    uint8_t* xp = xs + m0 * XP + c * 16;
+#pragma unroll
+    for (int u = 0; u < U; ++u, xp += 2 * XP) {
       const int m = m0 + 2 * u;
-      if (m >= p.M) break;  // uniform in a warp
+      if (u >= nu) break;  // uniform in a warp
       uint4 vv = v[u];
       uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
-      if (nrm) {
+      if (nrm) {  // bf16((x * r) * w), the products in packed pairs
         const float r = rsm[m];
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          pv[e] = pack_bf16x2(bf16_lo(pv[e]) * r * bf16_lo(pw[e]),
-                              bf16_hi(pv[e]) * r * bf16_hi(pw[e]));
+        for (int e = 0; e < 4; ++e) {
+          float a0 = bf16_lo(pv[e]), a1 = bf16_hi(pv[e]);
+          mul2(a0, a1, r, r);
+          mul2(a0, a1, wl[e], wh[e]);
+          pv[e] = pack_bf16x2(a0, a1);
+        }
       }
       uint4 o;
       if (BITS == 4) {
@@ -521,7 +537,7 @@ __device__ __forceinline__ void stage_block(const QmmParams& p, uint8_t* xs, int
         o.z = __byte_perm(vv.z, vv.w, 0x5410);
         o.w = __byte_perm(vv.z, vv.w, 0x7632);
       }
-      *reinterpret_cast<uint4*>(xs + m * XP + c * 16) = o;
+      *reinterpret_cast<uint4*>(xp) = o;
     }
   }
   (void)sx;
