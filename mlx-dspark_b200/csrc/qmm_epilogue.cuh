@@ -51,12 +51,43 @@ __device__ __forceinline__ void resid_prefetch(const QmmParams& p, int rank, int
   }
 }
 
+// What the EPI_QKROPE epilogue of a tile reads besides the tile: the q/k norm weights and RoPE
+// frequencies of this lane's columns (the same for every row), and the cache position / slot
+// offset of the warp's first row. Loaded ahead of the split-K reduction by the same threads, so
+// that their latency overlaps the wait for the partial tiles.
+struct QkPre {
+  float nq[4], nk[4], f[2];
+  int pos;
+  int64_t kvo;
+};
+
+template <int TN>
+__device__ __forceinline__ void qkrope_prefetch(const QmmParams& p, int rank, int cs, int nwarps,
+                                                int warp0, QkPre& q) {
+  constexpr int HPT = TN / 128;
+  const int tidx = int(threadIdx.x) - warp0 * 32;
+  const int warp = tidx >> 5, lane = tidx & 31;
+  const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    q.nq[i] = bf2f(p.qnorm[lane + 32 * i]);
+    q.nk[i] = bf2f(p.knorm[lane + 32 * i]);
+  }
+  q.f[0] = p.inv_freq[lane];
+  q.f[1] = p.inv_freq[lane + 32];
+  const int mi = warp / HPT;  // the warp's first item is u = warp
+  const int m = rank + mi * cs;
+  q.pos = mi < nmine ? p.row_pos[m] : 0;
+  q.kvo = (mi < nmine && p.row_kv != nullptr) ? p.row_kv[m] : 0;
+}
+
 // Run by `nwarps` warps starting at warp `warp0` of the CTA. `pre`: the residual words from
 // resid_prefetch for this tile (EPI_RESID, 128-column tiles), or null to load them here.
 template <int EPI, int TN, int PSTR, bool PEER = false>
 __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, int rank, int cs,
                                          int ntile, int n0, int nwarps, int warp0 = 0,
-                                         const uint32_t* pre = nullptr) {
+                                         const uint32_t* pre = nullptr, bool has_qk = false,
+                                         QkPre qk = {}) {
   const int nthr = nwarps * 32;
   const int tidx = int(threadIdx.x) - warp0 * 32;
   const int warp = tidx >> 5, lane = tidx & 31;
@@ -143,8 +174,9 @@ __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, i
       float v[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) v[i] = round_bf16(red[m * PSTR + t * 128 + lane + 32 * i]);
-      const int pos = p.row_pos[m];
-      const int64_t kvo = p.row_kv != nullptr ? p.row_kv[m] : 0;
+      const bool first = has_qk && u == warp;
+      const int pos = first ? qk.pos : p.row_pos[m];
+      const int64_t kvo = first ? qk.kvo : (p.row_kv != nullptr ? p.row_kv[m] : 0);
       if (hh >= p.hq && (pos < 0 || pos >= p.kv_cap)) {  // never write past a cache slot
         if (lane == 0) report_error(p.status, 0x301);
         continue;
@@ -158,12 +190,14 @@ __device__ __forceinline__ void epilogue(const QmmParams& p, const float* red, i
         const float r = rsqrtf(ss / 128.0f + p.eps);
         float y[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) y[i] = round_bf16(v[i] * r * bf2f(nw[lane + 32 * i]));
+        for (int i = 0; i < 4; ++i)
+          y[i] = round_bf16(v[i] * r *
+                            (has_qk ? (isq ? qk.nq[i] : qk.nk[i]) : bf2f(nw[lane + 32 * i])));
         // rotate-half RoPE: pairs (d, d+64) for d = lane, lane+32
         float o[4];
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
-          const float f = p.inv_freq[lane + 32 * i];
+          const float f = has_qk ? qk.f[i] : p.inv_freq[lane + 32 * i];
           float sn, c;
           sincosf(float(pos) * f, &sn, &c);
           o[i] = y[i] * c - y[i + 2] * sn;

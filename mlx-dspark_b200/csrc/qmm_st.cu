@@ -972,6 +972,8 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
       // the residual of this tile comes from an earlier kernel: load it before the wait
       uint32_t pre[2 * kResidRows];
       if constexpr (EPI == EPI_RESID) resid_prefetch<TN>(p, rank, cs, t * TN, NWE, WARP_EPI, pre);
+      QkPre qk = {};
+      if constexpr (EPI == EPI_QKROPE) qkrope_prefetch<TN>(p, rank, cs, NWE, WARP_EPI, qk);
       if constexpr (TC) {
         // read the tile's D (this warp's 32 lanes: tile rows 32 * (warp % 4) + lane, one column
         // per x row), free it for tile j + 2, and push its rows to their owners like the
@@ -1034,7 +1036,7 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
           mbar_arrive(&freeb[pbuf]);
       }
       epilogue<EPI, TN, PSTR, PEER>(p, red, rank, cs, t, t * TN, NWE, WARP_EPI,
-                              EPI == EPI_RESID ? pre : nullptr);
+                                    EPI == EPI_RESID ? pre : nullptr, EPI == EPI_QKROPE, qk);
       asm volatile("bar.sync 2, %0;" ::"n"(NE));  // red reads done
       if (PEER && p.peer_world > 0 && nmine > 0) {
         // this tile's rows, written locally by the epilogue, go to every peer's arena as
