@@ -133,7 +133,7 @@ __device__ __forceinline__ int64_t q_base(const AttnParams& p, int b, const int6
 // four producer warps load the codes with 16-byte loads, dequantize (scale * q + bias, rounded to
 // bf16) into the same padded ring rows, and arrive on the stage's barrier.
 template <int QB>
-__host__ __device__ constexpr int n_producers() { return QB ? 4 : 1; }
+__host__ __device__ constexpr int n_producers() { return QB ? 4 : 2; }
 
 // TM: K/V tiles arrive by 2-D tensor-map copies (*kmap / *vmap over [.., L, D], no multicast)
 // issued by one producer thread, instead of the producer warp's 16-byte cp.async copies. The
@@ -324,14 +324,18 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* kmap, const CUtenso
         mbar_wait(&full[st % NSLOT], (st / NSLOT) & 1, p.status, kErrWaitKV);
     }
     __syncwarp();
-  } else if (warp == NC) {
-    // ------------------------------------------------------------------ producer warp
+  } else if (warp >= NC) {
+    // ------------------------------------------------------------------ producer warps
     // 16-byte cp.async copies, lanes on consecutive chunks of a row (coalesced); keys past
     // the split's end are zero-filled without a read, so masked keys always hold finite
-    // values. Each lane's copies of a stage complete on full[slot] (32 arrivals).
+    // values. The NP warps take alternate row groups of a stage (one warp issuing a whole
+    // stage's 2048 copies set the first tile's latency); every producer lane's copies of a
+    // stage complete on full[slot] (32 NP arrivals).
     constexpr int CPR = D * 2 / 16;          // 16-byte chunks per row (32, 16 or 8)
     constexpr int RPI = 32 / CPR;            // rows per warp instruction (1, 2 or 4)
-    const int rsub = lane / CPR, ch = lane % CPR;
+    static_assert((KTD / RPI) % NP == 0, "whole row groups per producer warp");
+    const int pw = warp - NC;                // this warp's row groups: pw, pw + NP, ...
+    const int rsub = lane / CPR + pw * RPI, ch = lane % CPR;
     const uint32_t ring_a = smem_u32(ring);
     bool ok = true;
     for (int st = 0; st < nst && ok; ++st) {
@@ -342,17 +346,17 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* kmap, const CUtenso
       uint32_t dk = ring_a + slot * STG + rsub * ROWB + ch * 16;
       const bf16* kp = kb_ptr + int64_t(kt + rsub) * p.k_ss + ch * 8;
       const bf16* vp = vb_ptr + int64_t(kt + rsub) * p.v_ss + ch * 8;
-      const int64_t kstep = int64_t(RPI) * p.k_ss, vstep = int64_t(RPI) * p.v_ss;
+      const int64_t kstep = int64_t(NP * RPI) * p.k_ss, vstep = int64_t(NP * RPI) * p.v_ss;
       int key = kt + rsub;
 #pragma unroll 8
-      for (int i = 0; i < KTD / RPI; ++i) {
+      for (int i = 0; i < KTD / RPI / NP; ++i) {
         const bool valid = key < kend;
         cp_async_16_zfill(dk, valid ? kp : kb_ptr, valid);
         cp_async_16_zfill(dk + KTD * ROWB, valid ? vp : vb_ptr, valid);
-        dk += RPI * ROWB;
+        dk += NP * RPI * ROWB;
         kp += kstep;
         vp += vstep;
-        key += RPI;
+        key += NP * RPI;
       }
       cp_async_mbar_arrive(&full[slot]);
     }
@@ -748,7 +752,7 @@ static int max_clusters_t(int cs) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cs, 1, 1);
-  cfg.blockDim = dim3((NRT * KS * DS + 1) * 32);
+  cfg.blockDim = dim3((NRT * KS * DS + n_producers<0>()) * 32);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
@@ -899,6 +903,7 @@ static int launch_attn(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) 
   constexpr int smem = attn_smem_bytes<D, NRT, KS>();
   dim3 grid(pl.ns, p.B * p.Hk * pl.nrg, pl.ng);
   dim3 block((NRT * KS * DS + n_producers<QB>()) * 32);
+  const dim3 block_tma((NRT * KS * DS + 1) * 32);  // one TMA producer warp
   CUtensorMap km, vm;
   bool tma = false;
   if constexpr (QB == 0) tma = kv_maps<D>(p, &km, &vm);
@@ -908,7 +913,7 @@ static int launch_attn(const AttnParams& p, const AttnPlan& pl, cudaStream_t s) 
       DSPARK_CUDA_TRY(configure_once(reinterpret_cast<const void*>(kern), 1,
                                      [&] { return configure_attn(kern, smem); }),
                       "attn: set smem / cluster attributes");
-      DSPARK_CUDA_TRY(launch_ex(kern, grid, block, smem, s, pl.ns, true, km, vm, p), "attn: launch");
+      DSPARK_CUDA_TRY(launch_ex(kern, grid, block_tma, smem, s, pl.ns, true, km, vm, p), "attn: launch");
     }
   } else {
     auto kern = attn_kernel<D, NRT, KS, DS, F16, QB>;
