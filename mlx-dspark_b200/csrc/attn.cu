@@ -157,9 +157,7 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* kmap, const CUtenso
   extern __shared__ __align__(128) uint8_t smem_raw[];
   // the 128-byte swizzled TMA destinations need 1024-byte alignment (the allocation has 1 KB of
   // slack); the cp.async layout keeps the base as it is
-  uint8_t* smem = TM ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                                  ~uintptr_t(1023))
-                     : smem_raw;
+  uint8_t* smem = TM ? smem_align_up<1024>(smem_raw) : smem_raw;
   uint8_t* ring = smem;
   constexpr int BODY = attn_core_bytes<D, NRT, KS>() - (2 * KS + 2) * RPG * 4 - 2 * NSLOT * 8 - 128;
   float* bufO = reinterpret_cast<float*>(smem);            // [KS][RPG][D] (aliases the ring)

@@ -138,8 +138,7 @@ __global__ void __launch_bounds__((NW + 1) * 32)
   constexpr int PSTR = TN + 4;  // fp32 row stride of the partial / reduced tiles
 
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = smem_align_up<1024>(smem_raw);
   const int S = p.nslots;
   const SmemLayout Ls = smem_layout<BITS, NW, RT>(p.kslice, S);
   uint8_t* ring = smem + Ls.ring;

@@ -436,11 +436,10 @@ __device__ __forceinline__ int ssq_stage_width(const QmmParams& p, int rp, int s
 // few KB) is read by every CTA of the launch at the same moment; per-row strided loads made
 // hundreds of line requests per CTA, which queued at the lines' L2 slices (measured: ~2.5 us for
 // the one round trip). Here the epilogue threads first copy it into shared memory with 16-byte
-// loads (a few line requests per CTA), then each warp sums its rows from there in the same order
-// as norm_stats (lane-strided over entries, then the fixed shuffle tree): the same rs bits.
+// loads (a few line requests per CTA), then sums each row from there in the same order as
+// norm_stats (lane-strided over entries, then the fixed shuffle tree): the same rs bits.
 __device__ __forceinline__ void norm_stats_staged(const QmmParams& p, float* rsm, int rp, int w,
-                                                  float* scratch, int etid, int m0, int mstep,
-                                                  int lane) {
+                                                  float* scratch, int etid) {
   const int w4 = w / 4;
   for (int i = etid; i < p.ssq_n * w4; i += NE) {
     const int e = i / w4, c = i - e * w4;
@@ -448,24 +447,30 @@ __device__ __forceinline__ void norm_stats_staged(const QmmParams& p, float* rsm
         __ldcg(reinterpret_cast<const float4*>(&p.ssq_in[long(e) * p.ssq_stride + c * 4]));
   }
   asm volatile("bar.sync 2, %0;" ::"n"(NE));  // the block is staged
-  constexpr int MAXR = 8;
-  float ss[MAXR];
+  // One thread per row, every row at once (four rows per warp through dependent shuffle chains
+  // were measurably slower on this launch-head path). Each of the 32 partials a[l] sums entries
+  // l, l + 32, ... in order (a lane's share in norm_stats), and the partials are paired as the
+  // xor-shuffle tree pairs lanes (l with l + 16, then l + 8, ...): norm_stats' bits.
+  if (etid < rp) {
+    const int m = etid;
+    float r = 0.f;
+    if (m < p.M) {
+      float a[32];
 #pragma unroll
-  for (int i = 0; i < MAXR; ++i) ss[i] = 0.f;
-  for (int e = lane; e < p.ssq_n; e += 32) {
+      for (int l = 0; l < 32; ++l) a[l] = 0.f;
+      for (int e0 = 0; e0 < p.ssq_n; e0 += 32) {
 #pragma unroll
-    for (int i = 0; i < MAXR; ++i) {
-      const int m = m0 + i * mstep;
-      if (m < rp && m < p.M) ss[i] += scratch[e * w + m];
+        for (int l = 0; l < 32; ++l)
+          if (e0 + l < p.ssq_n) a[l] += scratch[(e0 + l) * w + m];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int l = 0; l < o; ++l) a[l] += a[l + o];
+      }
+      r = rsqrtf(a[0] / float(p.K) + p.eps);
     }
-  }
-#pragma unroll
-  for (int i = 0; i < MAXR; ++i) {
-    const int m = m0 + i * mstep;
-    float v = ss[i];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0 && m < rp) rsm[m] = m < p.M ? rsqrtf(v / float(p.K) + p.eps) : 0.f;
+    rsm[m] = r;
   }
 }
 
@@ -586,8 +591,7 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
   constexpr float MAGIC = Tr<BITS>::MAGIC;
 
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = smem_align_up<1024>(smem_raw);
   const int S = p.nslots;
   const int SS = scale_slots(BITS, S);
   const Layout Lo = layout(BITS, MT, p.kslice, S, p.cs, TC);
@@ -939,7 +943,7 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
         // `red` (the reduced-tile scratch) is free until the first tile's epilogue
         const int sw = ssq_stage_width(p, RP, RP * PSTR);
         if (sw)
-          norm_stats_staged(p, rsm, RP, sw, red, etid, warp - WARP_EPI, NWE, lane);
+          norm_stats_staged(p, rsm, RP, sw, red, etid);
         else
           norm_stats(p, rsm, RP, warp - WARP_EPI, NWE, lane);
         asm volatile("bar.sync 2, %0;" ::"n"(NE));  // rs of every row

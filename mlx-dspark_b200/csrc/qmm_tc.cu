@@ -167,8 +167,7 @@ __global__ void __launch_bounds__(NTHR, 1)
   static_assert(NWG * PER <= kTmemCols && ND >= 2, "TMEM budget");
 
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = smem_align_up<1024>(smem_raw);
   const int S = p.nslots;
   const Layout Lo = layout(BITS, RT, p.kslice, S);
   uint8_t* ring = smem + Lo.ring;

@@ -125,8 +125,7 @@ __global__ void __launch_bounds__(NTHR, 1)
   constexpr int WSTG = wstg<BITS>();
   constexpr uint32_t M128 = 0x43004300u;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = smem_align_up<1024>(smem_raw);
   uint8_t* xr = smem + Lo.xr;
   uint8_t* wr = smem + Lo.wr;
   uint8_t* sr = smem + Lo.sr;
