@@ -700,6 +700,7 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
     }
     __syncwarp();
     if (cs > 1) cluster_wait();
+    if (!TC && cs > 1) cluster_arrive();  // the exit barrier: no remote access from here on
   } else if (TC && warp < NWC) {
     // ------------------------------------------------------------- tcgen05: dequantization
     dequant_tc<BITS>(p, ring, sring, full, empty, afull, aempty, *tmem_slot, ntl, nsb, S, SS, ok);
@@ -925,6 +926,8 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
       if (lane == 0) mbar_arrive(&ready[pbuf]);  // this warp's local rows are in place
     }
     if (ntl == 0 && cs > 1) cluster_wait();
+    // the exit barrier: the last partial is pushed, no remote access from here on
+    if (!TC && cs > 1) cluster_arrive();
   } else {
     // ------------------------------------------------------------- epilogue warps
     pdl_wait();  // x, the statistics and the epilogues' buffers come from earlier kernels
@@ -962,6 +965,9 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
       }
     }
     if (cs > 1) cluster_wait();  // peers' barriers exist before the first remote arrive
+    // the exit barrier's arrive comes after this warp's last remote arrive (the release of tile
+    // ntl - 3 below): at once when no tile's buffer is released to a peer
+    if (!TC && cs > 1 && ntl < 3) cluster_arrive();
     const int ro = owned_rows(RP, cs);
     const int nmine = (p.M > rank) ? (p.M - rank + cs - 1) / cs : 0;
     // bytes each peer pushes into this CTA per tile: its 2 k halves (one D with tcgen05) of the
@@ -1032,13 +1038,15 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
         *reinterpret_cast<float4*>(&red[m * PSTR + n4 * 4]) = s;
       }
       asm volatile("bar.sync 2, %0;" ::"n"(NE));
-      // every CTA may push its next partial into this buffer again (lane c -> CTA c)
-      if (etid < cs) {
+      // every CTA may push its next partial into this buffer again (lane c -> CTA c); the last
+      // two tiles' buffers are pushed into no more, and nobody waits for their release
+      if (etid < cs && j + 2 < ntl) {
         if (cs > 1)
           mbar_arrive_cluster(&freeb[pbuf], etid);
         else
           mbar_arrive(&freeb[pbuf]);
       }
+      if (!TC && cs > 1 && j + 3 == ntl) cluster_arrive();  // the exit barrier (see above)
       epilogue<EPI, TN, PSTR, PEER>(p, red, rank, cs, t, t * TN, NWE, WARP_EPI,
                                     EPI == EPI_RESID ? pre : nullptr, EPI == EPI_QKROPE, qk);
       asm volatile("bar.sync 2, %0;" ::"n"(NE));  // red reads done
@@ -1071,8 +1079,17 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
     }
   }
 
-  // no CTA leaves while a peer may still read its partial tiles or arrive on its barriers
-  if (cs > 1) cluster_sync_all(); else __syncthreads();
+  // No CTA leaves while a peer may still write its partial tiles or arrive on its barriers. The
+  // mma.sync engine's warps made this barrier's arrive after their last access to a peer's shared
+  // memory (the producer after its set-up wait, the consumers after their last push, the
+  // epilogue warps after their last buffer release), so the wait here does not add a cluster
+  // round trip after the last epilogue. Every partial pushed into this CTA has landed before
+  // its last reduction (the ready barrier counts the bytes).
+  if (TC) {
+    if (cs > 1) cluster_sync_all(); else __syncthreads();
+  } else {
+    if (cs > 1) cluster_wait(); else __syncthreads();
+  }
   // a gather wait: the launch's last CTA advances this rank's cumulative target (every CTA read
   // it before counting itself here)
   if (PEER && p.wait_flag != nullptr && tid == 0) {
