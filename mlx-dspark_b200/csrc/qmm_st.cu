@@ -569,13 +569,15 @@ __device__ __forceinline__ void group_sums_mma(const uint8_t* xs, int XP, float*
       const uint32_t a = xa + uint32_t(mt * 8 * XP + gl * 128);
       const uint4 q0 = lds128(a);
       const uint4 q1 = lds128(a + 16);
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      // two independent accumulation chains (k 0-31 and 32-63 of the group), then their sum
+      float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};
       mma_bf16_16816(d, ONES, ONES, ONES, ONES, q0.x, q0.y);
+      mma_bf16_16816(e, ONES, ONES, ONES, ONES, q1.x, q1.y);
       mma_bf16_16816(d, ONES, ONES, ONES, ONES, q0.z, q0.w);
-      mma_bf16_16816(d, ONES, ONES, ONES, ONES, q1.x, q1.y);
-      mma_bf16_16816(d, ONES, ONES, ONES, ONES, q1.z, q1.w);
+      mma_bf16_16816(e, ONES, ONES, ONES, ONES, q1.z, q1.w);
       if (g8 == 0)
-        *reinterpret_cast<float2*>(sx + gl * RP + mt * 8 + 2 * t4) = make_float2(d[0], d[1]);
+        *reinterpret_cast<float2*>(sx + gl * RP + mt * 8 + 2 * t4) =
+            make_float2(d[0] + e[0], d[1] + e[1]);
     }
   }
 }
@@ -644,7 +646,9 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
       mbar_init(&ready[i], 1 + (TC ? NWE : NWC));
       mbar_init(&freeb[i], cs);
     }
-    for (int i = 0; i < kXBlocks; ++i) mbar_init(&xrdy[i], 1);
+    // x block staged: one arrive per epilogue warp after its group sums (mma.sync engine), or
+    // one after the block's barrier (tcgen05 engine)
+    for (int i = 0; i < kXBlocks; ++i) mbar_init(&xrdy[i], TC ? 1 : NWE);
     for (int i = 0; i < kTcBars; ++i) mbar_init(&tcbar[i], 1);
     if (TC) {
       for (int i = 0; i < 4; ++i) mbar_init(&afull[i], 4);
@@ -959,8 +963,13 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
           stage_block<BITS, RP, MT == 4 ? 4 : 8>(p, xs, XP, sx, rsm, nrm, kbase, kb, etid);
           asm volatile("bar.sync 2, %0;" ::"n"(NE));  // the block's chunks are stored
           group_sums_mma<RP>(xs, XP, sx, kb, warp - WARP_EPI, lane);
+          // this warp's sums are stored (and every chunk, by the barrier above): each warp
+          // releases the block on its own, no second barrier
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&xrdy[kb]);
+          continue;
         }
-        asm volatile("bar.sync 2, %0;" ::"n"(NE));  // the block's chunks and sums are stored
+        asm volatile("bar.sync 2, %0;" ::"n"(NE));  // the block's chunks are stored
         if (etid == 0) mbar_arrive(&xrdy[kb]);
       }
     }
