@@ -475,17 +475,19 @@ __device__ __forceinline__ void norm_stats_staged(const QmmParams& p, float* rsm
 }
 
 // Stage k block kb (512 k: chunks c = 64kb .. 64kb + 63 of the K slice) of every row of x into
-// shared memory (rows of XP bytes), by 128 threads: thread t takes chunk column 64kb + t % 64 and
-// rows t / 64, t / 64 + 2, ..., U loads in flight at once (16-byte global loads). Each chunk is
-// normed (x * rs * w rounded to bf16), permuted inside each 8-block (4-bit: 0,4,1,5,2,6,3,7) or
-// 4-block (8-bit: 0,2,1,3) as the magic extraction orders the weights, and summed per group of
-// 64 into sx: a group's 8 chunks sit on 8 consecutive lanes and reduce by shuffles in a fixed
-// order. The block's one division (the segment of k) comes before its loads are issued.
+// shared memory (rows of XP bytes). Epilogue warp `we` (of 4) stages the chunks of groups 2we and
+// 2we + 1 (16 chunk columns) of every row, which are the groups whose sums it forms next, so a
+// warp-level sync is the only one between the two: lane l takes chunk column 64kb + 16we + l % 16
+// and rows l / 16, l / 16 + 2, ..., U loads in flight at once (16-byte global loads). Each chunk
+// is normed (x * rs * w rounded to bf16) and permuted inside each 8-block (4-bit:
+// 0,4,1,5,2,6,3,7) or 4-block (8-bit: 0,2,1,3) as the magic extraction orders the weights. The
+// block's one division (the segment of k) comes before its loads are issued.
 template <int BITS, int RP, int U>
-__device__ __forceinline__ void stage_block(const QmmParams& p, uint8_t* xs, int XP, float* sx,
-                                            const float* rsm, bool nrm, int kbase, int kb, int t) {
+__device__ __forceinline__ void stage_block(const QmmParams& p, uint8_t* xs, int XP,
+                                            const float* rsm, bool nrm, int kbase, int kb, int we,
+                                            int lane) {
   const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
-  const int c = kb * 64 + (t & 63);
+  const int c = kb * 64 + 16 * we + (lane & 15);
   const int k = kbase + c * 8;
   const int xseg = int(p.x_seg);
   int seg = 0, off = k;
@@ -504,10 +506,10 @@ __device__ __forceinline__ void stage_block(const QmmParams& p, uint8_t* xs, int
     wl[e] = bf16_lo(pw[e]);
     wh[e] = bf16_hi(pw[e]);
   }
-  for (int m0 = t >> 6; m0 < p.M; m0 += 2 * U) {  // the row parity is uniform in a warp
+  for (int m0 = lane >> 4; m0 < p.M; m0 += 2 * U) {  // the row parity of a half-warp
     uint4 v[U];
     const bf16* rp = col + size_t(m0) * size_t(p.ldx);
-    const int nu = min(U, (p.M - m0 + 1) >> 1);  // rows of this pass (uniform in a warp)
+    const int nu = min(U, (p.M - m0 + 1) >> 1);  // rows of this pass (per half-warp)
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       v[u] = u < nu ? ldcg_v4(rp) : z4;
@@ -517,7 +519,7 @@ __device__ __forceinline__ void stage_block(const QmmParams& p, uint8_t* xs, int
 #pragma unroll
     for (int u = 0; u < U; ++u, xp += 2 * XP) {
       const int m = m0 + 2 * u;
-      if (u >= nu) break;  // uniform in a warp
+      if (u >= nu) break;  // uniform in a half-warp
       uint4 vv = v[u];
       uint32_t* pv = reinterpret_cast<uint32_t*>(&vv);
       if (nrm) {  // bf16((x * r) * w), the products in packed pairs
@@ -545,7 +547,6 @@ __device__ __forceinline__ void stage_block(const QmmParams& p, uint8_t* xs, int
       *reinterpret_cast<uint4*>(xp) = o;
     }
   }
-  (void)sx;
 }
 
 // The per-group sums of a staged k block (8 groups of 64 k, every row), sx[g * RP + m] = sum_k
@@ -553,7 +554,8 @@ __device__ __forceinline__ void stage_block(const QmmParams& p, uint8_t* xs, int
 // fragments as B (two k16 steps per 16-byte load, 8 rows per n tile) sums 16 k of 8 rows per
 // instruction, where per-element unpacking and shuffle trees cost ~20 instructions per 16-byte
 // chunk of every row in the staging warps. Epilogue warp w (of 4) takes groups 2w, 2w + 1 of the
-// block; lanes 0-3 write the rows' sums. Reads the block after every staging thread stored it.
+// block; lanes 0-3 write the rows' sums. Reads the chunks this warp staged (stage_block), after a
+// warp-level sync.
 template <int RP>
 __device__ __forceinline__ void group_sums_mma(const uint8_t* xs, int XP, float* sx, int kb,
                                                int we, int lane) {
@@ -960,11 +962,12 @@ __global__ void __launch_bounds__(TC ? NTHR_TC : NTHR, 1)
           stage_block_tc<BITS, (MT <= 2 ? 16 : 32), 4>(p, xs, rsm, nrm, kbase, kb, etid);
           fence_proxy_async_smem();  // the block becomes the tensor core's B operand
         } else {
-          stage_block<BITS, RP, MT == 4 ? 4 : 8>(p, xs, XP, sx, rsm, nrm, kbase, kb, etid);
-          asm volatile("bar.sync 2, %0;" ::"n"(NE));  // the block's chunks are stored
+          stage_block<BITS, RP, MT == 4 ? 4 : 8>(p, xs, XP, rsm, nrm, kbase, kb, warp - WARP_EPI,
+                                                lane);
+          __syncwarp();  // this warp's chunks (its two groups, every row) are stored
           group_sums_mma<RP>(xs, XP, sx, kb, warp - WARP_EPI, lane);
-          // this warp's sums are stored (and every chunk, by the barrier above): each warp
-          // releases the block on its own, no second barrier
+          // the warp's chunks and sums are stored: each warp releases its part of the block
+          // (the block's barrier counts one arrive per epilogue warp)
           __syncwarp();
           if (lane == 0) mbar_arrive(&xrdy[kb]);
           continue;
