@@ -427,8 +427,8 @@ def _qmm_bytes(n, k, m, bits):
 #   python bench.py --steps 3 --warmup 3 --quick --no-cpu-baseline --no-extras
 #   ncu --clock-control none --kernel-name-base demangled -k "regex:qmm_st_kernel<\\(int\\)4, \\(int\\)2, \\(int\\)2"
 #       -s 8 -c 1 --section SpeedOfLight --section MemoryWorkloadAnalysis <the same command>
-# dram__bytes.sum.per_second 1.820200 TB/s x gpu__time_duration.sum 31.328 us (cold, under ncu)
-GATEUP_SWIGLU_TRAFFIC = 57_023_226
+# dram__bytes.sum.per_second 1.886593 TB/s x gpu__time_duration.sum 30.208 us (cold, under ncu)
+GATEUP_SWIGLU_TRAFFIC = 56_990_201
 
 
 def roofline(t, dev, pk) -> dict:
